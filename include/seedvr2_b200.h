@@ -1,0 +1,175 @@
+/*
+ * seedvr2_b200.h -- C ABI of the B200 (sm_100a) NaDiT DiT forward and its
+ * Adaptive Window Attention (AWA).
+ *
+ * This is the drop-in boundary for the reference's DiT hot path
+ * (AiChiTuDouPian/SeedVR2-2b-ncnn).  Every entry point names the reference
+ * interface it replaces (file:line in that project).  Conventions:
+ *   - every call returns an int status, 0 = S2B_OK; on failure the context's
+ *     message is available from s2b_last_error(ctx) (the reference prints to
+ *     stderr and returns false / -1);
+ *   - a context owns one CUDA device, its weights (resident in HBM) and all
+ *     scratch; it is not thread-safe: one context per host thread and device;
+ *   - host-buffer entry points copy in, run, copy out and return when the
+ *     result is on the host (the reference's submit_and_wait semantics);
+ *     "_dev" entry points take device pointers and a cudaStream_t (passed as
+ *     void*) and only enqueue (the ncnn custom-layer semantics: record on the
+ *     caller's command stream);
+ *   - inputs are never retained; outputs are caller-owned.
+ * Layouts are the reference's: fp32, row-major, token index ((t*H)+h)*W+w,
+ * qkv rows [q(20x128) | k | v] (src/awa_vk.h:36), patches (ph,pw,c).
+ */
+#ifndef SEEDVR2_B200_H
+#define SEEDVR2_B200_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define S2B_OK 0
+#define S2B_ERR_ARG 1
+#define S2B_ERR_CUDA 2
+#define S2B_ERR_IO 3
+#define S2B_ERR_STATE 4
+#define S2B_ERR_UNSUPPORTED 5
+#define S2B_ERR_NCCL 6
+#define S2B_ERR_TIMEOUT 7
+#define S2B_ERR_NOMEM 8
+
+/* precision: GEMM/attention operand type (reference DitVk::init `precision`,
+ * src/dit_vk.h:37-39: 0 fp32, 1 fp16, 2 bf16).  fp16 is not offered on B200
+ * (returns S2B_ERR_UNSUPPORTED); the residual stream is fp32 in both modes. */
+#define S2B_PREC_FP32 0
+#define S2B_PREC_FP16 1
+#define S2B_PREC_BF16 2
+
+typedef struct s2b_ctx s2b_ctx;
+
+/* C mirror of the reference `Win` (src/dit_vk.h:17-22): grid (t,h,w), window
+ * slices [st,en) x [sh,eh) x [sw,ew) and the RoPE angle tables
+ * vid_freq[sum(f_i) x 126] (window-packed order) and
+ * txt_freq[nwin x txt_len x 126]. */
+typedef struct s2b_win {
+    int t, h, w, nwin, txt_len;
+    const int *st, *en, *sh, *eh, *sw, *ew;
+    const float* vid_freq;
+    long n_vid_freq;
+    const float* txt_freq;
+    long n_txt_freq;
+} s2b_win;
+
+/* ---- context --------------------------------------------------------- */
+/* Replaces DitVk::DitVk + the device half of DitVk::init (src/dit_vk.cpp:140-155). */
+int s2b_ctx_create(int device, int precision, s2b_ctx** out);
+/* Replaces DitVk::~DitVk (src/dit_vk.cpp:97-107). */
+int s2b_ctx_destroy(s2b_ctx* ctx);
+const char* s2b_last_error(const s2b_ctx* ctx);
+int s2b_ctx_precision(const s2b_ctx* ctx);
+/* Device bytes held by the context (weights + activations + scratch). */
+int s2b_ctx_device_bytes(const s2b_ctx* ctx, uint64_t* bytes);
+/* Number of kernels the last forward enqueued (for launch accounting). */
+int s2b_ctx_last_launches(const s2b_ctx* ctx, int* launches);
+
+/* ---- weights --------------------------------------------------------- */
+/* Replaces the weight half of DitVk::init (src/dit_vk.cpp:156-177) and the
+ * per-Linear ncnn Net loads of DitVk::lin/get_net (src/dit_vk.cpp:204-293):
+ * reads the m5 directory layout (<base>.param/.bin fp16 Linear blobs, raw
+ * fp32 vectors) for layers [layer_lo, layer_hi) plus the top-level modules,
+ * and keeps everything resident in HBM. */
+int s2b_load_weights_dir(s2b_ctx* ctx, const char* m5_dir, int layer_lo, int layer_hi);
+/* Same tensors as s2b_synth_write_m5(seed) would write, generated in host
+ * memory and uploaded without touching the disk. */
+int s2b_load_weights_synth(s2b_ctx* ctx, uint64_t seed, int layer_lo, int layer_hi);
+
+/* ---- geometry -------------------------------------------------------- */
+/* Replaces awa::make_win (src/awa_window.cpp:161-178).  Two-step: query the
+ * sizes, then fill caller buffers (st..ew: nwin ints each). */
+int s2b_make_win_size(int t, int h, int w, const int num_windows[3], int txt_len, int shifted,
+                      int* nwin, long* n_vid_freq, long* n_txt_freq);
+int s2b_make_win_fill(int t, int h, int w, const int num_windows[3], int txt_len, int shifted,
+                      int* st, int* en, int* sh, int* eh, int* sw, int* ew, float* vid_freq, float* txt_freq);
+/* Replaces DitVk::set_windows (src/dit_vk.h:58) and the AWA layers'
+ * set_window_geometry injection (src/dit_graph.cpp:221-262): even layers use
+ * `ns`, odd layers `sh` (src/dit_vk.cpp:518). */
+int s2b_set_windows(s2b_ctx* ctx, const s2b_win* ns, const s2b_win* sh);
+
+/* ---- DiT forward ----------------------------------------------------- */
+/* Replaces DitVk::forward_latent (src/dit_vk.cpp:486-699).  Runs layers
+ * [l0, l1).  do_init: vid_in is the (Lv,132) patch input and txt_in (TXT,5120);
+ * else they are the (Lv,2560)/(TXT,2560) residual latents of a previous chunk.
+ * do_final: writes sr_out (Lv,64) (vid_lat/txt_lat untouched); else writes
+ * vid_lat (Lv,2560) and txt_lat (TXT,2560). */
+int s2b_forward_latent(s2b_ctx* ctx, const float* vid_in, int Lv, const float* txt_in, int TXT,
+                       float timestep, int l0, int l1, int do_init, int do_final,
+                       float* vid_lat, float* txt_lat, float* sr_out);
+/* Replaces DitVk::forward (src/dit_vk.cpp:710-715) and DitVk::forward_graph
+ * (src/dit_graph.cpp:264-549): all 32 layers, replayed from one captured CUDA
+ * graph per (Lv, TXT) with weights resident. */
+int s2b_forward(s2b_ctx* ctx, const float* vid_patch, int Lv, const float* txt, int TXT,
+                float timestep, float* sr_out);
+/* Device-pointer form of s2b_forward; enqueues on `stream` (cudaStream_t).
+ * d_vid_patch (Lv,132) fp32, d_txt (TXT,5120) fp32, d_sr_out (Lv,64) fp32. */
+int s2b_forward_dev(s2b_ctx* ctx, const float* d_vid_patch, int Lv, const float* d_txt, int TXT,
+                    float timestep, float* d_sr_out, void* stream);
+/* Replaces DitVk::forward_grid (src/dit_vk.cpp:752-763). */
+int s2b_forward_grid(s2b_ctx* ctx, const float* vid_grid, int T, int H, int W, const float* txt, int TXT,
+                     float timestep, float* sr_latent);
+/* Replace DitVk::patchify_grid / unpatchify_latent (src/dit_vk.cpp:717-750). */
+int s2b_patchify_grid(const float* vid_grid, int T, int H, int W, float* vid_patch);
+int s2b_unpatchify_latent(const float* sr, int T, int H, int W, float* sr_latent);
+
+/* ---- AWA operator ---------------------------------------------------- */
+/* Replaces AwaVk::forward (src/awa_vk.h:39-44, src/awa_vk.cpp:114-251) and
+ * the CPU attention branch of DitVk::awa_forward (src/dit_vk.cpp:344-455):
+ * qk RMSNorm (eps), 3-axis RoPE, per-window SDPA over [window vid | txt],
+ * reverse partition (tokens outside every window get 0), txt mean over
+ * windows.  vqkv (Lv,7680), tqkv (TXT,7680), nq_v/nk_v/nq_t/nk_t (128) fp32 host;
+ * vid_out (Lv,2560), txt_out (TXT,2560). */
+int s2b_awa_forward(s2b_ctx* ctx, const float* vqkv, const float* tqkv, const s2b_win* win,
+                    const float* nq_v, const float* nk_v, const float* nq_t, const float* nk_t,
+                    int Lv, int TXT, float eps, float* vid_out, float* txt_out);
+/* Replaces AwaLayer::forward (src/awa_layer.cpp:284-453): same op on device
+ * buffers, enqueued on `stream`; the geometry is the one last passed to
+ * s2b_awa_set_geometry for `win_type` (0 non-shifted, 1 shifted), like
+ * AwaLayer::set_window_geometry (src/awa_layer.cpp:73-91). */
+int s2b_awa_set_geometry(s2b_ctx* ctx, int win_type, const s2b_win* win);
+int s2b_awa_forward_dev(s2b_ctx* ctx, int win_type, const float* d_vqkv, const float* d_tqkv,
+                        const float* d_nq_v, const float* d_nk_v, const float* d_nq_t, const float* d_nk_t,
+                        int Lv, int TXT, float eps, float* d_vid_out, float* d_txt_out, void* stream);
+
+/* ---- adaLN ----------------------------------------------------------- */
+/* Replaces DitVk::time_embedding (src/dit_vk.cpp:295-309): emb[15360]. */
+int s2b_time_embedding(s2b_ctx* ctx, float timestep, float* emb);
+/* Replaces AdaComposeLayer::forward (src/ada_compose.cpp:166-235) and
+ * DitVk::compute_ada (src/dit_graph.cpp:196-216): from emb[15360] writes the
+ * 32*12 + 2 modulation vectors of 2560 in the layer's output order
+ * [layer][flow vid,txt][a_sc,a_sh,a_g,m_sc,m_sh,m_g], then fin_sc, fin_sh. */
+int s2b_ada_compose(s2b_ctx* ctx, const float* emb, float* out);
+
+/* ---- synthetic data (no checkpoint ships with this build) ------------- */
+/* Writes the m5 directory layout for layers [layer_lo, layer_hi) with
+ * seeded random-init weights (Linear N(0,0.02) stored fp16; biases and
+ * shifts N(0,0.02); norm weights, scales, gates 1+N(0,0.02)). */
+int s2b_synth_write_m5(const char* dir, uint64_t seed, int layer_lo, int layer_hi);
+/* Seeded inputs: vid_grid (T,H,W,33) = [noise N(0,1) x16 | condition N(0,1)
+ * x16 | mask 1], txt (TXT,5120) N(0,1); fp32 normals of a named stream. */
+int s2b_synth_vid_grid(float* vid_grid, int T, int H, int W, uint64_t seed);
+int s2b_synth_txt(float* txt, int TXT, uint64_t seed);
+int s2b_synth_normal(float* out, long n, uint64_t seed, const char* stream, float mean, float stdv);
+
+/* ---- multi-GPU ------------------------------------------------------- */
+/* Window-sharded image mode: one rank per GPU; each rank owns a subset of
+ * the windows of every layer, txt rows are replicated, and the txt partial
+ * sums of the attention are summed across ranks with one NCCL all-reduce
+ * per layer.  `nccl_id` is the 128-byte ncclUniqueId created by rank 0 and
+ * shared over any host channel. */
+int s2b_nccl_unique_id(uint8_t nccl_id[128]);
+int s2b_shard_init(s2b_ctx* ctx, const uint8_t nccl_id[128], int world, int rank);
+int s2b_shard_forward(s2b_ctx* ctx, const float* vid_patch, int Lv, const float* txt, int TXT,
+                      float timestep, float* sr_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SEEDVR2_B200_H */

@@ -1,0 +1,691 @@
+// dit_b200.cpp -- B200 NaDiT DiT host engine (see dit_b200.h).
+//
+// One forward is the reference's DitVk::forward_latent (src/dit_vk.cpp:486-699)
+// laid out for the GPU:
+//   * one fp32 residual buffer X of (Lv + TXT) rows: vid rows first, txt rows
+//     after, so layers 10..31 (vid/txt share weights, src/dit_vk.cpp:163-164)
+//     run each Linear as ONE GEMM over both streams, and layers 0..9 run two;
+//   * every Linear's operands in the context precision (fp32 or bf16), fp32
+//     accumulation, and the adaLN gate + residual add fused in the GEMM
+//     epilogue; proj_in / proj_in_gate are one GEMM over interleaved weights;
+//   * AWA = pack (qk-norm + RoPE into window-packed Q/K/V) -> attention ->
+//     txt coalesce;
+//   * the 32*12+2 modulation vectors are composed once per timestep
+//     (AdaComposeLayer semantics, src/ada_compose.cpp:166-235);
+//   * s2b_forward replays the whole forward from one captured CUDA graph.
+#include "dit_b200.h"
+#include "dit_shard.h"
+#include "synth.h"
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <sstream>
+
+namespace s2b {
+
+DitB200::~DitB200() {
+    if (dev_ >= 0) cudaSetDevice(dev_);
+    shard_.reset();
+    if (gexec_) cudaGraphExecDestroy(gexec_);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+int DitB200::cuda_check(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return OK;
+    err = std::string(what) + ": " + cudaGetErrorString(e);
+    return e == cudaErrorMemoryAllocation ? ERR_NOMEM : ERR_CUDA;
+}
+
+int DitB200::create(int device, int precision) {
+    if (precision == PREC_FP16) return fail(ERR_UNSUPPORTED, "fp16 operands are not offered on B200; use fp32 (0) or bf16 (2)");
+    if (precision != PREC_FP32 && precision != PREC_BF16) return fail(ERR_ARG, "precision must be 0 (fp32) or 2 (bf16)");
+    int n = 0;
+    if (int rc = cuda_check(cudaGetDeviceCount(&n), "cudaGetDeviceCount")) return rc;
+    if (device < 0 || device >= n) return fail(ERR_ARG, "device index out of range");
+    dev_ = device;
+    if (int rc = cuda_check(cudaSetDevice(dev_), "cudaSetDevice")) return rc;
+    cudaDeviceProp prop;
+    if (int rc = cuda_check(cudaGetDeviceProperties(&prop, dev_), "cudaGetDeviceProperties")) return rc;
+    if (prop.major != 10) return fail(ERR_UNSUPPORTED, std::string("sm_100a kernels need a B200-class GPU, found ") + prop.name);
+    prec_ = precision;
+    act_ = (precision == PREC_BF16) ? ACT_BF16 : ACT_F32;
+    if (int rc = cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate")) return rc;
+    if (kernels_init_device() != 0) return fail(ERR_CUDA, "kernel attribute setup failed");
+    return OK;
+}
+
+uint64_t DitB200::device_bytes() const {
+    uint64_t t = 0;
+    auto lin = [&](const Linear& L) { t += L.w.bytes + L.b.bytes; };
+    lin(vid_in_); lin(txt_in_); lin(emb_in_); lin(emb_hid_); lin(emb_out_); lin(vid_out_);
+    for (int i = 0; i < NUM_LAYERS; i++)
+        for (int f = 0; f < (i < MM_LAYERS ? 2 : 1); f++) {
+            const Block& B = blk_[i][f];
+            lin(B.qkv); lin(B.out); lin(B.mlp_hg); lin(B.mlp_out);
+        }
+    for (const DevBuf* b : {&branch_, &qknorm_, &von_w_, &ada_, &emb_, &X_, &Xn_, &QKV_, &ATT_, &Qp_, &Kp_, &Vp_,
+                            &TOUTW_, &HG_, &Hs_, &VPIN_, &TIN_, &SR_, &VIDIN_F_, &TXTIN_F_})
+        t += b->bytes;
+    return t;
+}
+
+// ------------------------------------------------------------------ weights
+int DitB200::upload_linear(Linear& L, const void* w_src, bool src_f16, const float* bias, int out, int in, ActT t,
+                           int ld, int interleave_role) {
+    // interleave_role: -1 plain; 0 / 1: proj_in / proj_in_gate into the [h|g]
+    // 128-row block layout of mlp_hg (destination already sized 2*out rows).
+    DevBuf stage;
+    const size_t src_bytes = (size_t)out * in * (src_f16 ? 2 : 4);
+    if (int rc = cuda_check(stage.ensure(src_bytes), "cudaMalloc(weight staging)")) return rc;
+    if (int rc = cuda_check(cudaMemcpy(stage.p, w_src, src_bytes, cudaMemcpyHostToDevice), "upload weight")) return rc;
+    if (interleave_role < 0) {
+        L.t = t; L.out = out; L.in = in; L.ld = ld;
+        if (int rc = cuda_check(L.w.ensure((size_t)out * ld * act_bytes(t)), "cudaMalloc(weight)")) return rc;
+        ingest_weight(stage.p, src_f16, out, in, L.w.p, t, ld, 0, 0, 0, stream_);
+    } else {
+        if (!L.w.p) {
+            L.t = t; L.out = 2 * out; L.in = in; L.ld = ld;
+            if (int rc = cuda_check(L.w.ensure((size_t)2 * out * ld * act_bytes(t)), "cudaMalloc(weight)")) return rc;
+        }
+        ingest_weight(stage.p, src_f16, out, in, L.w.p, t, ld, 128, 256, interleave_role * 128, stream_);
+    }
+    if (bias) {
+        if (int rc = cuda_check(L.b.ensure((size_t)out * 4), "cudaMalloc(bias)")) return rc;
+        if (int rc = cuda_check(cudaMemcpy(L.b.p, bias, (size_t)out * 4, cudaMemcpyHostToDevice), "upload bias")) return rc;
+    }
+    return cuda_check(cudaStreamSynchronize(stream_), "weight ingest");
+}
+
+namespace {
+// Weights as stored: fp16 bits (ncnn tag 0x01306B47) or fp32 (tag 0).
+struct HostLinear {
+    int out = 0, in = 0; bool has_bias = false; bool f16 = true;
+    std::vector<uint16_t> w; std::vector<float> wf; std::vector<float> b;
+    const void* data() const { return f16 ? (const void*)w.data() : (const void*)wf.data(); }
+};
+
+bool read_file(const std::string& p, std::vector<unsigned char>& out) {
+    std::ifstream f(p, std::ios::binary);
+    if (!f) return false;
+    f.seekg(0, std::ios::end);
+    out.resize((size_t)f.tellg());
+    f.seekg(0);
+    f.read((char*)out.data(), (std::streamsize)out.size());
+    return (bool)f;
+}
+
+// ncnn InnerProduct .param/.bin pair (format: src/verify_dit.cpp:62-104).
+bool load_host_linear(const std::string& dir, const std::string& base, HostLinear& L, std::string& err) {
+    std::ifstream pf(dir + base + ".param");
+    if (!pf) { err = "missing " + dir + base + ".param"; return false; }
+    std::string line;
+    int nout = 0, bias = 0, wsz = 0;
+    while (std::getline(pf, line)) {
+        if (line.find("InnerProduct") == std::string::npos) continue;
+        std::istringstream ss(line);
+        std::string tok;
+        while (ss >> tok) {
+            if (tok.rfind("0=", 0) == 0) nout = std::atoi(tok.c_str() + 2);
+            else if (tok.rfind("1=", 0) == 0) bias = std::atoi(tok.c_str() + 2);
+            else if (tok.rfind("2=", 0) == 0) wsz = std::atoi(tok.c_str() + 2);
+        }
+    }
+    if (nout <= 0 || wsz <= 0 || wsz % nout) { err = "bad InnerProduct param in " + base; return false; }
+    std::vector<unsigned char> blob;
+    if (!read_file(dir + base + ".bin", blob)) { err = "missing " + dir + base + ".bin"; return false; }
+    L.out = nout; L.in = wsz / nout; L.has_bias = bias != 0;
+    if (blob.size() < 4) { err = "short " + base + ".bin"; return false; }
+    uint32_t tag; std::memcpy(&tag, blob.data(), 4);
+    size_t off = 4;
+    if (tag == 0x01306B47u) {
+        if (blob.size() < off + 2 * (size_t)wsz) { err = "short " + base + ".bin"; return false; }
+        L.f16 = true;
+        L.w.resize((size_t)wsz);
+        std::memcpy(L.w.data(), blob.data() + off, 2 * (size_t)wsz);
+        off += 2 * (size_t)wsz;
+    } else if (tag == 0u) {
+        if (blob.size() < off + 4 * (size_t)wsz) { err = "short " + base + ".bin"; return false; }
+        L.f16 = false;
+        L.wf.resize((size_t)wsz);
+        std::memcpy(L.wf.data(), blob.data() + off, 4 * (size_t)wsz);
+        off += 4 * (size_t)wsz;
+    } else { err = "unsupported weight tag in " + base; return false; }
+    if (L.has_bias) {
+        if (blob.size() < off + 4 * (size_t)nout) { err = "short bias in " + base; return false; }
+        L.b.resize(nout);
+        std::memcpy(L.b.data(), blob.data() + off, 4 * (size_t)nout);
+    }
+    return true;
+}
+
+bool load_host_vector(const std::string& dir, const std::string& base, std::vector<float>& v, std::string& err) {
+    std::vector<unsigned char> blob;
+    if (!read_file(dir + base + ".bin", blob) || blob.size() < 8) { err = "missing " + dir + base + ".bin"; return false; }
+    int64_t nd; std::memcpy(&nd, blob.data(), 8);
+    if (nd < 0 || nd > 8 || blob.size() < 8 + 8 * (size_t)nd) { err = "bad header " + base; return false; }
+    int64_t total = 1;
+    for (int64_t i = 0; i < nd; i++) { int64_t d; std::memcpy(&d, blob.data() + 8 + 8 * i, 8); total *= d; }
+    const size_t off = 8 + 8 * (size_t)nd;
+    if (total < 0 || blob.size() < off + 4 * (size_t)total) { err = "short " + base; return false; }
+    v.resize((size_t)total);
+    std::memcpy(v.data(), blob.data() + off, 4 * (size_t)total);
+    return true;
+}
+}  // namespace
+
+int DitB200::load_weights(const char* dir_c, bool synth, uint64_t seed, int lo, int hi) {
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    lo = std::max(0, lo); hi = std::min(NUM_LAYERS, hi);
+    cudaSetDevice(dev_);
+    std::string dir = dir_c ? dir_c : "";
+    if (!synth && (dir.empty())) return fail(ERR_ARG, "empty model directory");
+    if (!synth && dir.back() != '/') dir += '/';
+    if (gexec_) { cudaGraphExecDestroy(gexec_); gexec_ = nullptr; graph_Lv_ = -1; }
+    for (auto& row : blk_) for (auto& b : row) b = Block();
+
+    auto get_lin = [&](const SynthLinear& S, HostLinear& H) -> bool {
+        if (synth) {
+            H.out = S.out; H.in = S.in; H.has_bias = S.has_bias;
+            H.w.resize((size_t)S.out * S.in);
+            H.b.resize(S.has_bias ? S.out : 0);
+            synth_linear(S, seed, H.w.data(), S.has_bias ? H.b.data() : nullptr);
+            return true;
+        }
+        if (!load_host_linear(dir, S.name, H, err)) return false;
+        if (H.out != S.out || H.in != S.in) { err = "shape mismatch for " + S.name; return false; }
+        return true;
+    };
+    const ActT wt = act_;
+    for (const auto& S : model_linears(lo, hi)) {
+        HostLinear H;
+        if (!get_lin(S, H)) return ERR_IO;
+        const float* b = H.has_bias ? H.b.data() : nullptr;
+        int rc = OK;
+        const std::string& n = S.name;
+        if (n == "vid_in_proj") rc = upload_linear(vid_in_, H.data(), H.f16, b, H.out, H.in, wt, PATCH_IN_PAD, -1);
+        else if (n == "txt_in") rc = upload_linear(txt_in_, H.data(), H.f16, b, H.out, H.in, wt, H.in, -1);
+        else if (n == "emb_proj_in") rc = upload_linear(emb_in_, H.data(), H.f16, b, H.out, H.in, ACT_F32, H.in, -1);
+        else if (n == "emb_proj_hid") rc = upload_linear(emb_hid_, H.data(), H.f16, b, H.out, H.in, ACT_F32, H.in, -1);
+        else if (n == "emb_proj_out") rc = upload_linear(emb_out_, H.data(), H.f16, b, H.out, H.in, ACT_F32, H.in, -1);
+        else if (n == "vid_out_proj") rc = upload_linear(vid_out_, H.data(), H.f16, b, H.out, H.in, wt, H.in, -1);
+        else {
+            // b{i}_{vid|txt|all}_{qkv,out,mlp_in,mlp_g,mlp_out}
+            int i = 0; char tag[8] = {0}, what[16] = {0};
+            if (std::sscanf(n.c_str(), "b%d_%3[a-z]_%15s", &i, tag, what) != 3) return fail(ERR_IO, "bad weight name " + n);
+            const int fl = (std::strcmp(tag, "txt") == 0) ? 1 : 0;
+            Block& B = blk_[i][fl];
+            const std::string w = what;
+            if (w == "qkv") rc = upload_linear(B.qkv, H.data(), H.f16, b, H.out, H.in, wt, H.in, -1);
+            else if (w == "out") rc = upload_linear(B.out, H.data(), H.f16, b, H.out, H.in, wt, H.in, -1);
+            else if (w == "mlp_in") rc = upload_linear(B.mlp_hg, H.data(), H.f16, b, H.out, H.in, wt, H.in, 0);
+            else if (w == "mlp_g") rc = upload_linear(B.mlp_hg, H.data(), H.f16, b, H.out, H.in, wt, H.in, 1);
+            else if (w == "mlp_out") { rc = upload_linear(B.mlp_out, H.data(), H.f16, b, H.out, H.in, wt, H.in, -1); B.loaded = true; }
+            else return fail(ERR_IO, "bad weight name " + n);
+        }
+        if (rc) return rc;
+    }
+    // raw vectors
+    std::vector<float> branch((size_t)(NUM_LAYERS * 12 + 2) * DIM), qkn((size_t)NUM_LAYERS * 2 * 2 * HEAD_D), von;
+    auto get_vec = [&](const std::string& name, int n, float mean, std::vector<float>& v) -> bool {
+        if (synth) { v.resize(n); synth_vector({name, n, mean}, seed, v.data()); return true; }
+        if (!load_host_vector(dir, name, v, err)) return false;
+        if ((int)v.size() != n) { err = "size mismatch for " + name; return false; }
+        return true;
+    };
+    std::vector<float> v;
+    if (!get_vec("vid_out_norm_w", DIM, 1.f, von)) return ERR_IO;
+    if (!get_vec("vid_out_ada_scale", DIM, 1.f, v)) return ERR_IO;
+    std::memcpy(&branch[(size_t)(NUM_LAYERS * 12) * DIM], v.data(), DIM * 4);
+    if (!get_vec("vid_out_ada_shift", DIM, 0.f, v)) return ERR_IO;
+    std::memcpy(&branch[(size_t)(NUM_LAYERS * 12 + 1) * DIM], v.data(), DIM * 4);
+    static const char* bnames[6] = {"attn_scale", "attn_shift", "attn_gate", "mlp_scale", "mlp_shift", "mlp_gate"};
+    static const float bmeans[6] = {1.f, 0.f, 1.f, 1.f, 0.f, 1.f};
+    for (int i = 0; i < NUM_LAYERS; i++)
+        for (int fl = 0; fl < 2; fl++) {
+            const std::string base = "b" + std::to_string(i) + "_" + (i < MM_LAYERS ? (fl ? "txt" : "vid") : "all") + "_";
+            for (int k = 0; k < 6; k++) {
+                if (!get_vec(base + bnames[k], DIM, bmeans[k], v)) return ERR_IO;
+                std::memcpy(&branch[((size_t)(i * 12 + fl * 6 + k)) * DIM], v.data(), DIM * 4);
+            }
+            if (!get_vec(base + "nq", HEAD_D, 1.f, v)) return ERR_IO;
+            std::memcpy(&qkn[((size_t)((i * 2 + fl) * 2 + 0)) * HEAD_D], v.data(), HEAD_D * 4);
+            if (!get_vec(base + "nk", HEAD_D, 1.f, v)) return ERR_IO;
+            std::memcpy(&qkn[((size_t)((i * 2 + fl) * 2 + 1)) * HEAD_D], v.data(), HEAD_D * 4);
+        }
+    if (int rc = cuda_check(branch_.ensure(branch.size() * 4), "cudaMalloc")) return rc;
+    if (int rc = cuda_check(qknorm_.ensure(qkn.size() * 4), "cudaMalloc")) return rc;
+    if (int rc = cuda_check(von_w_.ensure(DIM * 4), "cudaMalloc")) return rc;
+    if (int rc = cuda_check(ada_.ensure(branch.size() * 4), "cudaMalloc")) return rc;
+    if (int rc = cuda_check(emb_.ensure(EMB_DIM * 4), "cudaMalloc")) return rc;
+    if (int rc = cuda_check(temb_in_.ensure(TEMB_IN * 4), "cudaMalloc")) return rc;
+    if (int rc = cuda_check(temb_h1_.ensure(DIM * 4), "cudaMalloc")) return rc;
+    if (int rc = cuda_check(temb_h2_.ensure(DIM * 4), "cudaMalloc")) return rc;
+    cudaMemcpy(branch_.p, branch.data(), branch.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(qknorm_.p, qkn.data(), qkn.size() * 4, cudaMemcpyHostToDevice);
+    if (int rc = cuda_check(cudaMemcpy(von_w_.p, von.data(), DIM * 4, cudaMemcpyHostToDevice), "upload vectors")) return rc;
+    // shared layers: the txt flow uses the same Linear objects
+    layer_lo_ = lo; layer_hi_ = hi;
+    weights_ = true;
+    return OK;
+}
+
+// ------------------------------------------------------------------ geometry
+int DitB200::upload_geom(GeomDev& g, const WinGeom& w, int TXT_expected) {
+    const char* why = nullptr;
+    WinTables tab;
+    if (!build_tables(w, tab, &why)) return fail(ERR_ARG, std::string("window geometry: ") + why);
+    if (TXT_expected >= 0 && w.txt_len != TXT_expected) return fail(ERR_ARG, "window txt_len differs from TXT");
+    const int nwin = w.nwin(), TXT = w.txt_len;
+    std::vector<int> row_win((size_t)tab.cums[nwin]);
+    for (int i = 0; i < nwin; i++)
+        for (int p = tab.cums[i]; p < tab.cums[i + 1]; p++) row_win[p] = i;
+    // cos/sin of every element's own angle, in float as the reference
+    // evaluates them (src/dit_vk.cpp:66).
+    std::vector<float> vc(w.vid_freq.size()), vs(w.vid_freq.size()), tc(w.txt_freq.size()), ts(w.txt_freq.size());
+    for (size_t i = 0; i < vc.size(); i++) { vc[i] = cosf(w.vid_freq[i]); vs[i] = sinf(w.vid_freq[i]); }
+    for (size_t i = 0; i < tc.size(); i++) { tc[i] = cosf(w.txt_freq[i]); ts[i] = sinf(w.txt_freq[i]); }
+    auto up = [&](DevBuf& d, const void* src, size_t n) -> int {
+        if (int rc = cuda_check(d.ensure(std::max<size_t>(n, 16)), "cudaMalloc(geometry)")) return rc;
+        if (n) return cuda_check(cudaMemcpy(d.p, src, n, cudaMemcpyHostToDevice), "upload geometry");
+        return OK;
+    };
+    if (int rc = up(g.vidx, tab.vidx.data(), tab.vidx.size() * 4)) return rc;
+    if (int rc = up(g.cumf, tab.cumf.data(), tab.cumf.size() * 4)) return rc;
+    if (int rc = up(g.cums, tab.cums.data(), tab.cums.size() * 4)) return rc;
+    if (int rc = up(g.row_win, row_win.data(), row_win.size() * 4)) return rc;
+    if (int rc = up(g.vcos, vc.data(), vc.size() * 4)) return rc;
+    if (int rc = up(g.vsin, vs.data(), vs.size() * 4)) return rc;
+    if (int rc = up(g.tcos, tc.data(), tc.size() * 4)) return rc;
+    if (int rc = up(g.tsin, ts.data(), ts.size() * 4)) return rc;
+    g.host = w;
+    g.tab = tab;
+    AwaDev& v = g.view;
+    v.nwin = nwin; v.TXT = TXT; v.sumf = tab.sumf; v.sumS = tab.cums[nwin]; v.maxS = tab.maxS; v.Lv = w.tokens();
+    v.vidx = g.vidx.as<int>(); v.cumf = g.cumf.as<int>(); v.cums = g.cums.as<int>(); v.row_win = g.row_win.as<int>();
+    v.vcos = g.vcos.as<float>(); v.vsin = g.vsin.as<float>(); v.tcos = g.tcos.as<float>(); v.tsin = g.tsin.as<float>();
+    g.ready = true;
+    return OK;
+}
+
+int DitB200::set_windows(const WinGeom& ns, const WinGeom& sh) {
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    cudaSetDevice(dev_);
+    if (ns.tokens() != sh.tokens() || ns.txt_len != sh.txt_len) return fail(ERR_ARG, "non-shifted and shifted windows disagree on the grid");
+    if (int rc = upload_geom(geom_[0], ns, -1)) return rc;
+    if (int rc = upload_geom(geom_[1], sh, -1)) return rc;
+    if (!geom_[0].tab.covers_all || !geom_[1].tab.covers_all)
+        return fail(ERR_ARG, "DiT windows must tile the token grid exactly");
+    if (gexec_) { cudaGraphExecDestroy(gexec_); gexec_ = nullptr; graph_Lv_ = -1; }
+    return OK;
+}
+
+// ------------------------------------------------------------------ activations
+int DitB200::ensure_acts(int Lv, int TXT) {
+    const size_t M = (size_t)Lv + TXT, ab = act_bytes(act_);
+    size_t sumS = 0, nwinTXT = 0;
+    for (auto& g : geom_)
+        if (g.ready) { sumS = std::max(sumS, (size_t)g.view.sumS); nwinTXT = std::max(nwinTXT, (size_t)g.view.nwin * g.view.TXT); }
+    int rc;
+    if ((rc = cuda_check(X_.ensure(M * DIM * 4), "cudaMalloc(X)"))) return rc;
+    if ((rc = cuda_check(Xn_.ensure(M * DIM * ab), "cudaMalloc(Xn)"))) return rc;
+    if ((rc = cuda_check(QKV_.ensure(M * QKV * ab), "cudaMalloc(QKV)"))) return rc;
+    if ((rc = cuda_check(ATT_.ensure(M * DIM * ab), "cudaMalloc(ATT)"))) return rc;
+    if ((rc = cuda_check(Qp_.ensure(std::max<size_t>(sumS, 1) * DIM * ab), "cudaMalloc(Qp)"))) return rc;
+    if ((rc = cuda_check(Kp_.ensure(std::max<size_t>(sumS, 1) * DIM * ab), "cudaMalloc(Kp)"))) return rc;
+    if ((rc = cuda_check(Vp_.ensure(std::max<size_t>(sumS, 1) * DIM * ab), "cudaMalloc(Vp)"))) return rc;
+    if ((rc = cuda_check(TOUTW_.ensure(std::max<size_t>(nwinTXT, 1) * DIM * 4), "cudaMalloc(TOUTW)"))) return rc;
+    if (act_ == ACT_F32 && (rc = cuda_check(HG_.ensure(M * 2 * MLP_DIM * 4), "cudaMalloc(HG)"))) return rc;
+    if ((rc = cuda_check(Hs_.ensure(M * MLP_DIM * ab), "cudaMalloc(Hs)"))) return rc;
+    if ((rc = cuda_check(VPIN_.ensure((size_t)Lv * PATCH_IN_PAD * ab), "cudaMalloc(VPIN)"))) return rc;
+    if ((rc = cuda_check(TIN_.ensure((size_t)TXT * TXT_IN * ab), "cudaMalloc(TIN)"))) return rc;
+    if ((rc = cuda_check(SR_.ensure((size_t)Lv * OUT_CH * 4), "cudaMalloc(SR)"))) return rc;
+    if ((rc = cuda_check(VIDIN_F_.ensure((size_t)Lv * DIM * 4), "cudaMalloc(VIDIN)"))) return rc;
+    if ((rc = cuda_check(TXTIN_F_.ensure((size_t)TXT * TXT_IN * 4), "cudaMalloc(TXTIN)"))) return rc;
+    cap_Lv_ = std::max(cap_Lv_, Lv); cap_TXT_ = std::max(cap_TXT_, TXT);
+    return OK;
+}
+
+// ------------------------------------------------------------------ enqueue
+void DitB200::gemm(const void* A, int lda, const Linear& L, int M, const GemmEpi& e, cudaStream_t s) {
+    if (M <= 0) return;
+    if (act_ == ACT_BF16 && L.t == ACT_BF16 && gemm_tc_supported(M, L.out, L.in, lda, L.ld)) {
+        gemm_tc(A, lda, L.w.p, L.ld, M, L.out, L.in, e, s, &launches_);
+        return;
+    }
+    if (e.mode == EPI_SWIGLU) {
+        // SIMT path: materialise [h | g] in fp32, then combine.
+        GemmEpi st; st.mode = EPI_STORE; st.out = HG_.p; st.ldo = 2 * MLP_DIM; st.out_t = ACT_F32;
+        gemm_simt(A, act_, lda, L.w.p, L.t, L.ld, M, L.out, L.in, st, s);
+        swiglu_rows(HG_.as<float>(), M, 2 * MLP_DIM, e.out, e.ldo, e.out_t, s);
+        launches_ += 2;
+        return;
+    }
+    gemm_simt(A, act_, lda, L.w.p, L.t, L.ld, M, L.out, L.in, e, s);
+    launches_++;
+}
+
+static void sinusoidal256(float t, float* e) {   // src/dit_vk.cpp:295-302
+    const int half = 128;
+    for (int j = 0; j < 256; j++) {
+        float freq = (j < half) ? (float)std::exp(-logf(10000.f) * j / half) : (float)std::exp(-logf(10000.f) * (j - half) / half);
+        e[j] = (j < half) ? sinf(t * freq) : cosf(t * freq);
+    }
+}
+
+int DitB200::enqueue_temb(cudaStream_t s) {
+    // time embedding (src/dit_vk.cpp:303-309) in fp32, then AdaCompose.
+    GemmEpi e; e.mode = EPI_STORE; e.out_t = ACT_F32;
+    e.bias = emb_in_.bias(); e.out = temb_h1_.p; e.ldo = DIM;
+    gemm_simt(temb_in_.p, ACT_F32, TEMB_IN, emb_in_.w.p, ACT_F32, emb_in_.ld, 1, DIM, TEMB_IN, e, s);
+    silu_inplace(temb_h1_.as<float>(), DIM, s);
+    e.bias = emb_hid_.bias(); e.out = temb_h2_.p;
+    gemm_simt(temb_h1_.p, ACT_F32, DIM, emb_hid_.w.p, ACT_F32, emb_hid_.ld, 1, DIM, DIM, e, s);
+    silu_inplace(temb_h2_.as<float>(), DIM, s);
+    e.bias = emb_out_.bias(); e.out = emb_.p; e.ldo = EMB_DIM;
+    gemm_simt(temb_h2_.p, ACT_F32, DIM, emb_out_.w.p, ACT_F32, emb_out_.ld, 1, EMB_DIM, DIM, e, s);
+    s2b::ada_compose(emb_.as<float>(), branch_.as<float>(), NUM_LAYERS * 12 + 2, ada_.as<float>(), s);
+    launches_ += 6;
+    return OK;
+}
+
+int DitB200::enqueue_init(int Lv, int TXT, cudaStream_t s) {
+    // vid_in_proj (132 -> 2560) and txt_in (5120 -> 2560), src/dit_vk.cpp:494-497
+    pad_convert_rows(VIDIN_F_.as<float>(), Lv, PATCH_IN, VPIN_.p, PATCH_IN_PAD, act_, s);
+    pad_convert_rows(TXTIN_F_.as<float>(), TXT, TXT_IN, TIN_.p, TXT_IN, act_, s);
+    launches_ += 2;
+    GemmEpi e; e.mode = EPI_STORE; e.out_t = ACT_F32; e.ldo = DIM;
+    e.bias = vid_in_.bias(); e.out = X_.p;
+    gemm(VPIN_.p, PATCH_IN_PAD, vid_in_, Lv, e, s);
+    e.bias = txt_in_.bias(); e.out = X_.as<float>() + (size_t)Lv * DIM;
+    gemm(TIN_.p, TXT_IN, txt_in_, TXT, e, s);
+    return OK;
+}
+
+int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s) {
+    const bool dual = i < MM_LAYERS, last = (i == NUM_LAYERS - 1);
+    const int M = Lv + TXT;
+    const size_t ab = act_bytes(act_);
+    GeomDev& G = geom_[i % 2];
+    const Block& BV = blk_[i][0];
+    const Block& BT = dual ? blk_[i][1] : blk_[i][0];
+    char* xn = (char*)Xn_.p;
+    char* qkv = (char*)QKV_.p;
+    char* att = (char*)ATT_.p;
+    char* hs = (char*)Hs_.p;
+    float* X = X_.as<float>();
+
+    // 1. attention norm + modulate (txt unmodulated on the last layer, src/dit_vk.cpp:538)
+    rmsnorm_mod(X, DIM, M, Lv, ada(i, 0, 0), ada(i, 0, 1), last ? nullptr : ada(i, 1, 0), ada(i, 1, 1), nullptr,
+                NORM_EPS, Xn_.p, DIM, act_, s);
+    launches_++;
+    // 2. qkv projection (no bias)
+    GemmEpi e; e.mode = EPI_STORE; e.out_t = act_; e.ldo = QKV;
+    if (dual) {
+        e.out = qkv; gemm(xn, DIM, BV.qkv, Lv, e, s);
+        e.out = qkv + (size_t)Lv * QKV * ab; gemm(xn + (size_t)Lv * DIM * ab, DIM, BT.qkv, TXT, e, s);
+    } else {
+        e.out = qkv; gemm(xn, DIM, BV.qkv, M, e, s);
+    }
+    // 3. AWA
+    awa_pack(qkv, qkv + (size_t)Lv * QKV * ab, act_, QKV, G.view, normw(i, 0, 0), normw(i, 0, 1), normw(i, 1, 0),
+             normw(i, 1, 1), NORM_EPS, Qp_.p, Kp_.p, Vp_.p, act_, s);
+    launches_++;
+    awa_attend(Qp_.p, Kp_.p, Vp_.p, act_, G.view, 1.0f / sqrtf((float)HEAD_D), att, DIM, act_, TOUTW_.as<float>(), s,
+               &launches_);
+    awa_coalesce(TOUTW_.as<float>(), G.view.nwin, TXT, att + (size_t)Lv * DIM * ab, DIM, act_, s);
+    launches_++;
+    // 4. out projection (+bias), gate, residual (src/dit_vk.cpp:461-462, 558-575)
+    GemmEpi g; g.mode = EPI_GATE_RESID; g.ldr = DIM;
+    if (dual) {
+        g.resid = X; g.bias = BV.out.bias(); g.gate0 = ada(i, 0, 2); g.gate_split = M;
+        gemm(att, DIM, BV.out, Lv, g, s);
+        g.resid = X + (size_t)Lv * DIM; g.bias = BT.out.bias(); g.gate0 = last ? nullptr : ada(i, 1, 2);
+        gemm(att + (size_t)Lv * DIM * ab, DIM, BT.out, TXT, g, s);
+    } else {
+        g.resid = X; g.bias = BV.out.bias(); g.gate0 = ada(i, 0, 2); g.gate1 = last ? nullptr : ada(i, 1, 2);
+        g.gate_split = Lv;
+        gemm(att, DIM, BV.out, M, g, s);
+    }
+    // 5. MLP norm + modulate; txt skips the MLP on the last layer (src/dit_vk.cpp:579-620)
+    const int Mm = last ? Lv : M;
+    rmsnorm_mod(X, DIM, Mm, Lv, ada(i, 0, 3), ada(i, 0, 4), ada(i, 1, 3), ada(i, 1, 4), nullptr, NORM_EPS, Xn_.p, DIM,
+                act_, s);
+    launches_++;
+    // 6. SwiGLU: proj_out(silu(proj_in_gate x) * proj_in x)
+    GemmEpi sw; sw.mode = EPI_SWIGLU; sw.out_t = act_; sw.ldo = MLP_DIM;
+    GemmEpi mo; mo.mode = EPI_GATE_RESID; mo.ldr = DIM;
+    if (dual) {
+        sw.out = hs; gemm(xn, DIM, BV.mlp_hg, Lv, sw, s);
+        mo.resid = X; mo.gate0 = ada(i, 0, 5); mo.gate_split = M;
+        gemm(hs, MLP_DIM, BV.mlp_out, Lv, mo, s);
+        if (!last) {
+            sw.out = hs + (size_t)Lv * MLP_DIM * ab; gemm(xn + (size_t)Lv * DIM * ab, DIM, BT.mlp_hg, TXT, sw, s);
+            mo.resid = X + (size_t)Lv * DIM; mo.gate0 = ada(i, 1, 5);
+            gemm(hs + (size_t)Lv * MLP_DIM * ab, MLP_DIM, BT.mlp_out, TXT, mo, s);
+        }
+    } else {
+        sw.out = hs; gemm(xn, DIM, BV.mlp_hg, Mm, sw, s);
+        mo.resid = X; mo.gate0 = ada(i, 0, 5); mo.gate1 = ada(i, 1, 5); mo.gate_split = Lv;
+        gemm(hs, MLP_DIM, BV.mlp_out, Mm, mo, s);
+    }
+    return OK;
+}
+
+int DitB200::enqueue_final(int Lv, cudaStream_t s) {
+    // final RMSNorm (affine) + modulate (fin_sc, fin_sh) + vid_out_proj (src/dit_vk.cpp:657-675)
+    const float* fin_sc = ada_.as<float>() + (size_t)(NUM_LAYERS * 12) * DIM;
+    const float* fin_sh = fin_sc + DIM;
+    rmsnorm_mod(X_.as<float>(), DIM, Lv, Lv, fin_sc, fin_sh, nullptr, nullptr, von_w_.as<float>(), NORM_EPS, Xn_.p,
+                DIM, act_, s);
+    launches_++;
+    GemmEpi e; e.mode = EPI_STORE; e.out_t = ACT_F32; e.ldo = OUT_CH; e.bias = vid_out_.bias(); e.out = SR_.p;
+    gemm(Xn_.p, DIM, vid_out_, Lv, e, s);
+    return OK;
+}
+
+// ------------------------------------------------------------------ public forwards
+int DitB200::forward_latent(const float* vid_in, int Lv, const float* txt_in, int TXT, float t, int l0, int l1,
+                            bool do_init, bool do_final, float* vid_lat, float* txt_lat, float* sr_out) {
+    if (!weights_) return fail(ERR_STATE, "weights not loaded");
+    if (!geom_[0].ready || !geom_[1].ready) return fail(ERR_STATE, "windows not set");
+    if (Lv != geom_[0].view.Lv) return fail(ERR_ARG, "Lv does not match the window grid");
+    if (TXT != geom_[0].view.TXT || TXT <= 0) return fail(ERR_ARG, "TXT does not match the windows' txt_len");
+    if (l0 < 0 || l1 > NUM_LAYERS || l0 > l1) return fail(ERR_ARG, "layer range out of [0, 32]");
+    if (l0 < l1 && (l0 < layer_lo_ || l1 > layer_hi_)) return fail(ERR_STATE, "layers outside the loaded weight range");
+    if (!vid_in || !txt_in || (do_final && !sr_out) || (!do_final && (!vid_lat || !txt_lat)))
+        return fail(ERR_ARG, "null buffer");
+    cudaSetDevice(dev_);
+    if (int rc = ensure_acts(Lv, TXT)) return rc;
+    cudaStream_t s = stream_;
+    launches_ = 0;
+    float temb[TEMB_IN];
+    sinusoidal256(t, temb);
+    cudaMemcpyAsync(temb_in_.p, temb, sizeof temb, cudaMemcpyHostToDevice, s);
+    if (do_init) {
+        cudaMemcpyAsync(VIDIN_F_.p, vid_in, (size_t)Lv * PATCH_IN * 4, cudaMemcpyHostToDevice, s);
+        cudaMemcpyAsync(TXTIN_F_.p, txt_in, (size_t)TXT * TXT_IN * 4, cudaMemcpyHostToDevice, s);
+        enqueue_init(Lv, TXT, s);
+    } else {
+        cudaMemcpyAsync(X_.p, vid_in, (size_t)Lv * DIM * 4, cudaMemcpyHostToDevice, s);
+        cudaMemcpyAsync(X_.as<float>() + (size_t)Lv * DIM, txt_in, (size_t)TXT * DIM * 4, cudaMemcpyHostToDevice, s);
+    }
+    enqueue_temb(s);
+    for (int i = l0; i < l1; i++) enqueue_layer(i, Lv, TXT, s);
+    if (do_final) {
+        enqueue_final(Lv, s);
+        cudaMemcpyAsync(sr_out, SR_.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToHost, s);
+    } else {
+        cudaMemcpyAsync(vid_lat, X_.p, (size_t)Lv * DIM * 4, cudaMemcpyDeviceToHost, s);
+        cudaMemcpyAsync(txt_lat, X_.as<float>() + (size_t)Lv * DIM, (size_t)TXT * DIM * 4, cudaMemcpyDeviceToHost, s);
+    }
+    last_launches_ = launches_;
+    if (int rc = cuda_check(cudaGetLastError(), "kernel launch")) return rc;
+    return cuda_check(cudaStreamSynchronize(s), "forward_latent");
+}
+
+int DitB200::capture_full(int Lv, int TXT) {
+    if (gexec_ && graph_Lv_ == Lv && graph_TXT_ == TXT) return OK;
+    if (gexec_) { cudaGraphExecDestroy(gexec_); gexec_ = nullptr; }
+    cudaGraph_t graph = nullptr;
+    launches_ = 0;
+    if (int rc = cuda_check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "begin capture")) return rc;
+    enqueue_init(Lv, TXT, stream_);
+    enqueue_temb(stream_);
+    for (int i = 0; i < NUM_LAYERS; i++) enqueue_layer(i, Lv, TXT, stream_);
+    enqueue_final(Lv, stream_);
+    cudaError_t ce = cudaStreamEndCapture(stream_, &graph);
+    if (int rc = cuda_check(ce, "end capture")) return rc;
+    ce = cudaGraphInstantiate(&gexec_, graph, 0);
+    cudaGraphDestroy(graph);
+    if (int rc = cuda_check(ce, "graph instantiate")) { gexec_ = nullptr; return rc; }
+    graph_Lv_ = Lv; graph_TXT_ = TXT; graph_launches_ = launches_;
+    return OK;
+}
+
+int DitB200::forward_dev(const float* d_vid, int Lv, const float* d_txt, int TXT, float t, float* d_sr,
+                         cudaStream_t user) {
+    if (!weights_) return fail(ERR_STATE, "weights not loaded");
+    if (layer_lo_ != 0 || layer_hi_ != NUM_LAYERS) return fail(ERR_STATE, "full forward needs all 32 layers loaded");
+    if (!geom_[0].ready || !geom_[1].ready) return fail(ERR_STATE, "windows not set");
+    if (Lv != geom_[0].view.Lv || TXT != geom_[0].view.TXT || TXT <= 0) return fail(ERR_ARG, "Lv/TXT do not match the windows");
+    if (!d_vid || !d_txt || !d_sr) return fail(ERR_ARG, "null buffer");
+    cudaSetDevice(dev_);
+    if (int rc = ensure_acts(Lv, TXT)) return rc;
+    if (int rc = capture_full(Lv, TXT)) return rc;
+    // Order the internal stream after the caller's work, run, then order the
+    // caller after us.
+    cudaEvent_t ev_in, ev_out;
+    cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
+    cudaEventRecord(ev_in, user);
+    cudaStreamWaitEvent(stream_, ev_in, 0);
+    float temb[TEMB_IN];
+    sinusoidal256(t, temb);
+    cudaMemcpyAsync(temb_in_.p, temb, sizeof temb, cudaMemcpyHostToDevice, stream_);
+    cudaMemcpyAsync(VIDIN_F_.p, d_vid, (size_t)Lv * PATCH_IN * 4, cudaMemcpyDeviceToDevice, stream_);
+    cudaMemcpyAsync(TXTIN_F_.p, d_txt, (size_t)TXT * TXT_IN * 4, cudaMemcpyDeviceToDevice, stream_);
+    cudaGraphLaunch(gexec_, stream_);
+    cudaMemcpyAsync(d_sr, SR_.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToDevice, stream_);
+    cudaEventRecord(ev_out, stream_);
+    cudaStreamWaitEvent(user, ev_out, 0);
+    cudaEventDestroy(ev_in);
+    cudaEventDestroy(ev_out);
+    last_launches_ = graph_launches_;
+    return cuda_check(cudaGetLastError(), "forward_dev");
+}
+
+int DitB200::forward(const float* vid_patch, int Lv, const float* txt, int TXT, float t, float* sr_out) {
+    if (!vid_patch || !txt || !sr_out) return fail(ERR_ARG, "null buffer");
+    if (!weights_) return fail(ERR_STATE, "weights not loaded");
+    if (layer_lo_ != 0 || layer_hi_ != NUM_LAYERS) return fail(ERR_STATE, "full forward needs all 32 layers loaded");
+    if (!geom_[0].ready || !geom_[1].ready) return fail(ERR_STATE, "windows not set");
+    if (Lv != geom_[0].view.Lv || TXT != geom_[0].view.TXT || TXT <= 0) return fail(ERR_ARG, "Lv/TXT do not match the windows");
+    cudaSetDevice(dev_);
+    if (int rc = ensure_acts(Lv, TXT)) return rc;
+    if (int rc = capture_full(Lv, TXT)) return rc;
+    // the graph reads its inputs from VIDIN_F_/TXTIN_F_/temb_in_ and leaves sr in SR_
+    float temb[TEMB_IN];
+    sinusoidal256(t, temb);
+    cudaMemcpyAsync(temb_in_.p, temb, sizeof temb, cudaMemcpyHostToDevice, stream_);
+    cudaMemcpyAsync(VIDIN_F_.p, vid_patch, (size_t)Lv * PATCH_IN * 4, cudaMemcpyHostToDevice, stream_);
+    cudaMemcpyAsync(TXTIN_F_.p, txt, (size_t)TXT * TXT_IN * 4, cudaMemcpyHostToDevice, stream_);
+    cudaGraphLaunch(gexec_, stream_);
+    cudaMemcpyAsync(sr_out, SR_.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToHost, stream_);
+    last_launches_ = graph_launches_;
+    return cuda_check(cudaStreamSynchronize(stream_), "forward");
+}
+
+int DitB200::time_embedding(float t, float* emb_host) {
+    if (!weights_) return fail(ERR_STATE, "weights not loaded");
+    cudaSetDevice(dev_);
+    float temb[TEMB_IN];
+    sinusoidal256(t, temb);
+    cudaMemcpyAsync(temb_in_.p, temb, sizeof temb, cudaMemcpyHostToDevice, stream_);
+    enqueue_temb(stream_);
+    cudaMemcpyAsync(emb_host, emb_.p, EMB_DIM * 4, cudaMemcpyDeviceToHost, stream_);
+    return cuda_check(cudaStreamSynchronize(stream_), "time_embedding");
+}
+
+int DitB200::ada_compose(const float* emb_host, float* out_host) {
+    if (!weights_) return fail(ERR_STATE, "weights not loaded");
+    cudaSetDevice(dev_);
+    cudaMemcpyAsync(emb_.p, emb_host, EMB_DIM * 4, cudaMemcpyHostToDevice, stream_);
+    s2b::ada_compose(emb_.as<float>(), branch_.as<float>(), NUM_LAYERS * 12 + 2, ada_.as<float>(), stream_);
+    cudaMemcpyAsync(out_host, ada_.p, (size_t)(NUM_LAYERS * 12 + 2) * DIM * 4, cudaMemcpyDeviceToHost, stream_);
+    return cuda_check(cudaStreamSynchronize(stream_), "ada_compose");
+}
+
+// ------------------------------------------------------------------ AWA operator
+int DitB200::awa_set_geometry(int win_type, const WinGeom& win) {
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    if (win_type != 0 && win_type != 1) return fail(ERR_ARG, "win_type must be 0 or 1");
+    cudaSetDevice(dev_);
+    return upload_geom(awa_geom_[win_type], win, -1);
+}
+
+int DitB200::awa_run(GeomDev& G, const float* vqkv, const float* tqkv, const float* nqv, const float* nkv,
+                     const float* nqt, const float* nkt, int Lv, int TXT, float eps, float* vid_out, float* txt_out,
+                     cudaStream_t user) {
+    if (!G.ready) return fail(ERR_STATE, "AWA geometry not set");
+    if (Lv != G.view.Lv || TXT != G.view.TXT || TXT <= 0) return fail(ERR_ARG, "Lv/TXT do not match the geometry");
+    if (G.view.nwin <= 0) return fail(ERR_ARG, "no windows");
+    const size_t ab = act_bytes(act_), sumS = (size_t)G.view.sumS;
+    DevBuf q, k, v, tw;
+    int rc;
+    if ((rc = cuda_check(q.ensure(sumS * DIM * ab), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(k.ensure(sumS * DIM * ab), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(v.ensure(sumS * DIM * ab), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(tw.ensure((size_t)G.view.nwin * TXT * DIM * 4), "cudaMalloc"))) return rc;
+    // tokens outside every window read 0 (reference awa_init.comp)
+    if (!G.tab.covers_all) cudaMemsetAsync(vid_out, 0, (size_t)Lv * DIM * 4, user);
+    awa_pack(vqkv, tqkv, ACT_F32, QKV, G.view, nqv, nkv, nqt, nkt, eps, q.p, k.p, v.p, act_, user);
+    awa_attend(q.p, k.p, v.p, act_, G.view, 1.0f / sqrtf((float)HEAD_D), vid_out, DIM, ACT_F32, tw.as<float>(), user,
+               nullptr);
+    awa_coalesce(tw.as<float>(), G.view.nwin, TXT, txt_out, DIM, ACT_F32, user);
+    if ((rc = cuda_check(cudaGetLastError(), "awa launch"))) return rc;
+    // the scratch buffers above must outlive the enqueued kernels
+    return cuda_check(cudaStreamSynchronize(user), "awa");
+}
+
+int DitB200::awa_forward_dev(int win_type, const float* vqkv, const float* tqkv, const float* nqv, const float* nkv,
+                             const float* nqt, const float* nkt, int Lv, int TXT, float eps, float* vid_out,
+                             float* txt_out, cudaStream_t user) {
+    if (win_type != 0 && win_type != 1) return fail(ERR_ARG, "win_type must be 0 or 1");
+    if (!vqkv || !tqkv || !nqv || !nkv || !nqt || !nkt || !vid_out || !txt_out) return fail(ERR_ARG, "null buffer");
+    cudaSetDevice(dev_);
+    return awa_run(awa_geom_[win_type], vqkv, tqkv, nqv, nkv, nqt, nkt, Lv, TXT, eps, vid_out, txt_out, user);
+}
+
+int DitB200::awa_forward(const float* vqkv, const float* tqkv, const WinGeom& win, const float* nqv, const float* nkv,
+                         const float* nqt, const float* nkt, int Lv, int TXT, float eps, float* vid_out,
+                         float* txt_out) {
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    if (!vqkv || !tqkv || !nqv || !nkv || !nqt || !nkt || !vid_out || !txt_out) return fail(ERR_ARG, "null buffer");
+    if (Lv != win.tokens()) return fail(ERR_ARG, "Lv does not match the window grid");
+    if (TXT != win.txt_len || TXT <= 0) return fail(ERR_ARG, "TXT does not match win.txt_len");
+    cudaSetDevice(dev_);
+    GeomDev g;
+    if (int rc = upload_geom(g, win, TXT)) return rc;
+    DevBuf dvq, dtq, dn, dvo, dto;
+    int rc;
+    if ((rc = cuda_check(dvq.ensure((size_t)Lv * QKV * 4), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(dtq.ensure((size_t)TXT * QKV * 4), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(dn.ensure(4 * HEAD_D * 4), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(dvo.ensure((size_t)Lv * DIM * 4), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(dto.ensure((size_t)TXT * DIM * 4), "cudaMalloc"))) return rc;
+    cudaMemcpyAsync(dvq.p, vqkv, (size_t)Lv * QKV * 4, cudaMemcpyHostToDevice, stream_);
+    cudaMemcpyAsync(dtq.p, tqkv, (size_t)TXT * QKV * 4, cudaMemcpyHostToDevice, stream_);
+    const float* norms[4] = {nqv, nkv, nqt, nkt};
+    for (int i = 0; i < 4; i++)
+        cudaMemcpyAsync(dn.as<float>() + i * HEAD_D, norms[i], HEAD_D * 4, cudaMemcpyHostToDevice, stream_);
+    rc = awa_run(g, dvq.as<float>(), dtq.as<float>(), dn.as<float>(), dn.as<float>() + HEAD_D,
+                 dn.as<float>() + 2 * HEAD_D, dn.as<float>() + 3 * HEAD_D, Lv, TXT, eps, dvo.as<float>(),
+                 dto.as<float>(), stream_);
+    if (rc) return rc;
+    cudaMemcpyAsync(vid_out, dvo.p, (size_t)Lv * DIM * 4, cudaMemcpyDeviceToHost, stream_);
+    cudaMemcpyAsync(txt_out, dto.p, (size_t)TXT * DIM * 4, cudaMemcpyDeviceToHost, stream_);
+    return cuda_check(cudaStreamSynchronize(stream_), "awa_forward");
+}
+
+}  // namespace s2b

@@ -1,0 +1,154 @@
+// dit_b200.h -- B200 NaDiT DiT host engine (the DitVk / AwaVk / AwaLayer /
+// AdaComposeLayer method set of the reference, src/dit_vk.h:24-204,
+// src/awa_vk.h:14-52, backed by sm_100a kernels with weights resident in HBM).
+#pragma once
+#include "s2b_common.h"
+#include "awa_geometry.h"
+#include "kernels.h"
+#include <cuda_runtime.h>
+#include <string>
+#include <vector>
+#include <memory>
+
+namespace s2b {
+
+// Owning device allocation (move-only).
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    DevBuf() {}
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    DevBuf(DevBuf&& o) noexcept : p(o.p), bytes(o.bytes) { o.p = nullptr; o.bytes = 0; }
+    DevBuf& operator=(DevBuf&& o) noexcept {
+        if (this != &o) { release(); p = o.p; bytes = o.bytes; o.p = nullptr; o.bytes = 0; }
+        return *this;
+    }
+    ~DevBuf() { release(); }
+    void release() { if (p) cudaFree(p); p = nullptr; bytes = 0; }
+    cudaError_t ensure(size_t n) {
+        if (n <= bytes) return cudaSuccess;
+        if (p) { cudaFree(p); p = nullptr; bytes = 0; }
+        cudaError_t e = cudaMalloc(&p, n);
+        if (e == cudaSuccess) bytes = n;
+        return e;
+    }
+    template <typename T> T* as() const { return (T*)p; }
+};
+
+// Device copy of one window geometry (see AwaDev in kernels.h).
+struct GeomDev {
+    WinGeom host;
+    WinTables tab;
+    DevBuf vidx, cumf, cums, row_win, vcos, vsin, tcos, tsin;
+    AwaDev view;
+    bool ready = false;
+};
+
+struct Linear {
+    DevBuf w;          // [out][ld] in `t`
+    DevBuf b;          // [out] fp32 or empty
+    ActT t = ACT_F32;
+    int out = 0, in = 0, ld = 0;
+    const float* bias() const { return b.bytes ? b.as<const float>() : nullptr; }
+};
+
+struct Block {
+    Linear qkv, out, mlp_hg, mlp_out;   // mlp_hg: proj_in | proj_in_gate interleaved in 128-row blocks
+    bool loaded = false;
+};
+
+class DitB200 {
+public:
+    DitB200() {}
+    ~DitB200();
+    int create(int device, int precision);
+    int load_weights(const char* m5_dir, bool synth, uint64_t seed, int layer_lo, int layer_hi);
+    int set_windows(const WinGeom& ns, const WinGeom& sh);
+
+    // DitVk::forward_latent (host buffers)
+    int forward_latent(const float* vid_in, int Lv, const float* txt_in, int TXT, float t, int l0, int l1,
+                       bool do_init, bool do_final, float* vid_lat, float* txt_lat, float* sr_out);
+    // DitVk::forward / forward_graph: all 32 layers, CUDA-graph replay.
+    int forward(const float* vid_patch, int Lv, const float* txt, int TXT, float t, float* sr_out);
+    int forward_dev(const float* d_vid_patch, int Lv, const float* d_txt, int TXT, float t, float* d_sr,
+                    cudaStream_t user);
+    int time_embedding(float t, float* emb_host);
+    int ada_compose(const float* emb_host, float* out_host);
+    // AwaVk::forward (host) / AwaLayer::forward (device, stored geometry)
+    int awa_forward(const float* vqkv, const float* tqkv, const WinGeom& win, const float* nqv, const float* nkv,
+                    const float* nqt, const float* nkt, int Lv, int TXT, float eps, float* vid_out, float* txt_out);
+    int awa_set_geometry(int win_type, const WinGeom& win);
+    int awa_forward_dev(int win_type, const float* vqkv, const float* tqkv, const float* nqv, const float* nkv,
+                        const float* nqt, const float* nkt, int Lv, int TXT, float eps, float* vid_out,
+                        float* txt_out, cudaStream_t user);
+
+    int precision() const { return prec_; }
+    uint64_t device_bytes() const;
+    int last_launches() const { return last_launches_; }
+    std::string err;
+
+    // Multi-GPU window sharding (dit_shard.cpp).
+    int shard_init(const uint8_t id[128], int world, int rank);
+    int shard_forward(const float* vid_patch, int Lv, const float* txt, int TXT, float t, float* sr_out);
+
+private:
+    int fail(int code, const std::string& m) { err = m; return code; }
+    int cuda_check(cudaError_t e, const char* what);
+    int upload_linear(Linear& L, const void* w_src, bool src_f16, const float* bias, int out, int in, ActT t,
+                      int ld, int interleave_role);
+    int ensure_acts(int Lv, int TXT);
+    int capture_full(int Lv, int TXT);
+    int awa_run(GeomDev& G, const float* vqkv, const float* tqkv, const float* nqv, const float* nkv,
+                const float* nqt, const float* nkt, int Lv, int TXT, float eps, float* vid_out, float* txt_out,
+                cudaStream_t user);
+    int upload_geom(GeomDev& g, const WinGeom& w, int TXT_expected);
+    void gemm(const void* A, int lda, const Linear& L, int M, const GemmEpi& e, cudaStream_t s);
+    // Enqueue the pieces of forward_latent on stream s (device inputs already staged).
+    int enqueue_init(int Lv, int TXT, cudaStream_t s);
+    int enqueue_temb(cudaStream_t s);
+    int enqueue_layer(int i, int Lv, int TXT, cudaStream_t s);
+    int enqueue_final(int Lv, cudaStream_t s);
+    const float* ada(int layer, int flow, int k) const {
+        return ada_.as<float>() + ((size_t)(layer * 12 + flow * 6 + k)) * DIM;
+    }
+    const float* normw(int layer, int flow, int which) const {
+        return qknorm_.as<float>() + ((size_t)((layer * 2 + flow) * 2 + which)) * HEAD_D;
+    }
+
+    int dev_ = -1, prec_ = PREC_FP32;
+    ActT act_ = ACT_F32;
+    cudaStream_t stream_ = nullptr;
+    bool weights_ = false;
+    int layer_lo_ = 0, layer_hi_ = 0;
+
+    Linear vid_in_, txt_in_, emb_in_, emb_hid_, emb_out_, vid_out_;
+    Block blk_[NUM_LAYERS][2];
+    DevBuf branch_;     // [32*12+2][2560] branch vectors in AdaCompose output order
+    DevBuf qknorm_;     // [32][2 flows][2 (q,k)][128]
+    DevBuf von_w_;      // [2560] final norm affine
+    DevBuf ada_;        // [32*12+2][2560] composed modulation vectors
+    DevBuf emb_;        // [15360]
+    DevBuf temb_in_, temb_h1_, temb_h2_;   // [256], [2560], [2560]
+
+    GeomDev geom_[2];   // non-shifted (even layers), shifted (odd layers)
+    GeomDev awa_geom_[2];
+
+    // activations
+    int cap_Lv_ = 0, cap_TXT_ = 0;
+    DevBuf X_, Xn_, QKV_, ATT_, Qp_, Kp_, Vp_, TOUTW_, HG_, Hs_, VPIN_, TIN_, SR_, VIDIN_F_, TXTIN_F_;
+    size_t qkv_pack_rows_ = 0;
+
+    // captured full forward
+    cudaGraphExec_t gexec_ = nullptr;
+    int graph_Lv_ = -1, graph_TXT_ = -1;
+    int graph_launches_ = 0;
+    int last_launches_ = 0;
+    int launches_ = 0;
+
+public:
+    struct ShardState;
+    std::unique_ptr<ShardState> shard_;
+};
+
+}  // namespace s2b

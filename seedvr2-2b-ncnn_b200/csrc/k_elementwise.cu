@@ -1,0 +1,176 @@
+// k_elementwise.cu -- HBM-bound row kernels: RMSNorm + adaLN modulate,
+// SwiGLU combine, SiLU, AdaCompose, conversions.
+//
+// Arithmetic follows the reference host loops operation by operation, with
+// explicit round-to-nearest intrinsics so the compiler does not fuse a
+// multiply and an add the reference keeps separate (it builds with
+// -ffp-contract=off, CMakeLists.txt:220-228):
+//   RMSNorm  r = 1/sqrtf(mean(x^2 in double) + eps); y = x*r*w   (src/dit_vk.cpp:48-52)
+//   modulate y*(emb[6d+ks]+scB) + (emb[6d+kh]+shB)               (src/dit_vk.cpp:532-545)
+//   SwiGLU   silu(g)*h                                            (src/dit_vk.cpp:465-471)
+#include "kernels.h"
+#include "kcommon.cuh"
+#include <cuda_fp16.h>
+
+namespace s2b {
+
+namespace {
+
+constexpr int NORM_THREADS = 320;   // 2560 / 320 = 8 elements per thread, 2 x float4
+
+template <typename TO>
+__global__ void __launch_bounds__(NORM_THREADS)
+k_rmsnorm_mod(const float* __restrict__ X, int ldx, int split, const float* __restrict__ sc0,
+              const float* __restrict__ sh0, const float* __restrict__ sc1, const float* __restrict__ sh1,
+              const float* __restrict__ affine, float eps, TO* __restrict__ Y, int ldy) {
+    constexpr int D = 2560;
+    const int r = blockIdx.x;
+    const float* x = X + (size_t)r * ldx;
+    const int c0 = threadIdx.x * 4, c1 = c0 + D / 2;
+    float a[4], b[4];
+    load4(x + c0, a);
+    load4(x + c1, b);
+    double s = 0;
+    #pragma unroll
+    for (int j = 0; j < 4; j++) s += (double)a[j] * a[j] + (double)b[j] * b[j];
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    __shared__ double part[NORM_THREADS / 32];
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+    __syncthreads();
+    double tot = 0;
+    #pragma unroll
+    for (int w = 0; w < NORM_THREADS / 32; w++) tot += part[w];
+    const float rr = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float)(tot / D), eps)));
+    const float* sc = (r < split) ? sc0 : sc1;
+    const float* sh = (r < split) ? sh0 : sh1;
+    float ya[4], yb[4];
+    #pragma unroll
+    for (int j = 0; j < 4; j++) {
+        float u = __fmul_rn(a[j], rr), v = __fmul_rn(b[j], rr);
+        if (affine) { u = __fmul_rn(u, affine[c0 + j]); v = __fmul_rn(v, affine[c1 + j]); }
+        if (sc) {
+            u = __fadd_rn(__fmul_rn(u, sc[c0 + j]), sh[c0 + j]);
+            v = __fadd_rn(__fmul_rn(v, sc[c1 + j]), sh[c1 + j]);
+        }
+        ya[j] = u; yb[j] = v;
+    }
+    store4(Y + (size_t)r * ldy + c0, ya);
+    store4(Y + (size_t)r * ldy + c1, yb);
+}
+
+template <typename TO>
+__global__ void k_swiglu(const float* __restrict__ HG, int M, int ldhg, TO* __restrict__ Hs, int ldh) {
+    // one thread per 4 outputs; HG column block b holds [h 128 | g 128]
+    const size_t per_row = 6912 / 4;
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)M * per_row) return;
+    const int r = (int)(i / per_row), c = (int)(i % per_row) * 4;
+    const int blk = c >> 7, j = c & 127;
+    float h[4], g[4], o[4];
+    load4(HG + (size_t)r * ldhg + blk * 256 + j, h);
+    load4(HG + (size_t)r * ldhg + blk * 256 + 128 + j, g);
+    #pragma unroll
+    for (int k = 0; k < 4; k++) o[k] = __fmul_rn(silu_f(g[k]), h[k]);
+    store4(Hs + (size_t)r * ldh + c, o);
+}
+
+__global__ void k_silu(float* x, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) x[i] = silu_f(x[i]);
+}
+
+// AdaCompose output order (src/ada_compose.cpp:16, :180-195): per layer and
+// flow [a_sc,a_sh,a_g,m_sc,m_sh,m_g] read emb slots {1,0,2,4,3,5}; the two
+// final vectors fin_sc, fin_sh read slots 1, 0.
+__global__ void k_ada_compose(const float* __restrict__ emb, const float* __restrict__ branch, int nvec,
+                              float* __restrict__ out) {
+    const int v = blockIdx.y, d = blockIdx.x * blockDim.x + threadIdx.x;
+    if (d >= 2560 || v >= nvec) return;
+    const int nlay = nvec - 2;
+    int k;
+    if (v < nlay) { const int kmap[6] = {1, 0, 2, 4, 3, 5}; k = kmap[v % 6]; }
+    else k = (v == nlay) ? 1 : 0;
+    out[(size_t)v * 2560 + d] = __fadd_rn(emb[d * 6 + k], branch[(size_t)v * 2560 + d]);
+}
+
+template <typename TO>
+__global__ void k_pad_convert(const float* __restrict__ src, int rows, int cols, TO* __restrict__ dst, int ld) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)rows * ld) return;
+    const int r = (int)(i / ld), c = (int)(i % ld);
+    dst[i] = Cvt<TO>::from_f(c < cols ? src[(size_t)r * cols + c] : 0.f);
+}
+
+template <typename TO>
+__global__ void k_ingest(const void* __restrict__ src, bool f16, int out, int in, TO* __restrict__ dst, int ld,
+                         int blk_rows, int blk_stride, int row_off) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)out * ld) return;
+    const int r = (int)(i / ld), c = (int)(i % ld);
+    float v = 0.f;
+    if (c < in) v = f16 ? __half2float(((const __half*)src)[(size_t)r * in + c]) : ((const float*)src)[(size_t)r * in + c];
+    const int dr = blk_rows > 0 ? (r / blk_rows) * blk_stride + row_off + r % blk_rows : r;
+    dst[(size_t)dr * ld + c] = Cvt<TO>::from_f(v);
+}
+
+template <typename TI>
+__global__ void k_to_f32(const TI* __restrict__ src, size_t n, float* __restrict__ dst) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = Cvt<TI>::to_f(src[i]);
+}
+
+}  // namespace
+
+void rmsnorm_mod(const float* X, int ldx, int rows, int split, const float* sc0, const float* sh0,
+                 const float* sc1, const float* sh1, const float* affine, float eps, void* Y, int ldy,
+                 ActT yt, cudaStream_t s) {
+    if (rows <= 0) return;
+    if (yt == ACT_F32)
+        k_rmsnorm_mod<float><<<rows, NORM_THREADS, 0, s>>>(X, ldx, split, sc0, sh0, sc1, sh1, affine, eps, (float*)Y, ldy);
+    else
+        k_rmsnorm_mod<bf16><<<rows, NORM_THREADS, 0, s>>>(X, ldx, split, sc0, sh0, sc1, sh1, affine, eps, (bf16*)Y, ldy);
+}
+
+void swiglu_rows(const float* HG, int M, int ldhg, void* Hs, int ldh, ActT ht, cudaStream_t s) {
+    if (M <= 0) return;
+    const size_t n = (size_t)M * (6912 / 4);
+    const int blocks = (int)((n + 255) / 256);
+    if (ht == ACT_F32) k_swiglu<float><<<blocks, 256, 0, s>>>(HG, M, ldhg, (float*)Hs, ldh);
+    else k_swiglu<bf16><<<blocks, 256, 0, s>>>(HG, M, ldhg, (bf16*)Hs, ldh);
+}
+
+void silu_inplace(float* x, int n, cudaStream_t s) { k_silu<<<(n + 255) / 256, 256, 0, s>>>(x, n); }
+
+void ada_compose(const float* emb, const float* branch, int nvec, float* out, cudaStream_t s) {
+    k_ada_compose<<<dim3(10, nvec), 256, 0, s>>>(emb, branch, nvec, out);
+}
+
+void pad_convert_rows(const float* src, int rows, int cols, void* dst, int ld_dst, ActT t, cudaStream_t s) {
+    const size_t n = (size_t)rows * ld_dst;
+    if (!n) return;
+    const int blocks = (int)((n + 255) / 256);
+    if (t == ACT_F32) k_pad_convert<float><<<blocks, 256, 0, s>>>(src, rows, cols, (float*)dst, ld_dst);
+    else k_pad_convert<bf16><<<blocks, 256, 0, s>>>(src, rows, cols, (bf16*)dst, ld_dst);
+}
+
+void convert_f32(const float* src, size_t n, void* dst, ActT t, cudaStream_t s) {
+    pad_convert_rows(src, 1, (int)n, dst, (int)n, t, s);
+}
+
+void convert_to_f32(const void* src, ActT t, size_t n, float* dst, cudaStream_t s) {
+    if (!n) return;
+    const int blocks = (int)((n + 255) / 256);
+    if (t == ACT_F32) cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToDevice, s);
+    else k_to_f32<bf16><<<blocks, 256, 0, s>>>((const bf16*)src, n, dst);
+}
+
+void ingest_weight(const void* src, bool src_f16, int out, int in, void* dst, ActT t, int ld, int blk_rows,
+                   int blk_stride, int row_off, cudaStream_t s) {
+    const size_t n = (size_t)out * ld;
+    const int blocks = (int)((n + 255) / 256);
+    if (t == ACT_F32) k_ingest<float><<<blocks, 256, 0, s>>>(src, src_f16, out, in, (float*)dst, ld, blk_rows, blk_stride, row_off);
+    else k_ingest<bf16><<<blocks, 256, 0, s>>>(src, src_f16, out, in, (bf16*)dst, ld, blk_rows, blk_stride, row_off);
+}
+
+}  // namespace s2b

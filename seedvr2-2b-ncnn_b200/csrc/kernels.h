@@ -1,0 +1,91 @@
+// kernels.h -- host-side launchers of the sm_100a kernels (no torch types).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+namespace s2b {
+
+enum ActT { ACT_F32 = 0, ACT_BF16 = 1 };
+inline size_t act_bytes(ActT t) { return t == ACT_F32 ? 4 : 2; }
+
+// ---------------------------------------------------------------- GEMM
+enum EpiMode {
+    EPI_STORE = 0,       // out[r,c] = acc + bias[c]
+    EPI_GATE_RESID = 1,  // resid[r,c] = (acc + bias[c]) * gate[c] + resid[r,c]
+    EPI_SWIGLU = 2,      // 256-wide column blocks [h 128 | g 128]: out[r, blk*128+j] = silu(g_j) * h_j
+};
+
+struct GemmEpi {
+    EpiMode mode = EPI_STORE;
+    const float* bias = nullptr;     // [N] or null
+    void* out = nullptr;             // STORE / SWIGLU output
+    int ldo = 0;
+    ActT out_t = ACT_F32;
+    float* resid = nullptr;          // GATE_RESID target (fp32 residual stream)
+    int ldr = 0;
+    const float* gate0 = nullptr;    // rows < gate_split (null: gate 1)
+    const float* gate1 = nullptr;    // rows >= gate_split (null: gate 1)
+    int gate_split = 0;
+};
+
+// C = A[M,K] (row stride lda) x W[N,K]^T (row stride ldw), fp32 accumulate,
+// fused epilogue.  SIMT kernel; any M, N, K.
+void gemm_simt(const void* A, ActT at, int lda, const void* W, ActT wt, int ldw, int M, int N, int K,
+               const GemmEpi& e, cudaStream_t s);
+
+// tcgen05 (5th-gen tensor core) BF16 GEMM, TMA-staged, TMEM accumulators.
+// Requirements: A, W bf16, K % 64 == 0 (the TMA maps zero-fill ragged M/N),
+// lda/ldw multiples of 8 elements, 16-byte aligned bases.
+bool gemm_tc_supported(int M, int N, int K, int lda, int ldw);
+int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K, const GemmEpi& e,
+            cudaStream_t s, int* launches);
+
+// ---------------------------------------------------------------- elementwise
+// Row RMSNorm (eps, optional affine weight) + adaLN modulate.  Rows < split
+// use (sc0, sh0), the rest (sc1, sh1); a null scale means "norm only".
+// Output y[r*ldy + d] in type yt.
+void rmsnorm_mod(const float* X, int ldx, int rows, int split, const float* sc0, const float* sh0,
+                 const float* sc1, const float* sh1, const float* affine, float eps, void* Y, int ldy,
+                 ActT yt, cudaStream_t s);
+// HG rows hold 54 column blocks [h 128 | g 128]; Hs[r, b*128+j] = silu(g) * h.
+void swiglu_rows(const float* HG, int M, int ldhg, void* Hs, int ldh, ActT ht, cudaStream_t s);
+// out[i] = silu(x[i]) (time embedding MLP)
+void silu_inplace(float* x, int n, cudaStream_t s);
+// out[v][d] = emb[d*6 + k(v)] + branch[v][d] for the 32*12+2 modulation vectors.
+void ada_compose(const float* emb, const float* branch, int nvec, float* out, cudaStream_t s);
+// dst[r*ld_dst + c] = src[r*cols + c] for c < cols, 0 for cols <= c < ld_dst.
+void pad_convert_rows(const float* src, int rows, int cols, void* dst, int ld_dst, ActT t, cudaStream_t s);
+void convert_f32(const float* src, size_t n, void* dst, ActT t, cudaStream_t s);
+void convert_to_f32(const void* src, ActT t, size_t n, float* dst, cudaStream_t s);
+// Weight ingest: src [out][in] (fp16 bits or fp32) -> dst rows of `ld` elements
+// in type t, zero-padded past `in`.  With blk_rows > 0, source row r lands on
+// destination row (r / blk_rows) * blk_stride + row_off + r % blk_rows.
+void ingest_weight(const void* src, bool src_f16, int out, int in, void* dst, ActT t, int ld, int blk_rows,
+                   int blk_stride, int row_off, cudaStream_t s);
+// Per-device one-time kernel attributes (dynamic shared memory opt-ins).
+int kernels_init_device();
+
+// ---------------------------------------------------------------- AWA
+struct AwaDev {
+    int nwin = 0, TXT = 0, sumf = 0, sumS = 0, maxS = 0, Lv = 0;
+    const int* vidx = nullptr;      // [sumf]
+    const int* cumf = nullptr;      // [nwin+1]
+    const int* cums = nullptr;      // [nwin+1]
+    const int* row_win = nullptr;   // [sumS] window of each packed row
+    const float* vcos = nullptr;    // [sumf][126]
+    const float* vsin = nullptr;
+    const float* tcos = nullptr;    // [nwin*TXT][126]
+    const float* tsin = nullptr;
+};
+// qk RMSNorm + RoPE + window packing: Qp/Kp/Vp [HEADS][sumS][128].
+void awa_pack(const void* vqkv, const void* tqkv, ActT in_t, int ldq, const AwaDev& g, const float* nqv,
+              const float* nkv, const float* nqt, const float* nkt, float eps, void* Qp, void* Kp, void* Vp,
+              ActT pt, cudaStream_t s);
+// Per-window SDPA.  vid rows scattered to att[vidx]; txt rows to toutw[wi][i].
+void awa_attend(const void* Qp, const void* Kp, const void* Vp, ActT pt, const AwaDev& g, float scale,
+                void* att, int ld_att, ActT at, float* toutw, cudaStream_t s, int* launches);
+// att_txt[i, d] = sum_w toutw[w][i][d] / nwin
+void awa_coalesce(const float* toutw, int nwin, int TXT, void* att_txt, int ld_att, ActT at, cudaStream_t s);
+
+}  // namespace s2b
