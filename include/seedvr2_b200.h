@@ -147,6 +147,14 @@ int s2b_time_embedding(s2b_ctx* ctx, float timestep, float* emb);
  * [layer][flow vid,txt][a_sc,a_sh,a_g,m_sc,m_sh,m_g], then fin_sc, fin_sh. */
 int s2b_ada_compose(s2b_ctx* ctx, const float* emb, float* out);
 
+/* ---- GEMM engine ----------------------------------------------------- */
+/* One Linear y = x W^T (+ bias) on the context's GEMM engine (the ncnn
+ * InnerProduct that DitVk::lin runs, src/dit_vk.cpp:270-293): bf16 contexts
+ * round x and W to bf16 and run the tcgen05 kernel (fp32 accumulate); fp32
+ * contexts run the fp32 kernel.  x (M,K), W (N,K), bias (N) or NULL, y (M,N),
+ * fp32 host buffers. */
+int s2b_linear(s2b_ctx* ctx, const float* x, int M, int K, const float* W, int N, const float* bias, float* y);
+
 /* ---- synthetic data (no checkpoint ships with this build) ------------- */
 /* Writes the m5 directory layout for layers [layer_lo, layer_hi) with
  * seeded random-init weights (Linear N(0,0.02) stored fp16; biases and

@@ -199,6 +199,11 @@ int s2b_ada_compose(s2b_ctx* ctx, const float* emb, float* out) {
     return ctx->dit.ada_compose(emb, out);
 }
 
+int s2b_linear(s2b_ctx* ctx, const float* x, int M, int K, const float* W, int N, const float* bias, float* y) {
+    if (!ctx) return S2B_ERR_ARG;
+    return ctx->dit.linear(x, M, K, W, N, bias, y);
+}
+
 int s2b_synth_write_m5(const char* dir, uint64_t seed, int lo, int hi) {
     if (!dir) return S2B_ERR_ARG;
     std::string err;

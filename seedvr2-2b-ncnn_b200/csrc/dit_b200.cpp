@@ -335,7 +335,9 @@ int DitB200::ensure_acts(int Lv, int TXT) {
     if ((rc = cuda_check(Kp_.ensure(std::max<size_t>(sumS, 1) * DIM * ab), "cudaMalloc(Kp)"))) return rc;
     if ((rc = cuda_check(Vp_.ensure(std::max<size_t>(sumS, 1) * DIM * ab), "cudaMalloc(Vp)"))) return rc;
     if ((rc = cuda_check(TOUTW_.ensure(std::max<size_t>(nwinTXT, 1) * DIM * 4), "cudaMalloc(TOUTW)"))) return rc;
-    if (act_ == ACT_F32 && (rc = cuda_check(HG_.ensure(M * 2 * MLP_DIM * 4), "cudaMalloc(HG)"))) return rc;
+    // [h | g] fp32 staging of the SIMT SwiGLU path (the tcgen05 path fuses it)
+    const bool need_hg = act_ == ACT_F32 || !gemm_tc_supported((int)M, 2 * MLP_DIM, DIM, DIM, DIM);
+    if (need_hg && (rc = cuda_check(HG_.ensure(M * 2 * MLP_DIM * 4), "cudaMalloc(HG)"))) return rc;
     if ((rc = cuda_check(Hs_.ensure(M * MLP_DIM * ab), "cudaMalloc(Hs)"))) return rc;
     if ((rc = cuda_check(VPIN_.ensure((size_t)Lv * PATCH_IN_PAD * ab), "cudaMalloc(VPIN)"))) return rc;
     if ((rc = cuda_check(TIN_.ensure((size_t)TXT * TXT_IN * ab), "cudaMalloc(TIN)"))) return rc;
@@ -605,6 +607,40 @@ int DitB200::time_embedding(float t, float* emb_host) {
     enqueue_temb(stream_);
     cudaMemcpyAsync(emb_host, emb_.p, EMB_DIM * 4, cudaMemcpyDeviceToHost, stream_);
     return cuda_check(cudaStreamSynchronize(stream_), "time_embedding");
+}
+
+int DitB200::linear(const float* x, int M, int K, const float* W, int N, const float* bias, float* y) {
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    if (!x || !W || !y || M <= 0 || K <= 0 || N <= 0) return fail(ERR_ARG, "bad linear arguments");
+    cudaSetDevice(dev_);
+    const int ld = (K + 7) / 8 * 8;   // row stride padded to 16 bytes for TMA
+    const size_t ab = act_bytes(act_);
+    DevBuf dx, dw, dxa, dwa, db, dy;
+    int rc;
+    if ((rc = cuda_check(dx.ensure((size_t)M * K * 4), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(dw.ensure((size_t)N * K * 4), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(dxa.ensure((size_t)M * ld * ab), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(dwa.ensure((size_t)N * ld * ab), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(dy.ensure((size_t)M * N * 4), "cudaMalloc"))) return rc;
+    cudaMemcpyAsync(dx.p, x, (size_t)M * K * 4, cudaMemcpyHostToDevice, stream_);
+    cudaMemcpyAsync(dw.p, W, (size_t)N * K * 4, cudaMemcpyHostToDevice, stream_);
+    if (bias) {
+        if ((rc = cuda_check(db.ensure((size_t)N * 4), "cudaMalloc"))) return rc;
+        cudaMemcpyAsync(db.p, bias, (size_t)N * 4, cudaMemcpyHostToDevice, stream_);
+    }
+    pad_convert_rows(dx.as<float>(), M, K, dxa.p, ld, act_, stream_);
+    pad_convert_rows(dw.as<float>(), N, K, dwa.p, ld, act_, stream_);
+    Linear L;
+    L.t = act_; L.out = N; L.in = K; L.ld = ld;
+    L.w = std::move(dwa);
+    L.b = std::move(db);
+    GemmEpi e; e.mode = EPI_STORE; e.bias = L.bias(); e.out = dy.p; e.ldo = N; e.out_t = ACT_F32;
+    gemm(dxa.p, ld, L, M, e, stream_);
+    cudaMemcpyAsync(y, dy.p, (size_t)M * N * 4, cudaMemcpyDeviceToHost, stream_);
+    if ((rc = cuda_check(cudaStreamSynchronize(stream_), "linear"))) return rc;
+    int had = 0;
+    if (act_ == ACT_BF16 && gemm_tc_error_reset(&had) == 0 && had) return fail(ERR_TIMEOUT, "tcgen05 GEMM wait expired");
+    return OK;
 }
 
 int DitB200::ada_compose(const float* emb_host, float* out_host) {

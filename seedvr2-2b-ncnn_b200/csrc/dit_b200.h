@@ -74,6 +74,8 @@ public:
     int forward_dev(const float* d_vid_patch, int Lv, const float* d_txt, int TXT, float t, float* d_sr,
                     cudaStream_t user);
     int time_embedding(float t, float* emb_host);
+    // One Linear on the context's GEMM engine (host buffers).
+    int linear(const float* x, int M, int K, const float* W, int N, const float* bias, float* y);
     int ada_compose(const float* emb_host, float* out_host);
     // AwaVk::forward (host) / AwaLayer::forward (device, stored geometry)
     int awa_forward(const float* vqkv, const float* tqkv, const WinGeom& win, const float* nqv, const float* nkv,

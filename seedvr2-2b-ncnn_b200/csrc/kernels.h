@@ -40,6 +40,9 @@ void gemm_simt(const void* A, ActT at, int lda, const void* W, ActT wt, int ldw,
 bool gemm_tc_supported(int M, int N, int K, int lda, int ldw);
 int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K, const GemmEpi& e,
             cudaStream_t s, int* launches);
+// Reads and clears the current device's tcgen05-kernel error flag (set when a
+// bounded wait expired).  Returns a cudaError_t value.
+int gemm_tc_error_reset(int* had_error);
 
 // ---------------------------------------------------------------- elementwise
 // Row RMSNorm (eps, optional affine weight) + adaLN modulate.  Rows < split

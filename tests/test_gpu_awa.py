@@ -1,0 +1,123 @@
+"""AWA operator on the B200 (s2b_awa_forward / s2b_awa_forward_dev) against
+the oracle.  Tolerances: fp32 path cos >= 0.99999 and max|d|/max|ref| <= 1e-4;
+bf16 path (bf16 Q/K/V, fp32 softmax and accumulation) cos >= 0.9995."""
+import os
+
+import numpy as np
+import pytest
+
+import cases
+import s2b
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+TOL = {s2b.PREC_FP32: (0.99999, 1e-4), s2b.PREC_BF16: (0.9995, 2e-2)}
+
+
+@pytest.fixture(scope="module", params=[s2b.PREC_FP32, s2b.PREC_BF16], ids=["fp32", "bf16"])
+def ctx(request):
+    c = s2b.DitB200(0, request.param)
+    yield c
+    c.close()
+
+
+def check(ctx, a, b):
+    cmin, rmax = TOL[ctx.precision]
+    cos, rel = cases.compare(a, b)
+    assert cos >= cmin and rel <= rmax, (cos, rel)
+
+
+def win_of(t, h, w, txt_len, slices, vf, tf):
+    return s2b.Win(t, h, w, txt_len, np.asarray(slices, np.int32), vf, tf)
+
+
+def test_awa_unit_case_vs_reference_golden(ctx):
+    c = cases.awa_unit_case()
+    g = np.load(os.path.join(GOLD, "awa_unit.npz"))
+    win = win_of(c["t"], c["h"], c["w"], c["txt_len"], c["slices"], c["vf"], c["tf"])
+    vo, to = ctx.awa_forward(c["vqkv"], c["tqkv"], win, c["nqv"], c["nkv"], c["nqt"], c["nkt"], 12, 4, 1e-5)
+    check(ctx, vo, g["vid_out"])
+    check(ctx, to, g["txt_out"])
+
+
+@pytest.mark.parametrize("split", ["reference", "literal3x3"])
+def test_awa_cfg1_vs_port(ctx, port, split):
+    Lv, TXT = 24 * 28, 58
+    vqkv, tqkv, nq = cases.awa_cfg_inputs(Lv, TXT)
+    if split == "reference":
+        sl, vf, tf = port.make_win(1, 24, 28, (4, 3, 3), TXT, False)
+    else:
+        sl = cases.literal_3x3(1, 24, 28)
+        vf, tf = cases.freqs_for(sl, TXT)
+    vo_r, to_r = port.awa(vqkv, tqkv, 1, 24, 28, TXT, sl, vf, tf, *nq, 1e-6)
+    vo, to = ctx.awa_forward(vqkv, tqkv, win_of(1, 24, 28, TXT, sl, vf, tf), *nq, Lv, TXT, 1e-6)
+    check(ctx, vo, vo_r)
+    check(ctx, to, to_r)
+
+
+def test_awa_shifted_ragged_windows(ctx, port):
+    # 5x97 grid: shifted windows of uneven sizes down to single columns
+    t, h, w, TXT = 1, 5, 97, 58
+    vqkv, tqkv, nq = cases.awa_cfg_inputs(t * h * w, TXT, seed=11)
+    sl, vf, tf = port.make_win(t, h, w, (4, 3, 3), TXT, True)
+    vo_r, to_r = port.awa(vqkv, tqkv, t, h, w, TXT, sl, vf, tf, *nq, 1e-5)
+    vo, to = ctx.awa_forward(vqkv, tqkv, win_of(t, h, w, TXT, sl, vf, tf), *nq, t * h * w, TXT, 1e-5)
+    check(ctx, vo, vo_r)
+    check(ctx, to, to_r)
+
+
+def test_awa_uncovered_tokens_are_zero(ctx, port):
+    # windows that cover part of the grid: the rest of vid_out must be 0
+    t, h, w, TXT = 1, 6, 10, 3
+    sl = np.array([[0, 1, 0, 3, 0, 4], [0, 1, 3, 6, 6, 10]], np.int32)
+    vf, tf = cases.freqs_for(sl, TXT)
+    vqkv, tqkv, nq = cases.awa_cfg_inputs(t * h * w, TXT, seed=3)
+    vo_r, to_r = port.awa(vqkv, tqkv, t, h, w, TXT, sl, vf, tf, *nq, 1e-5)
+    vo, to = ctx.awa_forward(vqkv, tqkv, win_of(t, h, w, TXT, sl, vf, tf), *nq, t * h * w, TXT, 1e-5)
+    covered = np.zeros((h, w), bool)
+    for s in sl:
+        covered[s[2]:s[3], s[4]:s[5]] = True
+    assert np.all(vo.reshape(h, w, -1)[~covered] == 0)
+    check(ctx, vo, vo_r)
+    check(ctx, to, to_r)
+
+
+def test_awa_single_txt_token_single_window(ctx, port):
+    t, h, w, TXT = 1, 3, 4, 1
+    sl = np.array([[0, 1, 0, 3, 0, 4]], np.int32)
+    vf, tf = cases.freqs_for(sl, TXT)
+    vqkv, tqkv, nq = cases.awa_cfg_inputs(12, TXT, seed=4)
+    vo_r, to_r = port.awa(vqkv, tqkv, t, h, w, TXT, sl, vf, tf, *nq, 1e-5)
+    vo, to = ctx.awa_forward(vqkv, tqkv, win_of(t, h, w, TXT, sl, vf, tf), *nq, 12, TXT, 1e-5)
+    check(ctx, vo, vo_r)
+    check(ctx, to, to_r)
+
+
+def test_awa_rejects_overlapping_windows_and_bad_sizes(ctx):
+    sl = np.array([[0, 1, 0, 2, 0, 3], [0, 1, 0, 2, 2, 4]], np.int32)
+    vf, tf = cases.freqs_for(sl, 4)
+    vqkv, tqkv, nq = cases.awa_cfg_inputs(8, 4)
+    with pytest.raises(s2b.S2BError):
+        ctx.awa_forward(vqkv, tqkv, win_of(1, 2, 4, 4, sl, vf, tf), *nq, 8, 4, 1e-5)
+    sl = np.array([[0, 1, 0, 2, 0, 4]], np.int32)
+    vf, tf = cases.freqs_for(sl, 4)
+    with pytest.raises(s2b.S2BError):   # TXT disagrees with the window's txt_len
+        ctx.awa_forward(vqkv, tqkv[:3], win_of(1, 2, 4, 4, sl, vf, tf), *nq, 8, 3, 1e-5)
+
+
+def test_awa_dev_matches_host(ctx):
+    import torch
+    Lv, TXT = 24 * 28, 58
+    vqkv, tqkv, nq = cases.awa_cfg_inputs(Lv, TXT, seed=9)
+    win = s2b.make_win(1, 24, 28, (4, 3, 3), TXT, True)
+    vo, to = ctx.awa_forward(vqkv, tqkv, win, *nq, Lv, TXT, 1e-5)
+    ctx.awa_set_geometry(1, win)
+    dev = torch.device("cuda:0")
+    tv, tt = torch.from_numpy(vqkv).to(dev), torch.from_numpy(tqkv).to(dev)
+    tn = [torch.from_numpy(x).to(dev) for x in nq]
+    ov, ot = torch.empty(Lv, 2560, device=dev), torch.empty(TXT, 2560, device=dev)
+    s = torch.cuda.current_stream()
+    ctx.awa_forward_dev(1, tv.data_ptr(), tt.data_ptr(), *[x.data_ptr() for x in tn], Lv, TXT, 1e-5,
+                        ov.data_ptr(), ot.data_ptr(), s.cuda_stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(ov.cpu().numpy(), vo) and np.array_equal(ot.cpu().numpy(), to)
