@@ -147,6 +147,17 @@ int s2b_time_embedding(s2b_ctx* ctx, float timestep, float* emb);
  * [layer][flow vid,txt][a_sc,a_sh,a_g,m_sc,m_sh,m_g], then fin_sc, fin_sh. */
 int s2b_ada_compose(s2b_ctx* ctx, const float* emb, float* out);
 
+/* ---- tracing ---------------------------------------------------------- */
+/* The reference accumulates a GEMM / AWA / host-loop time split per chunk
+ * (g_lin_time / g_awa_time, src/dit_vk.cpp:23-24, 688-697).  This runs the
+ * 32-layer forward_latent with CUDA events around every kernel on the launch
+ * stream and returns, per kernel class (0 tcgen05 GEMM, 1 fp32 GEMM,
+ * 2 attention, 3 qk-norm/RoPE pack, 4 norm/convert, 5 other), the summed
+ * device milliseconds, algorithmic FLOPs and bytes, and launch counts
+ * (arrays of 6). */
+int s2b_forward_profile(s2b_ctx* ctx, const float* vid_patch, int Lv, const float* txt, int TXT, float timestep,
+                        double* ms, double* flops, double* bytes, int* launches);
+
 /* ---- GEMM engine ----------------------------------------------------- */
 /* One Linear y = x W^T (+ bias) on the context's GEMM engine (the ncnn
  * InnerProduct that DitVk::lin runs, src/dit_vk.cpp:270-293): bf16 contexts

@@ -12,7 +12,8 @@
 //     load_model(const unsigned char*) decodes the ncnn weight blob
 //     [u32 tag][weights][fp32 bias], tag 0x01306B47 = fp16 weights,
 //     tag 0 = fp32 weights (the layout reference export/ncnn_io.py writes);
-//     extract() runs y = x W^T + b in fp32 (blocked, OpenMP) on a 2-D input.
+//     extract() runs y = x W^T + b in fp32 (packed panels, AVX2/FMA 6x16
+//     register micro-kernel, OpenMP) on a 2-D input.
 // What is a stub: everything Vulkan (devices, allocators, pipelines,
 // command buffers).  create_gpu_instance() reports failure, which is the
 // state DitVk::init(use_cpu=true) expects.
@@ -150,7 +151,7 @@ public:
 
     // InnerProduct parameters and decoded weights (row-major W[out][in]).
     int num_output = 0, bias_term = 0, weight_data_size = 0;
-    std::vector<float> weight_t;   // transposed: [in][out]
+    std::vector<float> weight;
     std::vector<float> bias;
 };
 

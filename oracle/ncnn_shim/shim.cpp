@@ -9,6 +9,7 @@
 #include <sstream>
 #include <string>
 #include <algorithm>
+#include <immintrin.h>
 
 #include "awa_vk.h"
 #include "dit_vk.h"
@@ -59,53 +60,69 @@ int Net::load_model(const unsigned char* mem) {
     const int out = num_output, in = weight_data_size / num_output;
     uint32_t tag; std::memcpy(&tag, mem, 4);
     const unsigned char* p = mem + 4;
-    std::vector<float> w((size_t)out * in);
+    weight.resize((size_t)out * in);
+    const long n = (long)weight.size();
     if (tag == 0x01306B47u) {
-        for (size_t i = 0; i < w.size(); i++) {
-            uint16_t hv; std::memcpy(&hv, p + 2 * i, 2); w[i] = half_to_float(hv);
-        }
-        p += 2 * w.size();
+        const uint16_t* h = reinterpret_cast<const uint16_t*>(p);
+        #pragma omp parallel for schedule(static)
+        for (long i = 0; i < n; i++) { uint16_t hv; std::memcpy(&hv, h + i, 2); weight[i] = half_to_float(hv); }
+        p += 2 * weight.size();
     } else if (tag == 0u) {
-        std::memcpy(w.data(), p, 4 * w.size());
-        p += 4 * w.size();
+        std::memcpy(weight.data(), p, 4 * weight.size());
+        p += 4 * weight.size();
     } else {
         fprintf(stderr, "[ncnn-shim] unsupported weight tag 0x%08x\n", tag);
         return -1;
     }
-    weight_t.assign((size_t)in * out, 0.f);
-    for (int o = 0; o < out; o++)
-        for (int i = 0; i < in; i++) weight_t[(size_t)i * out + o] = w[(size_t)o * in + i];
     if (bias_term) { bias.resize(out); std::memcpy(bias.data(), p, 4 * out); p += 4 * out; }
     return (int)(p - mem);
 }
 
 int Extractor::input(const char*, const Mat& in) { in_ = in; return 0; }
 
-// y[M,N] = x[M,K] * wt[K,N] + b : register-blocked 4x16, fp32 accumulate.
-static void sgemm(const float* x, int M, int K, const float* wt, int N, const float* b, float* y) {
-    const int MB = 4, NB = 16;
-    const int mt = (M + MB - 1) / MB, nt = N / NB;
-    #pragma omp parallel for schedule(dynamic, 4)
-    for (long t = 0; t < (long)mt * nt; t++) {
-        const int m0 = (int)(t / nt) * MB, n0 = (int)(t % nt) * NB;
-        const int mr = std::min(MB, M - m0);
-        float acc[MB][NB] = {};
-        for (int k = 0; k < K; k++) {
-            const float* w = wt + (size_t)k * N + n0;
-            for (int r = 0; r < MB; r++) {
-                const float xv = (r < mr) ? x[(size_t)(m0 + r) * K + k] : 0.f;
-                for (int j = 0; j < NB; j++) acc[r][j] += xv * w[j];
+// y[M,N] = x[M,K] W[N,K]^T + b, fp32.  Tasks = (128-column panel, 480-row
+// chunk); each task packs its W panel K-major once, then runs a 6x16 AVX2/FMA
+// register micro-kernel over its rows.
+static void sgemm(const float* x, int M, int K, const float* W, int N, const float* b, float* y) {
+    constexpr int NB = 128, MC = 480, MR = 6;
+    const int nbn = (N + NB - 1) / NB, nbm = (M + MC - 1) / MC;
+    #pragma omp parallel
+    {
+        std::vector<float> Bp((size_t)K * NB);
+        #pragma omp for schedule(dynamic, 1)
+        for (long t = 0; t < (long)nbn * nbm; t++) {
+            const int n0 = (int)(t % nbn) * NB, m0 = (int)(t / nbn) * MC;
+            const int nw = std::min(NB, N - n0), m1 = std::min(M, m0 + MC);
+            for (int j = 0; j < NB; j++) {
+                if (j < nw) { const float* wr = W + (size_t)(n0 + j) * K; for (int k = 0; k < K; k++) Bp[(size_t)k * NB + j] = wr[k]; }
+                else for (int k = 0; k < K; k++) Bp[(size_t)k * NB + j] = 0.f;
+            }
+            for (int r0 = m0; r0 < m1; r0 += MR) {
+                const int mr = std::min(MR, m1 - r0);
+                const float* xr[MR];
+                for (int r = 0; r < MR; r++) xr[r] = x + (size_t)(r0 + (r < mr ? r : 0)) * K;
+                for (int c0 = 0; c0 < nw; c0 += 16) {
+                    __m256 acc[MR][2];
+                    for (int r = 0; r < MR; r++) { acc[r][0] = _mm256_setzero_ps(); acc[r][1] = _mm256_setzero_ps(); }
+                    const float* bp = Bp.data() + c0;
+                    for (int k = 0; k < K; k++) {
+                        const __m256 b0 = _mm256_loadu_ps(bp + (size_t)k * NB), b1 = _mm256_loadu_ps(bp + (size_t)k * NB + 8);
+                        for (int r = 0; r < MR; r++) {
+                            const __m256 xv = _mm256_broadcast_ss(xr[r] + k);
+                            acc[r][0] = _mm256_fmadd_ps(xv, b0, acc[r][0]);
+                            acc[r][1] = _mm256_fmadd_ps(xv, b1, acc[r][1]);
+                        }
+                    }
+                    for (int r = 0; r < mr; r++) {
+                        float tmp[16];
+                        _mm256_storeu_ps(tmp, acc[r][0]); _mm256_storeu_ps(tmp + 8, acc[r][1]);
+                        for (int j = 0; j < 16 && c0 + j < nw; j++)
+                            y[(size_t)(r0 + r) * N + n0 + c0 + j] = tmp[j] + (b ? b[n0 + c0 + j] : 0.f);
+                    }
+                }
             }
         }
-        for (int r = 0; r < mr; r++)
-            for (int j = 0; j < NB; j++) y[(size_t)(m0 + r) * N + n0 + j] = acc[r][j] + (b ? b[n0 + j] : 0.f);
     }
-    for (int n = nt * NB; n < N; n++)  // ragged N tail
-        for (int m = 0; m < M; m++) {
-            float a = 0.f;
-            for (int k = 0; k < K; k++) a += x[(size_t)m * K + k] * wt[(size_t)k * N + n];
-            y[(size_t)m * N + n] = a + (b ? b[n] : 0.f);
-        }
 }
 
 int Extractor::extract(const char*, Mat& out) {
@@ -116,7 +133,7 @@ int Extractor::extract(const char*, Mat& out) {
     }
     const int M = in_.h;
     out.create(N, M, 4u);
-    sgemm((const float*)in_.data, M, K, net->weight_t.data(), N,
+    sgemm((const float*)in_.data, M, K, net->weight.data(), N,
           net->bias_term ? net->bias.data() : nullptr, (float*)out.data);
     return 0;
 }

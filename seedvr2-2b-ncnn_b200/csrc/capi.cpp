@@ -199,6 +199,12 @@ int s2b_ada_compose(s2b_ctx* ctx, const float* emb, float* out) {
     return ctx->dit.ada_compose(emb, out);
 }
 
+int s2b_forward_profile(s2b_ctx* ctx, const float* vid_patch, int Lv, const float* txt, int TXT, float t, double* ms,
+                        double* flops, double* bytes, int* launches) {
+    if (!ctx) return S2B_ERR_ARG;
+    return ctx->dit.forward_profile(vid_patch, Lv, txt, TXT, t, ms, flops, bytes, launches);
+}
+
 int s2b_linear(s2b_ctx* ctx, const float* x, int M, int K, const float* W, int N, const float* bias, float* y) {
     if (!ctx) return S2B_ERR_ARG;
     return ctx->dit.linear(x, M, K, W, N, bias, y);

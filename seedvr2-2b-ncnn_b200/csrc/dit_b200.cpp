@@ -26,6 +26,7 @@ namespace s2b {
 
 DitB200::~DitB200() {
     if (dev_ >= 0) cudaSetDevice(dev_);
+    for (cudaEvent_t e : ev_pool_) cudaEventDestroy(e);
     shard_.reset();
     if (gexec_) cudaGraphExecDestroy(gexec_);
     if (stream_) cudaStreamDestroy(stream_);
@@ -351,20 +352,27 @@ int DitB200::ensure_acts(int Lv, int TXT) {
 // ------------------------------------------------------------------ enqueue
 void DitB200::gemm(const void* A, int lda, const Linear& L, int M, const GemmEpi& e, cudaStream_t s) {
     if (M <= 0) return;
+    const double flops = 2.0 * M * L.out * L.in;
+    const double bytes = (double)M * L.in * act_bytes(act_) + (double)L.out * L.in * act_bytes(L.t) +
+                         (double)M * L.out * (e.mode == EPI_GATE_RESID ? 8 : e.mode == EPI_SWIGLU ? act_bytes(e.out_t) / 2.0 : act_bytes(e.out_t));
     if (act_ == ACT_BF16 && L.t == ACT_BF16 && gemm_tc_supported(M, L.out, L.in, lda, L.ld)) {
+        pbeg(KK_GEMM_TC, flops, bytes, s);
         gemm_tc(A, lda, L.w.p, L.ld, M, L.out, L.in, e, s, &launches_);
+        pend(s);
         return;
     }
+    pbeg(KK_GEMM_SIMT, flops, bytes, s);
     if (e.mode == EPI_SWIGLU) {
         // SIMT path: materialise [h | g] in fp32, then combine.
         GemmEpi st; st.mode = EPI_STORE; st.out = HG_.p; st.ldo = 2 * MLP_DIM; st.out_t = ACT_F32;
         gemm_simt(A, act_, lda, L.w.p, L.t, L.ld, M, L.out, L.in, st, s);
         swiglu_rows(HG_.as<float>(), M, 2 * MLP_DIM, e.out, e.ldo, e.out_t, s);
         launches_ += 2;
-        return;
+    } else {
+        gemm_simt(A, act_, lda, L.w.p, L.t, L.ld, M, L.out, L.in, e, s);
+        launches_++;
     }
-    gemm_simt(A, act_, lda, L.w.p, L.t, L.ld, M, L.out, L.in, e, s);
-    launches_++;
+    pend(s);
 }
 
 static void sinusoidal256(float t, float* e) {   // src/dit_vk.cpp:295-302
@@ -377,6 +385,7 @@ static void sinusoidal256(float t, float* e) {   // src/dit_vk.cpp:295-302
 
 int DitB200::enqueue_temb(cudaStream_t s) {
     // time embedding (src/dit_vk.cpp:303-309) in fp32, then AdaCompose.
+    pbeg(KK_OTHER, 2.0 * (TEMB_IN * DIM + DIM * DIM + (double)DIM * EMB_DIM), 4.0 * (TEMB_IN * DIM + DIM * DIM + (double)DIM * EMB_DIM), s);
     GemmEpi e; e.mode = EPI_STORE; e.out_t = ACT_F32;
     e.bias = emb_in_.bias(); e.out = temb_h1_.p; e.ldo = DIM;
     gemm_simt(temb_in_.p, ACT_F32, TEMB_IN, emb_in_.w.p, ACT_F32, emb_in_.ld, 1, DIM, TEMB_IN, e, s);
@@ -388,14 +397,17 @@ int DitB200::enqueue_temb(cudaStream_t s) {
     gemm_simt(temb_h2_.p, ACT_F32, DIM, emb_out_.w.p, ACT_F32, emb_out_.ld, 1, EMB_DIM, DIM, e, s);
     s2b::ada_compose(emb_.as<float>(), branch_.as<float>(), NUM_LAYERS * 12 + 2, ada_.as<float>(), s);
     launches_ += 6;
+    pend(s);
     return OK;
 }
 
 int DitB200::enqueue_init(int Lv, int TXT, cudaStream_t s) {
     // vid_in_proj (132 -> 2560) and txt_in (5120 -> 2560), src/dit_vk.cpp:494-497
+    pbeg(KK_NORM, 0, (double)Lv * PATCH_IN * 4 + (double)TXT * TXT_IN * 4 + ((double)Lv * PATCH_IN_PAD + (double)TXT * TXT_IN) * act_bytes(act_), s);
     pad_convert_rows(VIDIN_F_.as<float>(), Lv, PATCH_IN, VPIN_.p, PATCH_IN_PAD, act_, s);
     pad_convert_rows(TXTIN_F_.as<float>(), TXT, TXT_IN, TIN_.p, TXT_IN, act_, s);
     launches_ += 2;
+    pend(s);
     GemmEpi e; e.mode = EPI_STORE; e.out_t = ACT_F32; e.ldo = DIM;
     e.bias = vid_in_.bias(); e.out = X_.p;
     gemm(VPIN_.p, PATCH_IN_PAD, vid_in_, Lv, e, s);
@@ -417,10 +429,13 @@ int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s) {
     char* hs = (char*)Hs_.p;
     float* X = X_.as<float>();
 
+    const double norm_bytes = (double)DIM * (4 + ab);
     // 1. attention norm + modulate (txt unmodulated on the last layer, src/dit_vk.cpp:538)
+    pbeg(KK_NORM, 0, norm_bytes * M, s);
     rmsnorm_mod(X, DIM, M, Lv, ada(i, 0, 0), ada(i, 0, 1), last ? nullptr : ada(i, 1, 0), ada(i, 1, 1), nullptr,
                 NORM_EPS, Xn_.p, DIM, act_, s);
     launches_++;
+    pend(s);
     // 2. qkv projection (no bias)
     GemmEpi e; e.mode = EPI_STORE; e.out_t = act_; e.ldo = QKV;
     if (dual) {
@@ -430,13 +445,24 @@ int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s) {
         e.out = qkv; gemm(xn, DIM, BV.qkv, M, e, s);
     }
     // 3. AWA
+    double attn_flops = 0;
+    for (int w = 0; w < G.view.nwin; w++) {
+        const double S = G.tab.cums[w + 1] - G.tab.cums[w];
+        attn_flops += 4.0 * S * S * HEAD_D * HEADS;
+    }
+    pbeg(KK_PACK, 0, (double)G.view.sumS * QKV * ab * 2, s);
     awa_pack(qkv, qkv + (size_t)Lv * QKV * ab, act_, QKV, G.view, normw(i, 0, 0), normw(i, 0, 1), normw(i, 1, 0),
              normw(i, 1, 1), NORM_EPS, Qp_.p, Kp_.p, Vp_.p, act_, s);
     launches_++;
+    pend(s);
+    pbeg(KK_ATTN, attn_flops, (double)G.view.sumS * QKV * ab + (double)Lv * DIM * ab + (double)G.view.nwin * TXT * DIM * 4, s);
     awa_attend(Qp_.p, Kp_.p, Vp_.p, act_, G.view, 1.0f / sqrtf((float)HEAD_D), att, DIM, act_, TOUTW_.as<float>(), s,
                &launches_);
+    pend(s);
+    pbeg(KK_OTHER, 0, (double)G.view.nwin * TXT * DIM * 4 + (double)TXT * DIM * ab, s);
     awa_coalesce(TOUTW_.as<float>(), G.view.nwin, TXT, att + (size_t)Lv * DIM * ab, DIM, act_, s);
     launches_++;
+    pend(s);
     // 4. out projection (+bias), gate, residual (src/dit_vk.cpp:461-462, 558-575)
     GemmEpi g; g.mode = EPI_GATE_RESID; g.ldr = DIM;
     if (dual) {
@@ -451,9 +477,11 @@ int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s) {
     }
     // 5. MLP norm + modulate; txt skips the MLP on the last layer (src/dit_vk.cpp:579-620)
     const int Mm = last ? Lv : M;
+    pbeg(KK_NORM, 0, norm_bytes * Mm, s);
     rmsnorm_mod(X, DIM, Mm, Lv, ada(i, 0, 3), ada(i, 0, 4), ada(i, 1, 3), ada(i, 1, 4), nullptr, NORM_EPS, Xn_.p, DIM,
                 act_, s);
     launches_++;
+    pend(s);
     // 6. SwiGLU: proj_out(silu(proj_in_gate x) * proj_in x)
     GemmEpi sw; sw.mode = EPI_SWIGLU; sw.out_t = act_; sw.ldo = MLP_DIM;
     GemmEpi mo; mo.mode = EPI_GATE_RESID; mo.ldr = DIM;
@@ -478,11 +506,54 @@ int DitB200::enqueue_final(int Lv, cudaStream_t s) {
     // final RMSNorm (affine) + modulate (fin_sc, fin_sh) + vid_out_proj (src/dit_vk.cpp:657-675)
     const float* fin_sc = ada_.as<float>() + (size_t)(NUM_LAYERS * 12) * DIM;
     const float* fin_sh = fin_sc + DIM;
+    pbeg(KK_NORM, 0, (double)Lv * DIM * (4 + act_bytes(act_)), s);
     rmsnorm_mod(X_.as<float>(), DIM, Lv, Lv, fin_sc, fin_sh, nullptr, nullptr, von_w_.as<float>(), NORM_EPS, Xn_.p,
                 DIM, act_, s);
     launches_++;
+    pend(s);
     GemmEpi e; e.mode = EPI_STORE; e.out_t = ACT_F32; e.ldo = OUT_CH; e.bias = vid_out_.bias(); e.out = SR_.p;
     gemm(Xn_.p, DIM, vid_out_, Lv, e, s);
+    return OK;
+}
+
+// ------------------------------------------------------------------ profiling
+void DitB200::pbeg(int kind, double flops, double bytes, cudaStream_t s) {
+    if (!prof_on_) return;
+    while (ev_pool_.size() < 2 * (marks_.size() + 1)) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        ev_pool_.push_back(e);
+    }
+    ProfMark m;
+    m.kind = kind; m.flops = flops; m.bytes = bytes;
+    m.a = ev_pool_[2 * marks_.size()];
+    m.b = ev_pool_[2 * marks_.size() + 1];
+    cudaEventRecord(m.a, s);
+    marks_.push_back(m);
+}
+
+void DitB200::pend(cudaStream_t s) {
+    if (!prof_on_ || marks_.empty()) return;
+    cudaEventRecord(marks_.back().b, s);
+}
+
+int DitB200::forward_profile(const float* vid_patch, int Lv, const float* txt, int TXT, float t, double* ms,
+                             double* flops, double* bytes, int* count) {
+    if (!ms || !flops || !bytes || !count) return fail(ERR_ARG, "null profile arrays");
+    if (layer_lo_ != 0 || layer_hi_ != NUM_LAYERS) return fail(ERR_STATE, "profiling needs all 32 layers loaded");
+    std::vector<float> sr((size_t)std::max(Lv, 0) * OUT_CH);
+    marks_.clear();
+    prof_on_ = true;
+    const int rc = forward_latent(vid_patch, Lv, txt, TXT, t, 0, NUM_LAYERS, true, true, nullptr, nullptr, sr.data());
+    prof_on_ = false;
+    if (rc) return rc;
+    for (int k = 0; k < KK_COUNT; k++) { ms[k] = 0; flops[k] = 0; bytes[k] = 0; count[k] = 0; }
+    for (const auto& m : marks_) {
+        float e = 0;
+        cudaEventElapsedTime(&e, m.a, m.b);
+        ms[m.kind] += e; flops[m.kind] += m.flops; bytes[m.kind] += m.bytes; count[m.kind]++;
+    }
+    marks_.clear();
     return OK;
 }
 

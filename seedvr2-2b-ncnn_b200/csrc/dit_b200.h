@@ -58,6 +58,9 @@ struct Block {
     bool loaded = false;
 };
 
+// Kernel classes of the per-kernel profile (s2b_forward_profile).
+enum KernelKind { KK_GEMM_TC = 0, KK_GEMM_SIMT = 1, KK_ATTN = 2, KK_PACK = 3, KK_NORM = 4, KK_OTHER = 5, KK_COUNT = 6 };
+
 class DitB200 {
 public:
     DitB200() {}
@@ -74,6 +77,10 @@ public:
     int forward_dev(const float* d_vid_patch, int Lv, const float* d_txt, int TXT, float t, float* d_sr,
                     cudaStream_t user);
     int time_embedding(float t, float* emb_host);
+    // forward_latent(0, 32, init, final) with CUDA events around every kernel:
+    // per KernelKind the summed device ms, algorithmic FLOPs / bytes, launches.
+    int forward_profile(const float* vid_patch, int Lv, const float* txt, int TXT, float t, double* ms,
+                        double* flops, double* bytes, int* count);
     // One Linear on the context's GEMM engine (host buffers).
     int linear(const float* x, int M, int K, const float* W, int N, const float* bias, float* y);
     int ada_compose(const float* emb_host, float* out_host);
@@ -147,6 +154,14 @@ private:
     int graph_launches_ = 0;
     int last_launches_ = 0;
     int launches_ = 0;
+
+    // per-kernel CUDA-event profile
+    struct ProfMark { int kind; double flops, bytes; cudaEvent_t a, b; };
+    bool prof_on_ = false;
+    std::vector<ProfMark> marks_;
+    std::vector<cudaEvent_t> ev_pool_;
+    void pbeg(int kind, double flops, double bytes, cudaStream_t s);
+    void pend(cudaStream_t s);
 
 public:
     struct ShardState;

@@ -207,9 +207,17 @@ void awa_pack(const void* vqkv, const void* tqkv, ActT in_t, int ldq, const AwaD
                                                        nqt, nkt, eps, (float*)Qp, (float*)Kp, (float*)Vp);
 }
 
+int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, const AwaDev& g, float scale, void* att, int ld_att,
+                  ActT at, float* toutw, cudaStream_t s);
+
 void awa_attend(const void* Qp, const void* Kp, const void* Vp, ActT pt, const AwaDev& g, float scale,
                 void* att, int ld_att, ActT at, float* toutw, cudaStream_t s, int* launches) {
     if (g.nwin <= 0) return;
+    // bf16 operands: tensor-core kernel (k_awa_tc.cu); fp32: SIMT kernel below
+    if (pt == ACT_BF16 && awa_attend_tc(Qp, Kp, Vp, g, scale, att, ld_att, at, toutw, s) == 0) {
+        if (launches) (*launches)++;
+        return;
+    }
     dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
     const size_t smem = 2 * KT * 128 * sizeof(float);
     if (pt == ACT_F32 && at == ACT_F32)

@@ -224,7 +224,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, it++) {
             const int acc = it & 1;
             const uint32_t acc_phase = (it >> 1) & 1;
-            if (!wait_or_abort(&ctl->tfull[acc], acc_phase, abort_flag)) break;
+            // warp-uniform outcome: the tcgen05.ld below are warp-collective
+            if (!__all_sync(0xffffffffu, wait_or_abort(&ctl->tfull[acc], acc_phase, abort_flag))) break;
             sm100::tc_fence_after();
             const int mb = tile % p.num_m, nb = tile / p.num_m;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * ACC_COLS;
@@ -259,22 +260,23 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// bf16 [rows][K] with row stride ld elements; box = box_rows x 64, 128-B swizzle.
-bool make_tmap(CUtensorMap* m, const void* base, int rows, int K, int ld, int box_rows) {
+int g_num_sms[64];
+
+}  // namespace
+
+// bf16 [rows][cols] with row stride ld elements; box = box_rows x box_cols
+// (box_cols * 2 = 128 bytes: one 128-B swizzle row), 128-B swizzle, zero fill.
+bool make_tmap_bf16(CUtensorMap* m, const void* base, int rows, int cols, int ld, int box_rows, int box_cols) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
-
-int g_num_sms[64];
-
-}  // namespace
 
 bool gemm_tc_supported(int M, int N, int K, int lda, int ldw) {
     return M > 0 && N > 0 && K > 0 && N % 32 == 0 && lda % 8 == 0 && ldw % 8 == 0 && encode_fn() != nullptr;
@@ -286,7 +288,7 @@ int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K,
     if (((uintptr_t)A & 15) || ((uintptr_t)W & 15)) return -1;
     if (e.mode == EPI_SWIGLU && N % BN) return -1;
     CUtensorMap ta, tb;
-    if (!make_tmap(&ta, A, M, K, lda, BM) || !make_tmap(&tb, W, N, K, ldw, BN)) return -1;
+    if (!make_tmap_bf16(&ta, A, M, K, lda, BM, BK) || !make_tmap_bf16(&tb, W, N, K, ldw, BN, BK)) return -1;
     TcParams p;
     p.M = M; p.N = N;
     p.num_m = (M + BM - 1) / BM;
@@ -313,6 +315,7 @@ int gemm_tc_error_reset(int* had_error) {
 }
 
 int awa_init_device();
+int awa_tc_init_device();
 
 int kernels_init_device() {
     int dev = 0;
@@ -320,6 +323,7 @@ int kernels_init_device() {
     if (dev < 64) cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
     cudaError_t e = cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
+    if (int rc = awa_tc_init_device()) return rc;
     return awa_init_device();
 }
 

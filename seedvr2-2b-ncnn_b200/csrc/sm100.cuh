@@ -19,7 +19,7 @@ namespace sm100 {
 
 // Every spin-wait is bounded; on expiry the caller records an error and
 // unwinds instead of hanging the GPU.
-constexpr uint32_t WAIT_LIMIT = 1u << 26;
+constexpr uint32_t WAIT_LIMIT = 1u << 24;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

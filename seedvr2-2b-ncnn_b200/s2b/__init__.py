@@ -77,6 +77,9 @@ def lib() -> ctypes.CDLL:
         "s2b_awa_forward_dev": [vp, ip, vp, vp, vp, vp, vp, vp, ip, ip, ctypes.c_float, vp, vp, vp],
         "s2b_time_embedding": [vp, ctypes.c_float, _F32P],
         "s2b_ada_compose": [vp, _F32P, _F32P],
+        "s2b_linear": [vp, _F32P, ip, ip, _F32P, ip, _F32P, _F32P],
+        "s2b_forward_profile": [vp, _F32P, ip, _F32P, ip, ctypes.c_float, ctypes.POINTER(ctypes.c_double),
+                                ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), _I32P],
         "s2b_synth_write_m5": [ctypes.c_char_p, u64, ip, ip],
         "s2b_synth_vid_grid": [_F32P, ip, ip, ip, u64],
         "s2b_synth_txt": [_F32P, ip, u64],
@@ -290,6 +293,16 @@ class DitB200:
         out = np.zeros((NUM_LAYERS * 12 + 2, DIM), np.float32)
         self._c(lib().s2b_ada_compose(self._ctx, _p(e), _p(out)))
         return out
+
+    KERNEL_KINDS = ("gemm_tcgen05", "gemm_fp32", "attention", "awa_pack", "norm_convert", "other")
+
+    def forward_profile(self, vid_patch, Lv, txt, TXT, timestep=1000.0) -> dict:
+        """Per kernel class: device ms, algorithmic FLOPs / bytes, launches (CUDA events)."""
+        v, t = _f32(vid_patch), _f32(txt)
+        D6 = ctypes.c_double * 6
+        ms, fl, by, n = D6(), D6(), D6(), (ctypes.c_int * 6)()
+        self._c(lib().s2b_forward_profile(self._ctx, _p(v), Lv, _p(t), TXT, timestep, ms, fl, by, n))
+        return {k: dict(ms=ms[i], flops=fl[i], bytes=by[i], launches=n[i]) for i, k in enumerate(self.KERNEL_KINDS)}
 
     def last_launches(self) -> int:
         n = ctypes.c_int()

@@ -1,0 +1,51 @@
+"""GEMM engine (s2b_linear) against a plain PyTorch fp32 matmul.
+
+bf16 contexts run the tcgen05 kernel on bf16-rounded operands: compared with
+torch fp32 on the same rounded operands, only the fp32 accumulation order
+differs (max|d|/max|ref| <= 1e-3).  fp32 contexts: <= 1e-5."""
+import numpy as np
+import pytest
+
+import s2b
+
+pytestmark = pytest.mark.gpu
+SHAPES = [(128, 256, 64), (5498, 7680, 2560), (58, 2560, 2560), (300, 13824, 2560), (1000, 2560, 6912),
+          (77, 64, 2560), (640, 2560, 136), (200, 2560, 132), (1, 2560, 256), (129, 288, 72)]
+
+
+@pytest.fixture(scope="module", params=[s2b.PREC_FP32, s2b.PREC_BF16], ids=["fp32", "bf16"])
+def ctx(request):
+    c = s2b.DitB200(0, request.param)
+    yield c
+    c.close()
+
+
+def linear(ctx, x, W, b=None):
+    import ctypes
+    M, K = x.shape
+    N = W.shape[0]
+    y = np.zeros((M, N), np.float32)
+    F = ctypes.POINTER(ctypes.c_float)
+    L = s2b.lib()
+    L.s2b_linear.argtypes = [ctypes.c_void_p, F, ctypes.c_int, ctypes.c_int, F, ctypes.c_int, F, F]
+    rc = L.s2b_linear(ctx._ctx, x.ctypes.data_as(F), M, K, W.ctypes.data_as(F), N,
+                      None if b is None else b.ctypes.data_as(F), y.ctypes.data_as(F))
+    assert rc == 0, L.s2b_last_error(ctx._ctx)
+    return y
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_linear_vs_torch_fp32(ctx, M, N, K):
+    import torch
+    x = s2b.synth_normal((M, K), 1, f"x{M}{K}")
+    W = s2b.synth_normal((N, K), 2, f"w{N}{K}", 0.0, 0.02)
+    b = s2b.synth_normal((N,), 3, f"b{N}", 0.0, 0.02)
+    y = linear(ctx, x, W, b)
+    xt, wt = torch.from_numpy(x).cuda(), torch.from_numpy(W).cuda()
+    if ctx.precision == s2b.PREC_BF16:
+        xt, wt = xt.bfloat16().float(), wt.bfloat16().float()
+    with torch.no_grad():
+        torch.backends.cuda.matmul.allow_tf32 = False
+        ref = (xt @ wt.T + torch.from_numpy(b).cuda()).cpu().numpy()
+    rel = np.abs(y - ref).max() / np.abs(ref).max()
+    assert rel <= (1e-3 if ctx.precision == s2b.PREC_BF16 else 1e-5), rel
