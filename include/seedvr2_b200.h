@@ -138,6 +138,24 @@ int s2b_awa_forward_dev(s2b_ctx* ctx, int win_type, const float* d_vqkv, const f
                         const float* d_nq_v, const float* d_nk_v, const float* d_nq_t, const float* d_nk_t,
                         int Lv, int TXT, float eps, float* d_vid_out, float* d_txt_out, void* stream);
 
+/* No counterpart in the reference.  s2b_awa_forward_dev without any device
+ * allocation, for callers that cannot allocate device memory while they run
+ * (a host framework that owns all device memory and hands a plugin only its
+ * inputs and outputs, or a latency-critical loop where cudaMalloc/cudaFree
+ * would synchronise the device).  Its scratch (packed Q/K/V and the per-window
+ * txt partials) lives in one fixed 32 MiB device array inside the library
+ * that every device loading the library holds until exit; a geometry needing
+ * more (3 * sumS * 2560 * (4 fp32 | 2 bf16) + nwin * TXT * 2560 * 4 bytes,
+ * sumS = sum over windows of (f_i + TXT)) is rejected with S2B_ERR_ARG.  The
+ * geometry comes from s2b_awa_set_geometry, which does allocate: call it at
+ * set-up time.  The first call on a device also resolves the array's device
+ * address: make it before any stream capture.  Calls share the array, so
+ * calls whose GPU work overlaps race; serialise them.  Enqueues on `stream`
+ * and returns without waiting. */
+int s2b_awa_forward_dev_static(s2b_ctx* ctx, int win_type, const float* d_vqkv, const float* d_tqkv,
+                               const float* d_nq_v, const float* d_nk_v, const float* d_nq_t, const float* d_nk_t,
+                               int Lv, int TXT, float eps, float* d_vid_out, float* d_txt_out, void* stream);
+
 /* ---- adaLN ----------------------------------------------------------- */
 /* Replaces DitVk::time_embedding (src/dit_vk.cpp:295-309): emb[15360]. */
 int s2b_time_embedding(s2b_ctx* ctx, float timestep, float* emb);

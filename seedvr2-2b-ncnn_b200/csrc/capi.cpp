@@ -189,6 +189,14 @@ int s2b_awa_forward_dev(s2b_ctx* ctx, int win_type, const float* vqkv, const flo
                                     (cudaStream_t)stream);
 }
 
+int s2b_awa_forward_dev_static(s2b_ctx* ctx, int win_type, const float* vqkv, const float* tqkv, const float* nqv,
+                               const float* nkv, const float* nqt, const float* nkt, int Lv, int TXT, float eps,
+                               float* vid_out, float* txt_out, void* stream) {
+    if (!ctx) return S2B_ERR_ARG;
+    return ctx->dit.awa_forward_dev_static(win_type, vqkv, tqkv, nqv, nkv, nqt, nkt, Lv, TXT, eps, vid_out, txt_out,
+                                           (cudaStream_t)stream);
+}
+
 int s2b_time_embedding(s2b_ctx* ctx, float t, float* emb) {
     if (!ctx || !emb) return S2B_ERR_ARG;
     return ctx->dit.time_embedding(t, emb);

@@ -764,6 +764,35 @@ int DitB200::awa_forward_dev(int win_type, const float* vqkv, const float* tqkv,
     return awa_run(awa_geom_[win_type], vqkv, tqkv, nqv, nkv, nqt, nkt, Lv, TXT, eps, vid_out, txt_out, user);
 }
 
+size_t awa_static_bytes_needed(const AwaDev& g, ActT pt);
+size_t awa_static_capacity();
+int awa_forward_static(const float* vqkv, const float* tqkv, const AwaDev& g, const float* nqv, const float* nkv,
+                       const float* nqt, const float* nkt, float eps, float scale, ActT pt, float* vid_out,
+                       float* txt_out, cudaStream_t s);
+
+int DitB200::awa_forward_dev_static(int win_type, const float* vqkv, const float* tqkv, const float* nqv,
+                                    const float* nkv, const float* nqt, const float* nkt, int Lv, int TXT, float eps,
+                                    float* vid_out, float* txt_out, cudaStream_t user) {
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    if (win_type != 0 && win_type != 1) return fail(ERR_ARG, "win_type must be 0 or 1");
+    if (!vqkv || !tqkv || !nqv || !nkv || !nqt || !nkt || !vid_out || !txt_out) return fail(ERR_ARG, "null buffer");
+    const GeomDev& G = awa_geom_[win_type];
+    if (!G.ready) return fail(ERR_STATE, "AWA geometry not set (s2b_awa_set_geometry)");
+    if (Lv != G.view.Lv || TXT != G.view.TXT || TXT <= 0) return fail(ERR_ARG, "Lv/TXT do not match the geometry");
+    if (G.view.nwin <= 0) return fail(ERR_ARG, "no windows");
+    const size_t need = awa_static_bytes_needed(G.view, act_), cap = awa_static_capacity();
+    if (need > cap)
+        return fail(ERR_ARG, "geometry needs " + std::to_string(need) + " bytes of scratch; the static scratch holds " +
+                                 std::to_string(cap) + " bytes");
+    cudaSetDevice(dev_);
+    if (!G.tab.covers_all) cudaMemsetAsync(vid_out, 0, (size_t)Lv * DIM * 4, user);
+    const int rc = awa_forward_static(vqkv, tqkv, G.view, nqv, nkv, nqt, nkt, eps, 1.0f / sqrtf((float)HEAD_D), act_,
+                                      vid_out, txt_out, user);
+    if (rc == -1) return fail(ERR_ARG, "geometry does not fit the static scratch");
+    if (rc) return cuda_check((cudaError_t)rc, "static scratch address");
+    return cuda_check(cudaGetLastError(), "awa_forward_dev_static");
+}
+
 int DitB200::awa_forward(const float* vqkv, const float* tqkv, const WinGeom& win, const float* nqv, const float* nkv,
                          const float* nqt, const float* nkt, int Lv, int TXT, float eps, float* vid_out,
                          float* txt_out) {

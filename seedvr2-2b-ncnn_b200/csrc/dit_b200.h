@@ -92,6 +92,12 @@ public:
                         const float* nqt, const float* nkt, int Lv, int TXT, float eps, float* vid_out,
                         float* txt_out, cudaStream_t user);
 
+    // awa_forward_dev with its scratch in the library's fixed device array
+    // (k_awa_static.cu): no device allocation, enqueue only.
+    int awa_forward_dev_static(int win_type, const float* vqkv, const float* tqkv, const float* nqv,
+                               const float* nkv, const float* nqt, const float* nkt, int Lv, int TXT, float eps,
+                               float* vid_out, float* txt_out, cudaStream_t user);
+
     int precision() const { return prec_; }
     uint64_t device_bytes() const;
     int last_launches() const { return last_launches_; }
