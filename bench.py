@@ -307,8 +307,61 @@ def run_ours(args):
     return 0
 
 
+KERNEL_CASES = {
+    # one Linear of the 1080p forward (M = 5440 vid + 58 txt rows), bf16 tcgen05 GEMM
+    "gemm_qkv": (5498, 7680, 2560),
+    "gemm_out": (5498, 2560, 2560),
+    "gemm_mlp_in": (5498, 13824, 2560),
+    "gemm_mlp_out": (5498, 2560, 6912),
+}
+
+
+def run_kernel_case(case: str):
+    """Small single-kernel workloads for ncu captures (2 calls each)."""
+    import ctypes
+    import numpy as np
+    import s2b
+    c = s2b.DitB200(0, s2b.PREC_BF16)
+    if case in KERNEL_CASES:
+        M, N, K = KERNEL_CASES[case]
+        x = s2b.synth_normal((M, K), 1, "x")
+        W = s2b.synth_normal((N, K), 2, "w", 0.0, 0.02)
+        y = np.zeros((M, N), np.float32)
+        F = ctypes.POINTER(ctypes.c_float)
+        for _ in range(2):
+            rc = s2b.lib().s2b_linear(c._ctx, x.ctypes.data_as(F), M, K, W.ctypes.data_as(F), N, None,
+                                      y.ctypes.data_as(F))
+            assert rc == 0, s2b.lib().s2b_last_error(c._ctx)
+    elif case == "layer_1080p":
+        # one shared-weight MM-DiT block (layer 12) at 1080p from a random residual
+        T, H, W = GRID
+        Lv = T * H * W
+        c.init_synth(WEIGHT_SEED, 12, 13)
+        c.set_windows(s2b.make_win(T, H, W, (4, 3, 3), TXT, False), s2b.make_win(T, H, W, (4, 3, 3), TXT, True))
+        v = s2b.synth_normal((Lv, 2560), 1, "v")
+        t = s2b.synth_normal((TXT, 2560), 1, "t")
+        for _ in range(2):
+            c.forward_latent(v, Lv, t, TXT, TIMESTEP, 12, 13, False, False)
+    elif case == "attn_1080p":
+        T, H, W = GRID
+        Lv = T * H * W
+        win = s2b.make_win(T, H, W, (4, 3, 3), TXT, False)
+        vqkv = s2b.synth_normal((Lv, 7680), 1, "vqkv")
+        tqkv = s2b.synth_normal((TXT, 7680), 1, "tqkv")
+        nq = [s2b.synth_normal((128,), 1, n, 1.0, 0.02) for n in ("a", "b", "c", "d")]
+        for _ in range(2):
+            c.awa_forward(vqkv, tqkv, win, *nq, Lv, TXT, 1e-5)
+    else:
+        raise SystemExit(f"unknown kernel case {case}")
+    print("kernel case", case, "ok")
+    c.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel-case", choices=sorted(list(KERNEL_CASES) + ["attn_1080p", "layer_1080p"]),
+                    help="run one small single-kernel workload (for ncu captures) instead of the bench")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
@@ -317,6 +370,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the reference CPU baseline leg")
     args = ap.parse_args()
     args.warmup_ref = 0
+    if args.kernel_case:
+        return run_kernel_case(args.kernel_case)
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":

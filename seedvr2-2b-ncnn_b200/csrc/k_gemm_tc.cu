@@ -1,21 +1,32 @@
-// k_gemm_tc.cu -- persistent tcgen05 BF16 GEMM with the DiT's fused epilogues.
+// k_gemm_tc.cu -- persistent tcgen05 BF16 GEMMs with the DiT's fused epilogues.
 //
 // C[M,N] = A[M,K] B[N,K]^T, A/B bf16 K-major, fp32 accumulation in TMEM.
-// One CTA per SM loops over 128x256 output tiles (m fastest, so the CTAs in
-// flight share a few B column blocks and the A panel stays in L2):
-//   warp 0      TMA producer: A 128x64 and B 256x64 tiles, 128-byte swizzle,
-//               STAGES-deep ring guarded by full/empty mbarriers;
-//   warp 1      allocates 512 TMEM columns (two 256-column accumulators) and
-//               issues tcgen05.mma (M=128, N=256, K=16) from one thread,
-//               releasing smem stages and publishing accumulators with
-//               tcgen05.commit;
-//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns at a time, fused
-//               bias / adaLN gate + fp32 residual / SwiGLU, direct stores;
-//               the accumulator is handed back once read, so the next
-//               tile's MMAs overlap this tile's epilogue.
-// Loads are plain (non-multicast) TMA tile loads of this GPU's memory.
-// Every mbarrier wait is bounded; on expiry the kernel records an error in
-// g_tc_err, waits (bounded) for its own TMA loads, frees TMEM and returns.
+//
+// Pair kernel (M > 128, every vid Linear): clusters of two CTAs on two SMs
+// share one 256x256 output tile per step through tcgen05 cta_group::2.  Each
+// CTA stages only its own 128 A rows and 128 of the 256 B rows per 64-wide
+// k-block (32 KB), so per unit of MMA work an SM moves a third less data
+// through shared memory than with one CTA per 128x256 tile -- the 1-CTA
+// kernel is shared-memory-bandwidth bound (ncu: L1TEX ~80 % busy, tensor
+// pipe ~35 %).  Roles per CTA:
+//   warp 0      TMA producer: 6-stage ring of [A 128x64 | B 128x64] tiles
+//               (128-byte swizzle); both CTAs' loads complete on the even
+//               CTA's full barrier;
+//   warp 1      allocates 512 TMEM columns in both CTAs (two 256-column
+//               accumulators); in the even CTA one thread issues
+//               tcgen05.mma.cta_group::2 (M=256, N=256, K=16) and commits
+//               stage releases / accumulator hand-offs to the barriers of
+//               BOTH CTAs (one commit each, no multicast);
+//   warps 2-5   epilogue on this CTA's 128 accumulator rows: tcgen05.ld 32
+//               lanes x 32 columns, fused bias / adaLN gate + fp32 residual /
+//               SwiGLU, direct stores; then release the accumulator to the
+//               even CTA's MMA thread.
+// Single kernel (M <= 128: the 58-row txt Linears of layers 0..9): one CTA
+// per 128x256 tile, 4-stage ring, same roles within one CTA.
+// All loads are plain TMA tile loads of this GPU's memory (no cluster
+// multicast).  Every mbarrier wait is bounded; on expiry a kernel records
+// g_tc_err, drains its own TMA loads (bounded), frees TMEM and returns.
+// Warp-collective TMEM instructions run only under warp-uniform control flow.
 #include "kernels.h"
 #include "kcommon.cuh"
 #include "sm100.cuh"
@@ -25,12 +36,20 @@
 namespace s2b {
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int NUM_THREADS = 192;
+constexpr int BK = 64, NUM_THREADS = 192;
 constexpr int ACC_COLS = 256, NUM_ACC = 2, TMEM_COLS = ACC_COLS * NUM_ACC;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-constexpr uint32_t IDESC = sm100::idesc_bf16_f32(BM, BN);
+
+// single-CTA kernel
+constexpr int BM1 = 128, BN1 = 256, STAGES1 = 4;
+constexpr int A1_BYTES = BM1 * BK * 2, B1_BYTES = BN1 * BK * 2, STAGE1_BYTES = A1_BYTES + B1_BYTES;
+constexpr int SMEM1_BYTES = STAGES1 * STAGE1_BYTES + 1024 + 256;
+constexpr uint32_t IDESC1 = sm100::idesc_bf16_f32(BM1, BN1);
+
+// CTA-pair kernel: per CTA 128 rows of A and 128 rows of B per stage
+constexpr int BM2 = 256, BN2 = 256, STAGES2 = 6;
+constexpr int A2_BYTES = 128 * BK * 2, B2_BYTES = 128 * BK * 2, STAGE2_BYTES = A2_BYTES + B2_BYTES;
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
+constexpr uint32_t IDESC2 = sm100::idesc_bf16_f32(BM2, BN2);
 
 __device__ int g_tc_err;
 
@@ -39,6 +58,7 @@ struct TcParams {
     GemmEpi e;
 };
 
+template <int STAGES>
 struct Ctl {
     uint64_t full[STAGES], empty[STAGES], tfull[NUM_ACC], tempty[NUM_ACC];
     uint32_t tmem_slot;
@@ -71,7 +91,20 @@ __device__ __forceinline__ void store32(bf16* dst, const float v[32]) {
     }
 }
 
-__device__ __forceinline__ void epilogue_tile(const TcParams& p, uint32_t taddr, int row, int n0) {
+// Pull this thread's residual row segment of a tile into L2 ahead of its
+// epilogue (8 x 128-B lines of fp32).
+__device__ __forceinline__ void prefetch_resid(const TcParams& p, int row, int n0) {
+    if (p.e.mode != EPI_GATE_RESID || row >= p.M) return;
+    const float* base = p.e.resid + (size_t)row * p.e.ldr + n0;
+    #pragma unroll
+    for (int j = 0; j < 8; j++)
+        if (n0 + 32 * j < p.N) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + 32 * j));
+}
+
+// Epilogue of one accumulator row (thread = TMEM lane = output row) over the
+// tile's 256 columns starting at n0.  The tcgen05.ld are warp-collective and
+// executed by every lane; only the stores depend on the row.
+__device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, int row, int n0) {
     const GemmEpi& e = p.e;
     const bool row_ok = row < p.M;
     if (e.mode == EPI_SWIGLU) {
@@ -91,8 +124,51 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, uint32_t taddr,
         return;
     }
     const float* gate = (row < e.gate_split) ? e.gate0 : e.gate1;
+    if (e.mode == EPI_GATE_RESID) {
+        // residual read-modify-write: the chunk's 8 residual loads are issued
+        // together, before the TMEM load, so their latency overlaps it and the
+        // loads never queue behind the previous chunk's stores.
+        float* __restrict__ rrow = e.resid + (size_t)row * e.ldr;
+        #pragma unroll 1
+        for (int c0 = 0; c0 < 256; c0 += 32) {
+            if (n0 + c0 >= p.N) break;         // warp-uniform
+            const int col = n0 + c0;
+            const bool full = col + 32 <= p.N;
+            float4 r[8];
+            if (row_ok && full) {
+                #pragma unroll
+                for (int j = 0; j < 8; j++) r[j] = __ldcg(reinterpret_cast<const float4*>(rrow + col) + j);
+            }
+            float v[32];
+            sm100::tmem_ld32(taddr + c0, v);
+            if (!row_ok) continue;
+            if (full) {
+                #pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f), g4 = make_float4(1.f, 1.f, 1.f, 1.f);
+                    if (e.bias) b4 = __ldg(reinterpret_cast<const float4*>(e.bias + col) + j);
+                    if (gate) g4 = __ldg(reinterpret_cast<const float4*>(gate + col) + j);
+                    float t0 = __fadd_rn(v[4 * j], b4.x), t1 = __fadd_rn(v[4 * j + 1], b4.y);
+                    float t2 = __fadd_rn(v[4 * j + 2], b4.z), t3 = __fadd_rn(v[4 * j + 3], b4.w);
+                    if (gate) { t0 = __fmul_rn(t0, g4.x); t1 = __fmul_rn(t1, g4.y); t2 = __fmul_rn(t2, g4.z); t3 = __fmul_rn(t3, g4.w); }
+                    r[j].x = __fadd_rn(t0, r[j].x); r[j].y = __fadd_rn(t1, r[j].y);
+                    r[j].z = __fadd_rn(t2, r[j].z); r[j].w = __fadd_rn(t3, r[j].w);
+                }
+                #pragma unroll
+                for (int j = 0; j < 8; j++) __stcg(reinterpret_cast<float4*>(rrow + col) + j, r[j]);
+            } else {
+                for (int j = 0; j < 32 && col + j < p.N; j++) {
+                    float t = v[j];
+                    if (e.bias) t = __fadd_rn(t, e.bias[col + j]);
+                    if (gate) t = __fmul_rn(t, gate[col + j]);
+                    rrow[col + j] = __fadd_rn(t, rrow[col + j]);
+                }
+            }
+        }
+        return;
+    }
     #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
+    for (int c0 = 0; c0 < 256; c0 += 32) {
         if (n0 + c0 >= p.N) break;             // warp-uniform
         float v[32];
         sm100::tmem_ld32(taddr + c0, v);
@@ -138,19 +214,20 @@ __device__ __forceinline__ void epilogue_tile(const TcParams& p, uint32_t taddr,
     }
 }
 
+// ------------------------------------------------------------ single CTA
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
-    uint8_t* sB = smem + STAGES * A_BYTES;
-    Ctl* ctl = reinterpret_cast<Ctl*>(smem + STAGES * STAGE_BYTES);
+    uint8_t* sB = smem + STAGES1 * A1_BYTES;
+    Ctl<STAGES1>* ctl = reinterpret_cast<Ctl<STAGES1>*>(smem + STAGES1 * STAGE1_BYTES);
     volatile int* abort_flag = &ctl->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_tiles = p.num_m * p.num_n;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; s++) { sm100::mbar_init(&ctl->full[s], 1); sm100::mbar_init(&ctl->empty[s], 1); }
+        for (int s = 0; s < STAGES1; s++) { sm100::mbar_init(&ctl->full[s], 1); sm100::mbar_init(&ctl->empty[s], 1); }
         for (int a = 0; a < NUM_ACC; a++) { sm100::mbar_init(&ctl->tfull[a], 1); sm100::mbar_init(&ctl->tempty[a], 4); }
         ctl->abort = 0;
         sm100::fence_barrier_init();
@@ -175,19 +252,18 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
                 const int mb = tile % p.num_m, nb = tile / p.num_m;
                 for (int kb = 0; kb < p.num_kb; kb++) {
                     if (!wait_or_abort(&ctl->empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
-                    sm100::mbar_arrive_expect_tx(&ctl->full[stage], STAGE_BYTES);
-                    sm100::tma_load_2d(sA + stage * A_BYTES, &tA, &ctl->full[stage], kb * BK, mb * BM);
-                    sm100::tma_load_2d(sB + stage * B_BYTES, &tB, &ctl->full[stage], kb * BK, nb * BN);
+                    sm100::mbar_arrive_expect_tx(&ctl->full[stage], STAGE1_BYTES);
+                    sm100::tma_load_2d(sA + stage * A1_BYTES, &tA, &ctl->full[stage], kb * BK, mb * BM1);
+                    sm100::tma_load_2d(sB + stage * B1_BYTES, &tB, &ctl->full[stage], kb * BK, nb * BN1);
                     issued++;
-                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                    if (++stage == STAGES1) { stage = 0; phase ^= 1; }
                 }
             }
             if (!ok) {
-                // drain our own loads still in flight (bounded) before smem goes away
-                const long n = issued < STAGES ? issued : STAGES;
+                const long n = issued < STAGES1 ? issued : STAGES1;
                 for (long i = 1; i <= n; i++) {
                     const long k = issued - i;
-                    const uint32_t s = (uint32_t)(k % STAGES), ph = (uint32_t)((k / STAGES) & 1);
+                    const uint32_t s = (uint32_t)(k % STAGES1), ph = (uint32_t)((k / STAGES1) & 1);
                     for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->full[s], ph); w++) {}
                 }
             }
@@ -206,14 +282,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
                 for (int kb = 0; kb < p.num_kb; kb++) {
                     if (!wait_or_abort(&ctl->full[stage], phase, abort_flag)) { ok = false; break; }
                     sm100::tc_fence_after();
-                    const uint8_t* a = sA + stage * A_BYTES;
-                    const uint8_t* b = sB + stage * B_BYTES;
+                    const uint8_t* a = sA + stage * A1_BYTES;
+                    const uint8_t* b = sB + stage * B1_BYTES;
                     #pragma unroll
                     for (int kk = 0; kk < BK / 16; kk++)
                         sm100::mma_bf16(d, sm100::desc_kmajor_sw128(a, kk * 32), sm100::desc_kmajor_sw128(b, kk * 32),
-                                        IDESC, (kb | kk) != 0);
+                                        IDESC1, (kb | kk) != 0);
                     sm100::mma_commit(&ctl->empty[stage]);
-                    if (++stage == STAGES) { stage = 0; phase ^= 1; }
+                    if (++stage == STAGES1) { stage = 0; phase ^= 1; }
                 }
                 if (ok) sm100::mma_commit(&ctl->tfull[acc]);
             }
@@ -229,7 +305,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
             sm100::tc_fence_after();
             const int mb = tile % p.num_m, nb = tile / p.num_m;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * ACC_COLS;
-            epilogue_tile(p, taddr, mb * BM + q * 32 + lane, nb * BN);
+            const int nt = tile + gridDim.x;
+            if (nt < num_tiles) prefetch_resid(p, (nt % p.num_m) * BM1 + q * 32 + lane, (nt / p.num_m) * BN1);
+            epilogue_row(p, taddr, mb * BM1 + q * 32 + lane, nb * BN1);
             sm100::tc_fence_before();
             __syncwarp();
             if (lane == 0) sm100::mbar_arrive(&ctl->tempty[acc]);
@@ -239,6 +317,124 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
     if (warp == 1) {
         sm100::tc_fence_after();
         sm100::tmem_dealloc(tmem_base, TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------ CTA pair
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+k_gemm_tc_pair(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB, const TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES2 * A2_BYTES;
+    Ctl<STAGES2>* ctl = reinterpret_cast<Ctl<STAGES2>*>(smem + STAGES2 * STAGE2_BYTES);
+    volatile int* abort_flag = &ctl->abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = sm100::cluster_ctarank();        // 0: issues the MMAs
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int num_tiles = p.num_m * p.num_n;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES2; s++) { sm100::mbar_init(&ctl->full[s], 1); sm100::mbar_init(&ctl->empty[s], 1); }
+        for (int a = 0; a < NUM_ACC; a++) { sm100::mbar_init(&ctl->tfull[a], 1); sm100::mbar_init(&ctl->tempty[a], 8); }
+        ctl->abort = 0;
+        sm100::fence_barrier_init();
+        sm100::tma_prefetch_desc(&tA);
+        sm100::tma_prefetch_desc(&tB);
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc_pair(&ctl->tmem_slot, TMEM_COLS);
+        sm100::tmem_relinquish_pair();
+    }
+    sm100::tc_fence_before();
+    sm100::cluster_sync();                 // both CTAs' barriers initialised before any remote use
+    sm100::tc_fence_after();
+    const uint32_t tmem_base = ctl->tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0;
+            long issued = 0;
+            bool ok = true;
+            for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+                const int mb = tile % p.num_m, nb = tile / p.num_m;
+                for (int kb = 0; kb < p.num_kb; kb++) {
+                    if (!wait_or_abort(&ctl->empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+                    // both CTAs' bytes complete on the even CTA's full barrier
+                    if (rank == 0) sm100::mbar_arrive_expect_tx(&ctl->full[stage], 2 * STAGE2_BYTES);
+                    const uint32_t fb = sm100::map_to_rank(&ctl->full[stage], 0);
+                    sm100::tma_load_2d_pair(sA + stage * A2_BYTES, &tA, fb, kb * BK, mb * BM2 + (int)rank * 128);
+                    sm100::tma_load_2d_pair(sB + stage * B2_BYTES, &tB, fb, kb * BK, nb * BN2 + (int)rank * 128);
+                    issued++;
+                    if (++stage == STAGES2) { stage = 0; phase ^= 1; }
+                }
+            }
+            if (!ok && rank == 0) {
+                // drain this CTA pair's loads (bounded) before shared memory goes away
+                const long n = issued < STAGES2 ? issued : STAGES2;
+                for (long i = 1; i <= n; i++) {
+                    const long k = issued - i;
+                    const uint32_t s = (uint32_t)(k % STAGES2), ph = (uint32_t)((k / STAGES2) & 1);
+                    for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->full[s], ph); w++) {}
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            uint32_t stage = 0, phase = 0;
+            int it = 0;
+            bool ok = true;
+            for (int tile = pair; tile < num_tiles && ok; tile += npairs, it++) {
+                const int acc = it & 1;
+                const uint32_t acc_phase = (it >> 1) & 1;
+                if (!wait_or_abort(&ctl->tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
+                sm100::tc_fence_after();
+                const uint32_t d = tmem_base + acc * ACC_COLS;
+                for (int kb = 0; kb < p.num_kb; kb++) {
+                    if (!wait_or_abort(&ctl->full[stage], phase, abort_flag)) { ok = false; break; }
+                    sm100::tc_fence_after();
+                    const uint8_t* a = sA + stage * A2_BYTES;
+                    const uint8_t* b = sB + stage * B2_BYTES;
+                    #pragma unroll
+                    for (int kk = 0; kk < BK / 16; kk++)
+                        sm100::mma_bf16_pair(d, sm100::desc_kmajor_sw128(a, kk * 32),
+                                             sm100::desc_kmajor_sw128(b, kk * 32), IDESC2, (kb | kk) != 0);
+                    // release this stage in both CTAs
+                    sm100::mma_commit_pair(sm100::map_to_rank(&ctl->empty[stage], 0));
+                    sm100::mma_commit_pair(sm100::map_to_rank(&ctl->empty[stage], 1));
+                    if (++stage == STAGES2) { stage = 0; phase ^= 1; }
+                }
+                if (ok) {
+                    sm100::mma_commit_pair(sm100::map_to_rank(&ctl->tfull[acc], 0));
+                    sm100::mma_commit_pair(sm100::map_to_rank(&ctl->tfull[acc], 1));
+                }
+            }
+        }
+    } else {
+        const int q = warp & 3;
+        int it = 0;
+        for (int tile = pair; tile < num_tiles; tile += npairs, it++) {
+            const int acc = it & 1;
+            const uint32_t acc_phase = (it >> 1) & 1;
+            if (!__all_sync(0xffffffffu, wait_or_abort(&ctl->tfull[acc], acc_phase, abort_flag))) break;
+            sm100::tc_fence_after();
+            const int mb = tile % p.num_m, nb = tile / p.num_m;
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * ACC_COLS;
+            const int nt = tile + npairs;
+            if (nt < num_tiles)
+                prefetch_resid(p, (nt % p.num_m) * BM2 + (int)rank * 128 + q * 32 + lane, (nt / p.num_m) * BN2);
+            epilogue_row(p, taddr, mb * BM2 + (int)rank * 128 + q * 32 + lane, nb * BN2);
+            sm100::tc_fence_before();
+            __syncwarp();
+            // the accumulator is free once both CTAs' epilogue warps are done with it
+            if (lane == 0) sm100::mbar_arrive_cluster(sm100::map_to_rank(&ctl->tempty[acc], 0));
+        }
+    }
+    sm100::tc_fence_before();
+    sm100::cluster_sync();                 // no CTA leaves while its pair still signals it
+    if (warp == 1) {
+        sm100::tc_fence_after();
+        sm100::tmem_dealloc_pair(tmem_base, TMEM_COLS);
     }
 }
 
@@ -286,21 +482,31 @@ int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K,
             int* launches) {
     if (!gemm_tc_supported(M, N, K, lda, ldw)) return -1;
     if (((uintptr_t)A & 15) || ((uintptr_t)W & 15)) return -1;
-    if (e.mode == EPI_SWIGLU && N % BN) return -1;
-    CUtensorMap ta, tb;
-    if (!make_tmap_bf16(&ta, A, M, K, lda, BM, BK) || !make_tmap_bf16(&tb, W, N, K, ldw, BN, BK)) return -1;
-    TcParams p;
-    p.M = M; p.N = N;
-    p.num_m = (M + BM - 1) / BM;
-    p.num_n = (N + BN - 1) / BN;
-    p.num_kb = (K + BK - 1) / BK;
-    p.e = e;
+    if (e.mode == EPI_SWIGLU && N % 256) return -1;
     int dev = 0;
     cudaGetDevice(&dev);
     const int sms = (dev < 64 && g_num_sms[dev] > 0) ? g_num_sms[dev] : 148;
-    const int tiles = p.num_m * p.num_n;
-    const int grid = tiles < sms ? tiles : sms;
-    k_gemm_tc<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(ta, tb, p);
+    TcParams p;
+    p.M = M; p.N = N;
+    p.num_kb = (K + BK - 1) / BK;
+    p.e = e;
+    CUtensorMap ta, tb;
+    if (M > 128) {
+        // CTA pairs: 256 x 256 tiles, grid = one cluster of 2 per SM pair
+        if (!make_tmap_bf16(&ta, A, M, K, lda, 128, BK) || !make_tmap_bf16(&tb, W, N, K, ldw, 128, BK)) return -1;
+        p.num_m = (M + BM2 - 1) / BM2;
+        p.num_n = (N + BN2 - 1) / BN2;
+        const int tiles = p.num_m * p.num_n;
+        int pairs = sms / 2;
+        if (tiles < pairs) pairs = tiles;
+        k_gemm_tc_pair<<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(ta, tb, p);
+    } else {
+        if (!make_tmap_bf16(&ta, A, M, K, lda, BM1, BK) || !make_tmap_bf16(&tb, W, N, K, ldw, BN1, BK)) return -1;
+        p.num_m = (M + BM1 - 1) / BM1;
+        p.num_n = (N + BN1 - 1) / BN1;
+        const int tiles = p.num_m * p.num_n;
+        k_gemm_tc<<<tiles < sms ? tiles : sms, NUM_THREADS, SMEM1_BYTES, s>>>(ta, tb, p);
+    }
     if (launches) (*launches)++;
     return 0;
 }
@@ -321,7 +527,9 @@ int kernels_init_device() {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64) cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1_BYTES);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_gemm_tc_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
     if (e != cudaSuccess) return (int)e;
     if (int rc = awa_tc_init_device()) return rc;
     return awa_init_device();
