@@ -299,6 +299,52 @@ int DitB200::upload_geom(GeomDev& g, const WinGeom& w, int TXT_expected) {
     if (int rc = up(g.vsin, vs.data(), vs.size() * 4)) return rc;
     if (int rc = up(g.tcos, tc.data(), tc.size() * 4)) return rc;
     if (int rc = up(g.tsin, ts.data(), ts.size() * 4)) return rc;
+    // grid token -> (packed vid index, window, RoPE positions); gi = -1 for
+    // tokens outside every window.  The fused QKV epilogue also needs the
+    // angle tables to have the make_win structure (angle of pair i =
+    // pos[i / 21] * base[i % 21], vid pos = (txt_len + t, local h, local w),
+    // txt pos = (p, p, p)); that is checked bit for bit here, and geometries
+    // that fail it keep the separate pack kernel.
+    double base[21];
+    for (int j = 0; j < 21; j++) base[j] = 1.0 / std::pow(10000.0, (double)(2 * j) / 42);
+    std::vector<int> tokpos(4 * (size_t)std::max(w.tokens(), 1), -1);
+    bool structured = true;
+    int npos = TXT + 1;
+    for (int i = 0; i < nwin; i++) {
+        const Window& win = w.win[i];
+        int gi = tab.cumf[i];
+        for (int a = win.t0; a < win.t1; a++)
+            for (int b = win.h0; b < win.h1; b++)
+                for (int c = win.w0; c < win.w1; c++, gi++) {
+                    const int pos[3] = {TXT + a - win.t0, b - win.h0, c - win.w0};
+                    const int tok = (a * w.h + b) * w.w + c;
+                    tokpos[4 * (size_t)tok] = gi;
+                    tokpos[4 * (size_t)tok + 1] = i;
+                    tokpos[4 * (size_t)tok + 2] = pos[0] | (pos[1] << 16);
+                    tokpos[4 * (size_t)tok + 3] = pos[2];
+                    npos = std::max(npos, std::max(pos[0], std::max(pos[1], pos[2])) + 1);
+                    for (int k = 0; k < ROPE_ROT && structured; k++)
+                        if (w.vid_freq[(size_t)gi * ROPE_ROT + k] != (float)((double)pos[k / 42] * base[(k % 42) / 2]))
+                            structured = false;
+                }
+        for (int p = 0; p < TXT && structured; p++)
+            for (int k = 0; k < ROPE_ROT; k++)
+                if (w.txt_freq[((size_t)i * TXT + p) * ROPE_ROT + k] != (float)((double)p * base[(k % 42) / 2])) {
+                    structured = false;
+                    break;
+                }
+    }
+    if (npos >= 65536) structured = false;
+    std::vector<float> cs((size_t)npos * 21 * 2);
+    for (int p = 0; p < npos; p++)
+        for (int j = 0; j < 21; j++) {
+            const float ang = (float)((double)p * base[j]);
+            cs[((size_t)p * 21 + j) * 2] = cosf(ang);
+            cs[((size_t)p * 21 + j) * 2 + 1] = sinf(ang);
+        }
+    if (int rc = up(g.tokpos, tokpos.data(), tokpos.size() * 4)) return rc;
+    if (int rc = up(g.cs, cs.data(), cs.size() * 4)) return rc;
+    g.structured = structured;
     g.host = w;
     g.tab = tab;
     AwaDev& v = g.view;
@@ -436,13 +482,36 @@ int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s) {
                 NORM_EPS, Xn_.p, DIM, act_, s);
     launches_++;
     pend(s);
-    // 2. qkv projection (no bias)
-    GemmEpi e; e.mode = EPI_STORE; e.out_t = act_; e.ldo = QKV;
-    if (dual) {
-        e.out = qkv; gemm(xn, DIM, BV.qkv, Lv, e, s);
-        e.out = qkv + (size_t)Lv * QKV * ab; gemm(xn + (size_t)Lv * DIM * ab, DIM, BT.qkv, TXT, e, s);
+    // 2. qkv projection (no bias), then qk-norm + RoPE + window packing
+    const bool fused_pack = act_ == ACT_BF16 && BV.qkv.t == ACT_BF16 && G.structured &&
+                            gemm_tc_supported(M, QKV, DIM, DIM, DIM);
+    if (fused_pack) {
+        // one tcgen05 GEMM epilogue writes the packed Q/K/V directly (no qkv buffer)
+        GemmEpi e; e.mode = EPI_QKV_PACK;
+        PackEpi& k = e.pk;
+        k.tokpos = G.tokpos.as<const int4>(); k.cums = G.view.cums; k.cs = G.cs.as<const float2>();
+        k.nq0 = normw(i, 0, 0); k.nk0 = normw(i, 0, 1); k.nq1 = normw(i, 1, 0); k.nk1 = normw(i, 1, 1);
+        k.eps = NORM_EPS; k.Lv = Lv; k.TXT = TXT; k.nwin = G.view.nwin; k.sumS = G.view.sumS;
+        k.Qp = Qp_.p; k.Kp = Kp_.p; k.Vp = Vp_.p;
+        if (dual) {
+            k.row_base = 0; gemm(xn, DIM, BV.qkv, Lv, e, s);
+            k.row_base = Lv; gemm(xn + (size_t)Lv * DIM * ab, DIM, BT.qkv, TXT, e, s);
+        } else {
+            k.row_base = 0; gemm(xn, DIM, BV.qkv, M, e, s);
+        }
     } else {
-        e.out = qkv; gemm(xn, DIM, BV.qkv, M, e, s);
+        GemmEpi e; e.mode = EPI_STORE; e.out_t = act_; e.ldo = QKV;
+        if (dual) {
+            e.out = qkv; gemm(xn, DIM, BV.qkv, Lv, e, s);
+            e.out = qkv + (size_t)Lv * QKV * ab; gemm(xn + (size_t)Lv * DIM * ab, DIM, BT.qkv, TXT, e, s);
+        } else {
+            e.out = qkv; gemm(xn, DIM, BV.qkv, M, e, s);
+        }
+        pbeg(KK_PACK, 0, (double)G.view.sumS * QKV * ab * 2, s);
+        awa_pack(qkv, qkv + (size_t)Lv * QKV * ab, act_, QKV, G.view, normw(i, 0, 0), normw(i, 0, 1),
+                 normw(i, 1, 0), normw(i, 1, 1), NORM_EPS, Qp_.p, Kp_.p, Vp_.p, act_, s);
+        launches_++;
+        pend(s);
     }
     // 3. AWA
     double attn_flops = 0;
@@ -450,11 +519,6 @@ int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s) {
         const double S = G.tab.cums[w + 1] - G.tab.cums[w];
         attn_flops += 4.0 * S * S * HEAD_D * HEADS;
     }
-    pbeg(KK_PACK, 0, (double)G.view.sumS * QKV * ab * 2, s);
-    awa_pack(qkv, qkv + (size_t)Lv * QKV * ab, act_, QKV, G.view, normw(i, 0, 0), normw(i, 0, 1), normw(i, 1, 0),
-             normw(i, 1, 1), NORM_EPS, Qp_.p, Kp_.p, Vp_.p, act_, s);
-    launches_++;
-    pend(s);
     pbeg(KK_ATTN, attn_flops, (double)G.view.sumS * QKV * ab + (double)Lv * DIM * ab + (double)G.view.nwin * TXT * DIM * 4, s);
     awa_attend(Qp_.p, Kp_.p, Vp_.p, act_, G.view, 1.0f / sqrtf((float)HEAD_D), att, DIM, act_, TOUTW_.as<float>(), s,
                &launches_);

@@ -40,9 +40,10 @@ struct DevBuf {
 struct GeomDev {
     WinGeom host;
     WinTables tab;
-    DevBuf vidx, cumf, cums, row_win, vcos, vsin, tcos, tsin;
+    DevBuf vidx, cumf, cums, row_win, vcos, vsin, tcos, tsin, tokpos, cs;
     AwaDev view;
     bool ready = false;
+    bool structured = false;    // RoPE angles follow make_win (fused QKV epilogue allowed)
 };
 
 struct Linear {

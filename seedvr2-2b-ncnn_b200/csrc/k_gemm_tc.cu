@@ -101,11 +101,111 @@ __device__ __forceinline__ void prefetch_resid(const TcParams& p, int row, int n
         if (n0 + 32 * j < p.N) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + 32 * j));
 }
 
+// 128 values of one head as bf16 to a packed row (256 B, 16-B stores).
+__device__ __forceinline__ void store_head_bf16(bf16* dst, const float* x) {
+    #pragma unroll
+    for (int c = 0; c < 4; c++) store32(dst + 32 * c, x + 32 * c);
+}
+
+// RoPE of one normalised head: dims 0..125 rotate in adjacent pairs
+// (src/dit_vk.cpp:62-71), pair i with the angle of position pos[i / 21] and
+// frequency i % 21 (cos/sin from the [pos][21] table), dims 126..127 pass
+// through; the result is stored as bf16.
+__device__ __forceinline__ void rope_store(bf16* dst, const float* x, const float2* __restrict__ cs, int p0, int p1,
+                                           int p2) {
+    #pragma unroll
+    for (int c = 0; c < 4; c++) {
+        float o[32];
+        #pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+            const int k = 32 * c + j;
+            if (k < 126) {
+                const int i = k >> 1, ax = i / 21, f = i % 21;
+                const int pos = ax == 0 ? p0 : (ax == 1 ? p1 : p2);
+                const float2 t = __ldg(cs + pos * 21 + f);
+                const float a = x[k], b = x[k + 1];
+                o[j] = __fadd_rn(__fmul_rn(a, t.x), __fmul_rn(-b, t.y));
+                o[j + 1] = __fadd_rn(__fmul_rn(b, t.x), __fmul_rn(a, t.y));
+            } else {
+                o[j] = x[k]; o[j + 1] = x[k + 1];
+            }
+        }
+        store32(dst + 32 * c, o);
+    }
+}
+
+// EPI_QKV_PACK: the tile's 256 columns are two heads of one of q / k / v.
+// q and k heads get RMSNorm over their 128 dims (x / sqrt(mean(x^2)+eps) * w,
+// the division as a reciprocal multiply: this epilogue serves the bf16 path)
+// and RoPE, v heads pass through; each row lands in its window-packed slot(s)
+// (a txt row in every window, with the same angles in each).
+__device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t taddr, int row, int n0) {
+    const PackEpi& k = p.e.pk;
+    bool row_ok = row < p.M;
+    const int gr = k.row_base + row;
+    const bool vid = gr < k.Lv;
+    const int sec = n0 / 2560;                     // 0 q, 1 k, 2 v
+    const int h0 = (n0 % 2560) / 128;
+    bf16* base = (bf16*)(sec == 0 ? k.Qp : sec == 1 ? k.Kp : k.Vp);
+    int gi = 0, wi = 0, ti = 0, p0 = 0, p1 = 0, p2 = 0;
+    if (row_ok && vid) {
+        const int4 tp = k.tokpos[gr];
+        gi = tp.x; wi = tp.y; p0 = tp.z & 0xFFFF; p1 = tp.z >> 16; p2 = tp.w;
+        if (gi < 0) row_ok = false;                // token outside every window: no packed slot
+    }
+    if (!vid) { ti = gr - k.Lv; p0 = p1 = p2 = ti; }
+    const float* w = nullptr;
+    if (sec < 2) w = vid ? (sec == 0 ? k.nq0 : k.nk0) : (sec == 0 ? k.nq1 : k.nk1);
+    #pragma unroll 1
+    for (int hh = 0; hh < 2; hh++) {
+        float x[128];
+        #pragma unroll
+        for (int c = 0; c < 4; c++) sm100::tmem_ld32(taddr + hh * 128 + c * 32, x + c * 32);
+        if (!row_ok) continue;
+        const int h = h0 + hh;
+        if (sec < 2) {
+            float sq = 0.f;
+            #pragma unroll
+            for (int d = 0; d < 128; d++) sq = fmaf(x[d], x[d], sq);
+            const float inv = 1.f / sqrtf(__fadd_rn(sq * (1.f / 128.f), k.eps));
+            #pragma unroll
+            for (int d = 0; d < 128; d += 4) {
+                const float4 w4 = __ldg(reinterpret_cast<const float4*>(w + d));
+                x[d] = x[d] * inv * w4.x; x[d + 1] = x[d + 1] * inv * w4.y;
+                x[d + 2] = x[d + 2] * inv * w4.z; x[d + 3] = x[d + 3] * inv * w4.w;
+            }
+        }
+        if (vid) {
+            bf16* dst = base + ((size_t)h * k.sumS + gi + (size_t)wi * k.TXT) * 128;
+            if (sec < 2) rope_store(dst, x, k.cs, p0, p1, p2);
+            else store_head_bf16(dst, x);
+        } else {
+            // rotate once (txt angles do not depend on the window), store per window
+            if (sec < 2) {
+                bf16* first = base + ((size_t)h * k.sumS + k.cums[1] - k.TXT + ti) * 128;
+                rope_store(first, x, k.cs, p0, p1, p2);
+                #pragma unroll 1
+                for (int wj = 1; wj < k.nwin; wj++) {
+                    bf16* dst = base + ((size_t)h * k.sumS + k.cums[wj + 1] - k.TXT + ti) * 128;
+                    #pragma unroll
+                    for (int c = 0; c < 16; c++)
+                        reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(first)[c];
+                }
+            } else {
+                #pragma unroll 1
+                for (int wj = 0; wj < k.nwin; wj++)
+                    store_head_bf16(base + ((size_t)h * k.sumS + k.cums[wj + 1] - k.TXT + ti) * 128, x);
+            }
+        }
+    }
+}
+
 // Epilogue of one accumulator row (thread = TMEM lane = output row) over the
 // tile's 256 columns starting at n0.  The tcgen05.ld are warp-collective and
 // executed by every lane; only the stores depend on the row.
 __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, int row, int n0) {
     const GemmEpi& e = p.e;
+    if (e.mode == EPI_QKV_PACK) { epilogue_qkv_pack(p, taddr, row, n0); return; }
     const bool row_ok = row < p.M;
     if (e.mode == EPI_SWIGLU) {
         // column block [h 128 | g 128] -> 128 outputs at n0 / 2
@@ -483,6 +583,7 @@ int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K,
     if (!gemm_tc_supported(M, N, K, lda, ldw)) return -1;
     if (((uintptr_t)A & 15) || ((uintptr_t)W & 15)) return -1;
     if (e.mode == EPI_SWIGLU && N % 256) return -1;
+    if (e.mode == EPI_QKV_PACK && N != 3 * 2560) return -1;
     int dev = 0;
     cudaGetDevice(&dev);
     const int sms = (dev < 64 && g_num_sms[dev] > 0) ? g_num_sms[dev] : 148;

@@ -14,9 +14,30 @@ enum EpiMode {
     EPI_STORE = 0,       // out[r,c] = acc + bias[c]
     EPI_GATE_RESID = 1,  // resid[r,c] = (acc + bias[c]) * gate[c] + resid[r,c]
     EPI_SWIGLU = 2,      // 256-wide column blocks [h 128 | g 128]: out[r, blk*128+j] = silu(g_j) * h_j
+    EPI_QKV_PACK = 3,    // qkv projection -> qk RMSNorm + RoPE -> window-packed Q/K/V (tcgen05 kernel only)
+};
+
+// Window geometry + per-flow qk-norm weights for EPI_QKV_PACK.  Rows of the
+// GEMM are rows row_base.. of the [vid | txt] residual: row < Lv is grid
+// token `row` (one packed destination), row >= Lv is txt row row - Lv (one
+// destination per window).
+// RoPE angles must follow the make_win structure (checked on the host): the
+// angle of pair i of a row is pos[i / 21] * base[i % 21] with pos = (txt_len +
+// t, local h, local w) for vid rows and (p, p, p) for txt row p, so one
+// (cos, sin) table indexed [pos][21] reproduces the per-element tables.
+struct PackEpi {
+    const int4* tokpos = nullptr;   // [Lv] (vid packed index gi, window, pos0 | pos1 << 16, pos2)
+    const int* cums = nullptr;      // [nwin+1] packed row offsets of windows
+    const float2* cs = nullptr;     // [npos][21] (cos, sin)
+    const float *nq0 = nullptr, *nk0 = nullptr;     // vid flow qk-norm weights [128]
+    const float *nq1 = nullptr, *nk1 = nullptr;     // txt flow
+    float eps = 1e-5f;
+    int Lv = 0, TXT = 0, nwin = 0, sumS = 0, row_base = 0;
+    void *Qp = nullptr, *Kp = nullptr, *Vp = nullptr;   // bf16 [20][sumS][128]
 };
 
 struct GemmEpi {
+    PackEpi pk;
     EpiMode mode = EPI_STORE;
     const float* bias = nullptr;     // [N] or null
     void* out = nullptr;             // STORE / SWIGLU output
