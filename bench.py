@@ -184,11 +184,20 @@ def run_ours(args):
     ctx = s2b.DitB200(local, prec)
     ctx.init_synth(WEIGHT_SEED, 0, 32)
     ctx.set_windows(s2b.make_win(T, H, W, (4, 3, 3), TXT, False), s2b.make_win(T, H, W, (4, 3, 3), TXT, True))
+    image = args.mode == "image"
+    if image:
+        # window-sharded: rank 0's ncclUniqueId goes to every rank over the torch process group
+        uid = [s2b.nccl_unique_id() if rank == 0 else None]
+        if world > 1:
+            torch.distributed.broadcast_object_list(uid, src=0)
+        ctx.shard_init(uid[0], world, rank)
 
-    # frames of this rank: k = step * world + rank, seed 42 + k (round-robin)
+    # frame mode: frames of this rank k = step * world + rank, seed 42 + k (round-robin);
+    # image mode: every rank works on frame k = step, seed 42 + k
     nfr = args.warmup + args.steps
     txt = s2b.synth_txt(TXT, 42)
-    frames = [s2b.patchify_grid(s2b.synth_vid_grid(T, 2 * H, 2 * W, 42 + i * world + rank)) for i in range(min(nfr, 8))]
+    fseed = (lambda i: 42 + i) if image else (lambda i: 42 + i * world + rank)
+    frames = [s2b.patchify_grid(s2b.synth_vid_grid(T, 2 * H, 2 * W, fseed(i))) for i in range(min(nfr, 8))]
     d_txt = torch.from_numpy(txt).to(dev)
     d_vid = [torch.from_numpy(f).to(dev) for f in frames]
     d_sr = [torch.empty(Lv, 64, device=dev) for _ in frames]
@@ -200,8 +209,8 @@ def run_ours(args):
 
     def step(i):
         j = i % len(frames)
-        ctx.forward_dev(d_vid[j].data_ptr(), Lv, d_txt.data_ptr(), TXT, TIMESTEP, d_sr[j].data_ptr(),
-                        stream.cuda_stream)
+        fwd = ctx.shard_forward_dev if image else ctx.forward_dev
+        fwd(d_vid[j].data_ptr(), Lv, d_txt.data_ptr(), TXT, TIMESTEP, d_sr[j].data_ptr(), stream.cuda_stream)
 
     for i in range(args.warmup):
         step(i)
@@ -225,19 +234,20 @@ def run_ours(args):
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms_max = float(t.item())
-    frames_total = args.steps * world
+    frames_total = args.steps if image else args.steps * world
     value = ms_max / frames_total
 
     # e2e through the host-buffer public API: pinned input -> forward -> host result
     h_vid = [torch.from_numpy(f).pin_memory() for f in frames]
     h_txt = torch.from_numpy(txt).pin_memory()
     h_sr = torch.empty(Lv, 64).pin_memory()
+    host_fwd = ctx.shard_forward if image else ctx.forward
     for i in range(2):
-        ctx.forward(h_vid[i % len(frames)].numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
+        host_fwd(h_vid[i % len(frames)].numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
     barrier()
     w0 = time.perf_counter()
     for i in range(args.steps):
-        sr = ctx.forward(h_vid[i % len(frames)].numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
+        sr = host_fwd(h_vid[i % len(frames)].numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
     w1 = time.perf_counter()
     barrier()
     te = torch.tensor([(w1 - w0) * 1e3], device=dev, dtype=torch.float64)
@@ -248,7 +258,7 @@ def run_ours(args):
     d2h = Lv * 64 * 4
 
     # per-kernel profile of one forward (outside the timed region)
-    prof = ctx.forward_profile(frames[0], Lv, txt, TXT, TIMESTEP)
+    prof = ctx.forward_profile(frames[0], Lv, txt, TXT, TIMESTEP, sharded=image)
     pk, src = peaks()
     g = prof["gemm_tcgen05"] if prec == s2b.PREC_BF16 else prof["gemm_fp32"]
     gemm_tflops = g["flops"] / (g["ms"] * 1e-3) / 1e12 if g["ms"] > 0 else None
@@ -283,9 +293,13 @@ def run_ours(args):
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "ms/frame", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": False,
-                "scaling": "weak", "vs_baseline": None, "dtype": args.precision, "data": "synthetic",
-                "config": {"workload": "cfg3/cfg4: 1080p 32-layer NaDiT DiT forward per frame, frames round-robin "
-                                       "over GPUs (frame k: seed 42+k)",
+                "scaling": "strong" if image else "weak", "vs_baseline": None, "dtype": args.precision,
+                "data": "synthetic",
+                "config": {"workload": ("cfg3: 1080p 32-layer NaDiT DiT forward of one frame, windows sharded "
+                                        "over the GPUs (txt all-reduce + residual exchange per layer, NCCL)")
+                           if image else ("cfg3/cfg4: 1080p 32-layer NaDiT DiT forward per frame, frames "
+                                          "round-robin over GPUs (frame k: seed 42+k)"),
+                           "mode": args.mode,
                            "precision": args.precision, "grid": list(GRID), "txt": TXT, "windows": [16, 25],
                            "frames_per_step_per_gpu": 1,
                            "l2": "no flush: every forward streams 6.7 GB of bf16 weights (> 126 MB L2)"},
@@ -367,6 +381,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
+    ap.add_argument("--mode", choices=["frames", "image"], default="frames",
+                    help="frames: independent frames dealt round-robin (weak scaling); image: one frame's "
+                         "windows sharded over the GPUs (strong scaling)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the reference CPU baseline leg")
     args = ap.parse_args()
     args.warmup_ref = 0

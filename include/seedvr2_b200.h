@@ -205,6 +205,28 @@ int s2b_nccl_unique_id(uint8_t nccl_id[128]);
 int s2b_shard_init(s2b_ctx* ctx, const uint8_t nccl_id[128], int world, int rank);
 int s2b_shard_forward(s2b_ctx* ctx, const float* vid_patch, int Lv, const float* txt, int TXT,
                       float timestep, float* sr_out);
+/* s2b_shard_forward on device buffers, ordered on `stream` (cudaStream_t);
+ * every rank passes the whole vid_patch / txt and receives the whole sr. */
+int s2b_shard_forward_dev(s2b_ctx* ctx, const float* d_vid_patch, int Lv, const float* d_txt, int TXT,
+                          float timestep, float* d_sr, void* stream);
+/* The ownership and exchange plan rank `rank` of `world` uses (host only, no
+ * context).  Parity p = 0 is the non-shifted windows (even layers), p = 1 the
+ * shifted ones (odd layers).  Outputs (any may be null):
+ *   bounds[p*(world+1) + r]: first window of rank r (last entry = nwin);
+ *   n_local[p]: this rank's residual rows; tokens[p*Lv + j]: grid token of
+ *   local row j;
+ *   after a layer of parity p this rank sends its local rows
+ *   send_idx[p*Lv + send_off[p*(world+1)+q] ..] to rank q and stores rank q's
+ *   rows at its new local rows recv_idx[p*Lv + recv_off[p*(world+1)+q] ..],
+ *   in ascending grid-token order per pair.
+ * No reference counterpart (the reference runs a frame on one device,
+ * src/dit_vk.cpp:481-676). */
+/* s2b_forward_profile over this rank's part of s2b_shard_forward (its
+ * kernels only; the NCCL transfers are not a kernel class of their own). */
+int s2b_shard_forward_profile(s2b_ctx* ctx, const float* vid_patch, int Lv, const float* txt, int TXT,
+                              float timestep, double* ms, double* flops, double* bytes, int* launches);
+int s2b_shard_plan(const s2b_win* ns, const s2b_win* sh, int world, int rank, int* bounds, int* n_local,
+                   int* tokens, int* send_off, int* send_idx, int* recv_off, int* recv_idx);
 
 #ifdef __cplusplus
 }

@@ -3,6 +3,7 @@
 #include "dit_b200.h"
 #include "dit_shard.h"
 #include "synth.h"
+#include "shard_plan.h"
 #include <cstring>
 #include <new>
 #include <string>
@@ -213,6 +214,12 @@ int s2b_forward_profile(s2b_ctx* ctx, const float* vid_patch, int Lv, const floa
     return ctx->dit.forward_profile(vid_patch, Lv, txt, TXT, t, ms, flops, bytes, launches);
 }
 
+int s2b_shard_forward_profile(s2b_ctx* ctx, const float* vid_patch, int Lv, const float* txt, int TXT, float t, double* ms,
+                        double* flops, double* bytes, int* launches) {
+    if (!ctx) return S2B_ERR_ARG;
+    return ctx->dit.forward_profile(vid_patch, Lv, txt, TXT, t, ms, flops, bytes, launches, true);
+}
+
 int s2b_linear(s2b_ctx* ctx, const float* x, int M, int K, const float* W, int N, const float* bias, float* y) {
     if (!ctx) return S2B_ERR_ARG;
     return ctx->dit.linear(x, M, K, W, N, bias, y);
@@ -252,6 +259,36 @@ int s2b_shard_init(s2b_ctx* ctx, const uint8_t id[128], int world, int rank) {
 int s2b_shard_forward(s2b_ctx* ctx, const float* vid_patch, int Lv, const float* txt, int TXT, float t, float* sr_out) {
     if (!ctx) return S2B_ERR_ARG;
     return ctx->dit.shard_forward(vid_patch, Lv, txt, TXT, t, sr_out);
+}
+
+int s2b_shard_forward_dev(s2b_ctx* ctx, const float* d_vid_patch, int Lv, const float* d_txt, int TXT, float t,
+                          float* d_sr, void* stream) {
+    if (!ctx) return S2B_ERR_ARG;
+    return ctx->dit.shard_forward_dev(d_vid_patch, Lv, d_txt, TXT, t, d_sr, (cudaStream_t)stream);
+}
+
+int s2b_shard_plan(const s2b_win* ns, const s2b_win* sh, int world, int rank, int* bounds, int* n_local,
+                   int* tokens, int* send_off, int* send_idx, int* recv_off, int* recv_idx) {
+    s2b::WinGeom a, b;
+    std::string err;
+    if (to_geom(ns, a, err) || to_geom(sh, b, err)) return S2B_ERR_ARG;
+    s2b::WinTables ta, tb;
+    const char* why = nullptr;
+    if (!s2b::build_tables(a, ta, &why) || !s2b::build_tables(b, tb, &why)) return S2B_ERR_ARG;
+    s2b::ShardPlan P;
+    if (!s2b::make_shard_plan(a, ta, b, tb, world, rank, P, &why)) return S2B_ERR_ARG;
+    const int Lv = P.Lv;
+    for (int p = 0; p < 2; p++) {
+        auto put = [](int* dst, const std::vector<int>& v) { if (dst) std::memcpy(dst, v.data(), v.size() * sizeof(int)); };
+        put(bounds ? bounds + p * (world + 1) : nullptr, P.bounds[p]);
+        if (n_local) n_local[p] = P.n_local(p);
+        put(tokens ? tokens + (size_t)p * Lv : nullptr, P.tokens[p]);
+        put(send_off ? send_off + p * (world + 1) : nullptr, P.send_off[p]);
+        put(send_idx ? send_idx + (size_t)p * Lv : nullptr, P.send_idx[p]);
+        put(recv_off ? recv_off + p * (world + 1) : nullptr, P.recv_off[p]);
+        put(recv_idx ? recv_idx + (size_t)p * Lv : nullptr, P.recv_idx[p]);
+    }
+    return S2B_OK;
 }
 
 }  // extern "C"

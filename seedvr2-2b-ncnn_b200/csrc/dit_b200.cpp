@@ -272,33 +272,16 @@ int DitB200::load_weights(const char* dir_c, bool synth, uint64_t seed, int lo, 
 }
 
 // ------------------------------------------------------------------ geometry
+static void rope_base(double base[21]) {   // src/awa_window.cpp:122-123
+    for (int j = 0; j < 21; j++) base[j] = 1.0 / std::pow(10000.0, (double)(2 * j) / 42);
+}
+
 int DitB200::upload_geom(GeomDev& g, const WinGeom& w, int TXT_expected) {
     const char* why = nullptr;
     WinTables tab;
     if (!build_tables(w, tab, &why)) return fail(ERR_ARG, std::string("window geometry: ") + why);
     if (TXT_expected >= 0 && w.txt_len != TXT_expected) return fail(ERR_ARG, "window txt_len differs from TXT");
     const int nwin = w.nwin(), TXT = w.txt_len;
-    std::vector<int> row_win((size_t)tab.cums[nwin]);
-    for (int i = 0; i < nwin; i++)
-        for (int p = tab.cums[i]; p < tab.cums[i + 1]; p++) row_win[p] = i;
-    // cos/sin of every element's own angle, in float as the reference
-    // evaluates them (src/dit_vk.cpp:66).
-    std::vector<float> vc(w.vid_freq.size()), vs(w.vid_freq.size()), tc(w.txt_freq.size()), ts(w.txt_freq.size());
-    for (size_t i = 0; i < vc.size(); i++) { vc[i] = cosf(w.vid_freq[i]); vs[i] = sinf(w.vid_freq[i]); }
-    for (size_t i = 0; i < tc.size(); i++) { tc[i] = cosf(w.txt_freq[i]); ts[i] = sinf(w.txt_freq[i]); }
-    auto up = [&](DevBuf& d, const void* src, size_t n) -> int {
-        if (int rc = cuda_check(d.ensure(std::max<size_t>(n, 16)), "cudaMalloc(geometry)")) return rc;
-        if (n) return cuda_check(cudaMemcpy(d.p, src, n, cudaMemcpyHostToDevice), "upload geometry");
-        return OK;
-    };
-    if (int rc = up(g.vidx, tab.vidx.data(), tab.vidx.size() * 4)) return rc;
-    if (int rc = up(g.cumf, tab.cumf.data(), tab.cumf.size() * 4)) return rc;
-    if (int rc = up(g.cums, tab.cums.data(), tab.cums.size() * 4)) return rc;
-    if (int rc = up(g.row_win, row_win.data(), row_win.size() * 4)) return rc;
-    if (int rc = up(g.vcos, vc.data(), vc.size() * 4)) return rc;
-    if (int rc = up(g.vsin, vs.data(), vs.size() * 4)) return rc;
-    if (int rc = up(g.tcos, tc.data(), tc.size() * 4)) return rc;
-    if (int rc = up(g.tsin, ts.data(), ts.size() * 4)) return rc;
     // grid token -> (packed vid index, window, RoPE positions); gi = -1 for
     // tokens outside every window.  The fused QKV epilogue also needs the
     // angle tables to have the make_win structure (angle of pair i =
@@ -306,7 +289,7 @@ int DitB200::upload_geom(GeomDev& g, const WinGeom& w, int TXT_expected) {
     // txt pos = (p, p, p)); that is checked bit for bit here, and geometries
     // that fail it keep the separate pack kernel.
     double base[21];
-    for (int j = 0; j < 21; j++) base[j] = 1.0 / std::pow(10000.0, (double)(2 * j) / 42);
+    rope_base(base);
     std::vector<int> tokpos(4 * (size_t)std::max(w.tokens(), 1), -1);
     bool structured = true;
     int npos = TXT + 1;
@@ -335,6 +318,22 @@ int DitB200::upload_geom(GeomDev& g, const WinGeom& w, int TXT_expected) {
                 }
     }
     if (npos >= 65536) structured = false;
+    return upload_geom_with(g, w, tab, tokpos, structured, npos, w.tokens());
+}
+
+int DitB200::upload_geom_with(GeomDev& g, const WinGeom& w, const WinTables& tab, const std::vector<int>& tokpos,
+                              bool structured, int npos, int Lv) {
+    const int nwin = (int)tab.cumf.size() - 1, TXT = w.txt_len;
+    std::vector<int> row_win((size_t)tab.cums[nwin]);
+    for (int i = 0; i < nwin; i++)
+        for (int p = tab.cums[i]; p < tab.cums[i + 1]; p++) row_win[p] = i;
+    // cos/sin of every element's own angle, in float as the reference
+    // evaluates them (src/dit_vk.cpp:66).
+    std::vector<float> vc(w.vid_freq.size()), vs(w.vid_freq.size()), tc(w.txt_freq.size()), ts(w.txt_freq.size());
+    for (size_t i = 0; i < vc.size(); i++) { vc[i] = cosf(w.vid_freq[i]); vs[i] = sinf(w.vid_freq[i]); }
+    for (size_t i = 0; i < tc.size(); i++) { tc[i] = cosf(w.txt_freq[i]); ts[i] = sinf(w.txt_freq[i]); }
+    double base[21];
+    rope_base(base);
     std::vector<float> cs((size_t)npos * 21 * 2);
     for (int p = 0; p < npos; p++)
         for (int j = 0; j < 21; j++) {
@@ -342,13 +341,28 @@ int DitB200::upload_geom(GeomDev& g, const WinGeom& w, int TXT_expected) {
             cs[((size_t)p * 21 + j) * 2] = cosf(ang);
             cs[((size_t)p * 21 + j) * 2 + 1] = sinf(ang);
         }
+    auto up = [&](DevBuf& d, const void* src, size_t n) -> int {
+        if (int rc = cuda_check(d.ensure(std::max<size_t>(n, 16)), "cudaMalloc(geometry)")) return rc;
+        if (n) return cuda_check(cudaMemcpy(d.p, src, n, cudaMemcpyHostToDevice), "upload geometry");
+        return OK;
+    };
+    if (int rc = up(g.vidx, tab.vidx.data(), tab.vidx.size() * 4)) return rc;
+    if (int rc = up(g.cumf, tab.cumf.data(), tab.cumf.size() * 4)) return rc;
+    if (int rc = up(g.cums, tab.cums.data(), tab.cums.size() * 4)) return rc;
+    if (int rc = up(g.row_win, row_win.data(), row_win.size() * 4)) return rc;
+    if (int rc = up(g.vcos, vc.data(), vc.size() * 4)) return rc;
+    if (int rc = up(g.vsin, vs.data(), vs.size() * 4)) return rc;
+    if (int rc = up(g.tcos, tc.data(), tc.size() * 4)) return rc;
+    if (int rc = up(g.tsin, ts.data(), ts.size() * 4)) return rc;
     if (int rc = up(g.tokpos, tokpos.data(), tokpos.size() * 4)) return rc;
     if (int rc = up(g.cs, cs.data(), cs.size() * 4)) return rc;
     g.structured = structured;
+    g.tokpos_host = tokpos;
+    g.npos = npos;
     g.host = w;
     g.tab = tab;
     AwaDev& v = g.view;
-    v.nwin = nwin; v.TXT = TXT; v.sumf = tab.sumf; v.sumS = tab.cums[nwin]; v.maxS = tab.maxS; v.Lv = w.tokens();
+    v.nwin = nwin; v.TXT = TXT; v.sumf = tab.sumf; v.sumS = tab.cums[nwin]; v.maxS = tab.maxS; v.Lv = Lv;
     v.vidx = g.vidx.as<int>(); v.cumf = g.cumf.as<int>(); v.cums = g.cums.as<int>(); v.row_win = g.row_win.as<int>();
     v.vcos = g.vcos.as<float>(); v.vsin = g.vsin.as<float>(); v.tcos = g.tcos.as<float>(); v.tsin = g.tsin.as<float>();
     g.ready = true;
@@ -364,6 +378,7 @@ int DitB200::set_windows(const WinGeom& ns, const WinGeom& sh) {
     if (!geom_[0].tab.covers_all || !geom_[1].tab.covers_all)
         return fail(ERR_ARG, "DiT windows must tile the token grid exactly");
     if (gexec_) { cudaGraphExecDestroy(gexec_); gexec_ = nullptr; graph_Lv_ = -1; }
+    geom_gen_++;
     return OK;
 }
 
@@ -421,7 +436,7 @@ void DitB200::gemm(const void* A, int lda, const Linear& L, int M, const GemmEpi
     pend(s);
 }
 
-static void sinusoidal256(float t, float* e) {   // src/dit_vk.cpp:295-302
+void sinusoidal256(float t, float* e) {   // src/dit_vk.cpp:295-302
     const int half = 128;
     for (int j = 0; j < 256; j++) {
         float freq = (j < half) ? (float)std::exp(-logf(10000.f) * j / half) : (float)std::exp(-logf(10000.f) * (j - half) / half);
@@ -462,24 +477,36 @@ int DitB200::enqueue_init(int Lv, int TXT, cudaStream_t s) {
     return OK;
 }
 
+LayerBufs DitB200::default_bufs() {
+    LayerBufs b;
+    b.X = X_.as<float>(); b.Xn = Xn_.p; b.QKV = QKV_.p; b.ATT = ATT_.p; b.Hs = Hs_.p;
+    b.Qp = Qp_.p; b.Kp = Kp_.p; b.Vp = Vp_.p; b.TOUTW = TOUTW_.as<float>();
+    b.geom[0] = &geom_[0]; b.geom[1] = &geom_[1];
+    return b;
+}
+
 int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s) {
+    return enqueue_layer_on(i, Lv, TXT, s, default_bufs());
+}
+
+int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const LayerBufs& B) {
     const bool dual = i < MM_LAYERS, last = (i == NUM_LAYERS - 1);
     const int M = Lv + TXT;
     const size_t ab = act_bytes(act_);
-    GeomDev& G = geom_[i % 2];
+    GeomDev& G = *B.geom[i % 2];
     const Block& BV = blk_[i][0];
     const Block& BT = dual ? blk_[i][1] : blk_[i][0];
-    char* xn = (char*)Xn_.p;
-    char* qkv = (char*)QKV_.p;
-    char* att = (char*)ATT_.p;
-    char* hs = (char*)Hs_.p;
-    float* X = X_.as<float>();
+    char* xn = (char*)B.Xn;
+    char* qkv = (char*)B.QKV;
+    char* att = (char*)B.ATT;
+    char* hs = (char*)B.Hs;
+    float* X = B.X;
 
     const double norm_bytes = (double)DIM * (4 + ab);
     // 1. attention norm + modulate (txt unmodulated on the last layer, src/dit_vk.cpp:538)
     pbeg(KK_NORM, 0, norm_bytes * M, s);
     rmsnorm_mod(X, DIM, M, Lv, ada(i, 0, 0), ada(i, 0, 1), last ? nullptr : ada(i, 1, 0), ada(i, 1, 1), nullptr,
-                NORM_EPS, Xn_.p, DIM, act_, s);
+                NORM_EPS, B.Xn, DIM, act_, s);
     launches_++;
     pend(s);
     // 2. qkv projection (no bias), then qk-norm + RoPE + window packing
@@ -492,7 +519,7 @@ int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s) {
         k.tokpos = G.tokpos.as<const int4>(); k.cums = G.view.cums; k.cs = G.cs.as<const float2>();
         k.nq0 = normw(i, 0, 0); k.nk0 = normw(i, 0, 1); k.nq1 = normw(i, 1, 0); k.nk1 = normw(i, 1, 1);
         k.eps = NORM_EPS; k.Lv = Lv; k.TXT = TXT; k.nwin = G.view.nwin; k.sumS = G.view.sumS;
-        k.Qp = Qp_.p; k.Kp = Kp_.p; k.Vp = Vp_.p;
+        k.Qp = B.Qp; k.Kp = B.Kp; k.Vp = B.Vp;
         if (dual) {
             k.row_base = 0; gemm(xn, DIM, BV.qkv, Lv, e, s);
             k.row_base = Lv; gemm(xn + (size_t)Lv * DIM * ab, DIM, BT.qkv, TXT, e, s);
@@ -509,7 +536,7 @@ int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s) {
         }
         pbeg(KK_PACK, 0, (double)G.view.sumS * QKV * ab * 2, s);
         awa_pack(qkv, qkv + (size_t)Lv * QKV * ab, act_, QKV, G.view, normw(i, 0, 0), normw(i, 0, 1),
-                 normw(i, 1, 0), normw(i, 1, 1), NORM_EPS, Qp_.p, Kp_.p, Vp_.p, act_, s);
+                 normw(i, 1, 0), normw(i, 1, 1), NORM_EPS, B.Qp, B.Kp, B.Vp, act_, s);
         launches_++;
         pend(s);
     }
@@ -520,12 +547,21 @@ int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s) {
         attn_flops += 4.0 * S * S * HEAD_D * HEADS;
     }
     pbeg(KK_ATTN, attn_flops, (double)G.view.sumS * QKV * ab + (double)Lv * DIM * ab + (double)G.view.nwin * TXT * DIM * 4, s);
-    awa_attend(Qp_.p, Kp_.p, Vp_.p, act_, G.view, 1.0f / sqrtf((float)HEAD_D), att, DIM, act_, TOUTW_.as<float>(), s,
+    awa_attend(B.Qp, B.Kp, B.Vp, act_, G.view, 1.0f / sqrtf((float)HEAD_D), att, DIM, act_, B.TOUTW, s,
                &launches_);
     pend(s);
     pbeg(KK_OTHER, 0, (double)G.view.nwin * TXT * DIM * 4 + (double)TXT * DIM * ab, s);
-    awa_coalesce(TOUTW_.as<float>(), G.view.nwin, TXT, att + (size_t)Lv * DIM * ab, DIM, act_, s);
-    launches_++;
+    if (B.txt_sum) {
+        // window-sharded: sum this rank's windows, all-reduce across ranks,
+        // then divide by the global window count
+        awa_coalesce_div(B.TOUTW, G.view.nwin, TXT, B.txt_sum, DIM, ACT_F32, 0.f, s);
+        if (int rc = B.txt_reduce(B.reduce_ctx, s)) return rc;
+        awa_coalesce_div(B.txt_sum, 1, TXT, att + (size_t)Lv * DIM * ab, DIM, act_, (float)B.nwin_global[i % 2], s);
+        launches_ += 2;
+    } else {
+        awa_coalesce(B.TOUTW, G.view.nwin, TXT, att + (size_t)Lv * DIM * ab, DIM, act_, s);
+        launches_++;
+    }
     pend(s);
     // 4. out projection (+bias), gate, residual (src/dit_vk.cpp:461-462, 558-575)
     GemmEpi g; g.mode = EPI_GATE_RESID; g.ldr = DIM;
@@ -542,7 +578,7 @@ int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s) {
     // 5. MLP norm + modulate; txt skips the MLP on the last layer (src/dit_vk.cpp:579-620)
     const int Mm = last ? Lv : M;
     pbeg(KK_NORM, 0, norm_bytes * Mm, s);
-    rmsnorm_mod(X, DIM, Mm, Lv, ada(i, 0, 3), ada(i, 0, 4), ada(i, 1, 3), ada(i, 1, 4), nullptr, NORM_EPS, Xn_.p, DIM,
+    rmsnorm_mod(X, DIM, Mm, Lv, ada(i, 0, 3), ada(i, 0, 4), ada(i, 1, 3), ada(i, 1, 4), nullptr, NORM_EPS, B.Xn, DIM,
                 act_, s);
     launches_++;
     pend(s);
@@ -602,13 +638,14 @@ void DitB200::pend(cudaStream_t s) {
 }
 
 int DitB200::forward_profile(const float* vid_patch, int Lv, const float* txt, int TXT, float t, double* ms,
-                             double* flops, double* bytes, int* count) {
+                             double* flops, double* bytes, int* count, bool sharded) {
     if (!ms || !flops || !bytes || !count) return fail(ERR_ARG, "null profile arrays");
     if (layer_lo_ != 0 || layer_hi_ != NUM_LAYERS) return fail(ERR_STATE, "profiling needs all 32 layers loaded");
     std::vector<float> sr((size_t)std::max(Lv, 0) * OUT_CH);
     marks_.clear();
     prof_on_ = true;
-    const int rc = forward_latent(vid_patch, Lv, txt, TXT, t, 0, NUM_LAYERS, true, true, nullptr, nullptr, sr.data());
+    const int rc = sharded ? shard_forward(vid_patch, Lv, txt, TXT, t, sr.data())
+                           : forward_latent(vid_patch, Lv, txt, TXT, t, 0, NUM_LAYERS, true, true, nullptr, nullptr, sr.data());
     prof_on_ = false;
     if (rc) return rc;
     for (int k = 0; k < KK_COUNT; k++) { ms[k] = 0; flops[k] = 0; bytes[k] = 0; count[k] = 0; }

@@ -44,6 +44,8 @@ struct GeomDev {
     AwaDev view;
     bool ready = false;
     bool structured = false;    // RoPE angles follow make_win (fused QKV epilogue allowed)
+    std::vector<int> tokpos_host;   // host copy of tokpos (int4 per row)
+    int npos = 0;                   // rows of the cs table
 };
 
 struct Linear {
@@ -58,6 +60,25 @@ struct Block {
     Linear qkv, out, mlp_hg, mlp_out;   // mlp_hg: proj_in | proj_in_gate interleaved in 128-row blocks
     bool loaded = false;
 };
+
+// Buffers and geometry one block runs on: the context's own (single GPU) or a
+// window shard's local ones (dit_shard.cpp).
+struct LayerBufs {
+    float* X = nullptr;
+    void *Xn = nullptr, *QKV = nullptr, *ATT = nullptr, *Hs = nullptr;
+    void *Qp = nullptr, *Kp = nullptr, *Vp = nullptr;
+    float* TOUTW = nullptr;
+    GeomDev* geom[2] = {nullptr, nullptr};
+    // sharded only: this rank's txt partial sums, their cross-rank reduction
+    // and the global window counts the sum is divided by
+    float* txt_sum = nullptr;
+    int (*txt_reduce)(void* ctx, cudaStream_t s) = nullptr;
+    void* reduce_ctx = nullptr;
+    int nwin_global[2] = {0, 0};
+};
+
+// 256-wide sinusoidal timestep features (src/dit_vk.cpp:295-302).
+void sinusoidal256(float t, float* e);
 
 // Kernel classes of the per-kernel profile (s2b_forward_profile).
 enum KernelKind { KK_GEMM_TC = 0, KK_GEMM_SIMT = 1, KK_ATTN = 2, KK_PACK = 3, KK_NORM = 4, KK_OTHER = 5, KK_COUNT = 6 };
@@ -80,8 +101,9 @@ public:
     int time_embedding(float t, float* emb_host);
     // forward_latent(0, 32, init, final) with CUDA events around every kernel:
     // per KernelKind the summed device ms, algorithmic FLOPs / bytes, launches.
+    // sharded: profile this rank's part of shard_forward instead.
     int forward_profile(const float* vid_patch, int Lv, const float* txt, int TXT, float t, double* ms,
-                        double* flops, double* bytes, int* count);
+                        double* flops, double* bytes, int* count, bool sharded = false);
     // One Linear on the context's GEMM engine (host buffers).
     int linear(const float* x, int M, int K, const float* W, int N, const float* bias, float* y);
     int ada_compose(const float* emb_host, float* out_host);
@@ -107,6 +129,8 @@ public:
     // Multi-GPU window sharding (dit_shard.cpp).
     int shard_init(const uint8_t id[128], int world, int rank);
     int shard_forward(const float* vid_patch, int Lv, const float* txt, int TXT, float t, float* sr_out);
+    int shard_forward_dev(const float* d_vid_patch, int Lv, const float* d_txt, int TXT, float t, float* d_sr,
+                          cudaStream_t user);
 
 private:
     int fail(int code, const std::string& m) { err = m; return code; }
@@ -119,12 +143,19 @@ private:
                 const float* nqt, const float* nkt, int Lv, int TXT, float eps, float* vid_out, float* txt_out,
                 cudaStream_t user);
     int upload_geom(GeomDev& g, const WinGeom& w, int TXT_expected);
+    int upload_geom_with(GeomDev& g, const WinGeom& w, const WinTables& tab, const std::vector<int>& tokpos4,
+                         bool structured, int npos, int Lv);
     void gemm(const void* A, int lda, const Linear& L, int M, const GemmEpi& e, cudaStream_t s);
     // Enqueue the pieces of forward_latent on stream s (device inputs already staged).
     int enqueue_init(int Lv, int TXT, cudaStream_t s);
     int enqueue_temb(cudaStream_t s);
     int enqueue_layer(int i, int Lv, int TXT, cudaStream_t s);
+    int enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const LayerBufs& B);
+    LayerBufs default_bufs();
     int enqueue_final(int Lv, cudaStream_t s);
+    int shard_prepare(int Lv, int TXT);
+    int shard_enqueue(cudaStream_t s);
+    int shard_exchange(int p, cudaStream_t s);
     const float* ada(int layer, int flow, int k) const {
         return ada_.as<float>() + ((size_t)(layer * 12 + flow * 6 + k)) * DIM;
     }
@@ -148,6 +179,7 @@ private:
     DevBuf temb_in_, temb_h1_, temb_h2_;   // [256], [2560], [2560]
 
     GeomDev geom_[2];   // non-shifted (even layers), shifted (odd layers)
+    int geom_gen_ = 0;  // bumped by set_windows (shard plans follow it)
     GeomDev awa_geom_[2];
 
     // activations

@@ -1,23 +1,368 @@
 // dit_shard.cpp -- multi-GPU window-sharded forward (NCCL over NVLink).
+//
+// One process and one context per GPU.  Every rank holds all weights and
+// runs the per-token work (norms, GEMMs, gates) only for the grid tokens of
+// the windows it owns in the current layer's parity (shard_plan.h); the 58
+// txt rows are replicated.  Per layer there are two exchanges:
+//   * the txt outputs of the attention: each rank sums its windows' txt
+//     outputs, one ncclAllReduce(sum) of [TXT, 2560] fp32 adds the ranks'
+//     partial sums, and the total is divided by the global window count
+//     (the cross-window mean of src/dit_vk.cpp:435-437);
+//   * the residual rows whose owner changes between the non-shifted and the
+//     shifted windows: grouped ncclSend / ncclRecv between the ranks that
+//     exchange rows, with gather / scatter kernels on either side.
+// The vid input patches are replicated on every rank (each gathers its own
+// rows) and the [Lv, 64] output is assembled by an all-reduce of zero-filled
+// full-size buffers, so every rank returns the whole result.
 #include "dit_shard.h"
+#include <dlfcn.h>
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
 
 namespace s2b {
 
-DitB200::ShardState::~ShardState() {}
+const NcclLib* nccl_lib(std::string* err) {
+    static NcclLib lib;
+    static std::once_flag once;
+    static std::string load_err;
+    std::call_once(once, [] {
+        const char* name = std::getenv("S2B_NCCL_LIB");
+        void* h = dlopen(name && *name ? name : "libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) {
+            const char* e = dlerror();
+            load_err = std::string("cannot load NCCL: ") + (e ? e : "unknown dlopen error");
+            return;
+        }
+        bool ok = true;
+        auto sym = [&](auto& fn, const char* n) {
+            fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, n));
+            if (!fn) ok = false;
+        };
+        sym(lib.GetUniqueId, "ncclGetUniqueId");
+        sym(lib.CommInitRank, "ncclCommInitRank");
+        sym(lib.CommDestroy, "ncclCommDestroy");
+        sym(lib.AllReduce, "ncclAllReduce");
+        sym(lib.Send, "ncclSend");
+        sym(lib.Recv, "ncclRecv");
+        sym(lib.GroupStart, "ncclGroupStart");
+        sym(lib.GroupEnd, "ncclGroupEnd");
+        sym(lib.GetErrorString, "ncclGetErrorString");
+        if (!ok) {
+            load_err = "the NCCL library lacks an entry point this build needs";
+            dlclose(h);
+            return;
+        }
+        lib.handle = h;
+    });
+    if (!lib.handle) {
+        if (err) *err = load_err;
+        return nullptr;
+    }
+    return &lib;
+}
+
+int DitB200::ShardState::nccl_check(ncclResult_t r, const char* what, std::string& err) const {
+    if (r == ncclSuccess) return OK;
+    err = std::string(what) + ": " + (nl && nl->GetErrorString ? nl->GetErrorString(r) : "NCCL error");
+    return ERR_NCCL;
+}
+
+DitB200::ShardState::~ShardState() {
+    if (comm && nl) {
+        if (dev >= 0) cudaSetDevice(dev);
+        nl->CommDestroy(comm);
+    }
+}
 
 int DitB200::shard_init(const uint8_t id[128], int world, int rank) {
-    (void)id; (void)world; (void)rank;
-    return fail(ERR_UNSUPPORTED, "window-sharded mode is not built yet");
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    if (!weights_ || layer_lo_ != 0 || layer_hi_ != NUM_LAYERS)
+        return fail(ERR_STATE, "window-sharded mode needs all 32 layers loaded");
+    if (!id || world < 1 || rank < 0 || rank >= world) return fail(ERR_ARG, "rank outside [0, world)");
+    std::string e;
+    const NcclLib* nl = nccl_lib(&e);
+    if (!nl) return fail(ERR_NCCL, e);
+    cudaSetDevice(dev_);
+    shard_.reset();
+    auto S = std::make_unique<ShardState>();
+    S->world = world; S->rank = rank; S->nl = nl; S->dev = dev_;
+    ncclUniqueId uid;
+    static_assert(sizeof(uid.internal) == 128, "ncclUniqueId is 128 bytes");
+    std::memcpy(uid.internal, id, 128);
+    if (int rc = S->nccl_check(nl->CommInitRank(&S->comm, world, uid, rank), "ncclCommInitRank", err)) {
+        S->comm = nullptr;
+        return rc;
+    }
+    shard_ = std::move(S);
+    return OK;
+}
+
+int DitB200::shard_prepare(int Lv, int TXT) {
+    if (!shard_) return fail(ERR_STATE, "shard_init has not run");
+    if (!weights_) return fail(ERR_STATE, "weights not loaded");
+    if (!geom_[0].ready || !geom_[1].ready) return fail(ERR_STATE, "windows not set");
+    if (Lv != geom_[0].view.Lv || TXT != geom_[0].view.TXT || TXT <= 0) return fail(ERR_ARG, "Lv/TXT do not match the windows");
+    ShardState& S = *shard_;
+    if (S.plan_gen == geom_gen_) return OK;
+    const char* why = nullptr;
+    ShardPlan plan;
+    if (!make_shard_plan(geom_[0].host, geom_[0].tab, geom_[1].host, geom_[1].tab, S.world, S.rank, plan, &why))
+        return fail(ERR_ARG, std::string("window sharding: ") + why);
+    // local geometries: this rank's windows, vid rows numbered in local packed order
+    for (int p = 0; p < 2; p++) {
+        const GeomDev& G = geom_[p];
+        const int a = plan.bounds[p][S.rank], b = plan.bounds[p][S.rank + 1];
+        const int f0 = G.tab.cumf[a], f1 = G.tab.cumf[b], n = f1 - f0;
+        WinGeom lw;
+        lw.t = G.host.t; lw.h = G.host.h; lw.w = G.host.w; lw.txt_len = TXT;
+        lw.win.assign(G.host.win.begin() + a, G.host.win.begin() + b);
+        lw.vid_freq.assign(G.host.vid_freq.begin() + (size_t)f0 * ROPE_ROT, G.host.vid_freq.begin() + (size_t)f1 * ROPE_ROT);
+        lw.txt_freq.assign(G.host.txt_freq.begin() + (size_t)a * TXT * ROPE_ROT,
+                           G.host.txt_freq.begin() + (size_t)b * TXT * ROPE_ROT);
+        WinTables lt;
+        lt.sumf = n;
+        lt.covers_all = true;
+        lt.vidx.resize(n);
+        for (int j = 0; j < n; j++) lt.vidx[j] = j;
+        std::vector<int> tp(4 * (size_t)std::max(n, 1), -1);
+        for (int w = a; w <= b; w++) {
+            lt.cumf.push_back(G.tab.cumf[w] - f0);
+            lt.cums.push_back(G.tab.cums[w] - G.tab.cums[a]);
+        }
+        for (int w = a; w < b; w++) {
+            lt.maxS = std::max(lt.maxS, G.tab.cums[w + 1] - G.tab.cums[w]);
+            for (int gi = G.tab.cumf[w]; gi < G.tab.cumf[w + 1]; gi++) {
+                const int j = gi - f0, tok = G.tab.vidx[gi];
+                tp[4 * (size_t)j] = j;
+                tp[4 * (size_t)j + 1] = w - a;
+                tp[4 * (size_t)j + 2] = G.tokpos_host[4 * (size_t)tok + 2];
+                tp[4 * (size_t)j + 3] = G.tokpos_host[4 * (size_t)tok + 3];
+            }
+        }
+        if (int rc = upload_geom_with(S.geom[p], lw, lt, tp, G.structured, G.npos, n)) return rc;
+        S.nwin_global[p] = G.view.nwin;
+    }
+    const int n0 = plan.n_local(0), n1 = plan.n_local(1), nmax = std::max(n0, n1);
+    const size_t Mmax = (size_t)nmax + TXT, ab = act_bytes(act_);
+    size_t sumS = 0, nwT = 0;
+    for (int p = 0; p < 2; p++) {
+        sumS = std::max(sumS, (size_t)S.geom[p].view.sumS);
+        nwT = std::max(nwT, (size_t)S.geom[p].view.nwin * TXT);
+    }
+    // exchange index lists
+    size_t nsend = 0, nrecv = 0;
+    std::vector<int> snd[2], rcv[2], ssrc[2], sdst[2];
+    for (int p = 0; p < 2; p++) {
+        const int me = S.rank;
+        S.send_ns_off[p].assign(S.world + 1, 0);
+        S.recv_ns_off[p].assign(S.world + 1, 0);
+        for (int q = 0; q < S.world; q++) {
+            const int s0 = plan.send_off[p][q], s1 = plan.send_off[p][q + 1];
+            const int r0 = plan.recv_off[p][q], r1 = plan.recv_off[p][q + 1];
+            if (q == me) {
+                ssrc[p].assign(plan.send_idx[p].begin() + s0, plan.send_idx[p].begin() + s1);
+                sdst[p].assign(plan.recv_idx[p].begin() + r0, plan.recv_idx[p].begin() + r1);
+            } else {
+                snd[p].insert(snd[p].end(), plan.send_idx[p].begin() + s0, plan.send_idx[p].begin() + s1);
+                rcv[p].insert(rcv[p].end(), plan.recv_idx[p].begin() + r0, plan.recv_idx[p].begin() + r1);
+            }
+            S.send_ns_off[p][q + 1] = (int)snd[p].size();
+            S.recv_ns_off[p][q + 1] = (int)rcv[p].size();
+        }
+        if (ssrc[p].size() != sdst[p].size()) return fail(ERR_STATE, "inconsistent local exchange plan");
+        S.n_self[p] = (int)ssrc[p].size();
+        nsend = std::max(nsend, snd[p].size());
+        nrecv = std::max(nrecv, rcv[p].size());
+    }
+    auto alloc = [&](DevBuf& d, size_t n, const char* what) { return cuda_check(d.ensure(std::max<size_t>(n, 16)), what); };
+    auto up = [&](DevBuf& d, const std::vector<int>& v) -> int {
+        if (int rc = alloc(d, v.size() * 4, "cudaMalloc(shard index)")) return rc;
+        if (v.empty()) return OK;
+        return cuda_check(cudaMemcpy(d.p, v.data(), v.size() * 4, cudaMemcpyHostToDevice), "upload shard index");
+    };
+    int rc;
+    if ((rc = alloc(S.X[0], ((size_t)n0 + TXT) * DIM * 4, "cudaMalloc(shard X)"))) return rc;
+    if ((rc = alloc(S.X[1], ((size_t)n1 + TXT) * DIM * 4, "cudaMalloc(shard X)"))) return rc;
+    if ((rc = alloc(S.Xn, Mmax * DIM * ab, "cudaMalloc(shard Xn)"))) return rc;
+    if ((rc = alloc(S.QKV, Mmax * QKV * ab, "cudaMalloc(shard QKV)"))) return rc;
+    if ((rc = alloc(S.ATT, Mmax * DIM * ab, "cudaMalloc(shard ATT)"))) return rc;
+    if ((rc = alloc(S.Hs, Mmax * MLP_DIM * ab, "cudaMalloc(shard Hs)"))) return rc;
+    if ((rc = alloc(S.Qp, sumS * DIM * ab, "cudaMalloc(shard Qp)"))) return rc;
+    if ((rc = alloc(S.Kp, sumS * DIM * ab, "cudaMalloc(shard Kp)"))) return rc;
+    if ((rc = alloc(S.Vp, sumS * DIM * ab, "cudaMalloc(shard Vp)"))) return rc;
+    if ((rc = alloc(S.TOUTW, nwT * DIM * 4, "cudaMalloc(shard TOUTW)"))) return rc;
+    if ((rc = alloc(S.TXTSUM, (size_t)TXT * DIM * 4, "cudaMalloc(shard TXTSUM)"))) return rc;
+    if ((rc = alloc(S.VIDIN, (size_t)Lv * PATCH_IN * 4, "cudaMalloc(shard VIDIN)"))) return rc;
+    if ((rc = alloc(S.VIDLOC, (size_t)n0 * PATCH_IN * 4, "cudaMalloc(shard VIDLOC)"))) return rc;
+    if ((rc = alloc(S.VPIN, (size_t)n0 * PATCH_IN_PAD * ab, "cudaMalloc(shard VPIN)"))) return rc;
+    if ((rc = alloc(S.TXTIN, (size_t)TXT * TXT_IN * 4, "cudaMalloc(shard TXTIN)"))) return rc;
+    if ((rc = alloc(S.TIN, (size_t)TXT * TXT_IN * ab, "cudaMalloc(shard TIN)"))) return rc;
+    if ((rc = alloc(S.SRLOC, (size_t)n1 * OUT_CH * 4, "cudaMalloc(shard SRLOC)"))) return rc;
+    if ((rc = alloc(S.SRFULL, (size_t)Lv * OUT_CH * 4, "cudaMalloc(shard SRFULL)"))) return rc;
+    if ((rc = alloc(S.XSEND, nsend * DIM * 4, "cudaMalloc(shard XSEND)"))) return rc;
+    if ((rc = alloc(S.XRECV, nrecv * DIM * 4, "cudaMalloc(shard XRECV)"))) return rc;
+    // [h | g] fp32 staging of the SIMT SwiGLU path (the tcgen05 path fuses it)
+    if ((act_ == ACT_F32 || !gemm_tc_supported((int)Mmax, 2 * MLP_DIM, DIM, DIM, DIM)) &&
+        (rc = alloc(HG_, Mmax * 2 * MLP_DIM * 4, "cudaMalloc(HG)")))
+        return rc;
+    if ((rc = up(S.tok0, plan.tokens[0]))) return rc;
+    if ((rc = up(S.tok1, plan.tokens[(NUM_LAYERS - 1) % 2]))) return rc;
+    for (int p = 0; p < 2; p++) {
+        if ((rc = up(S.send_ns[p], snd[p]))) return rc;
+        if ((rc = up(S.recv_ns[p], rcv[p]))) return rc;
+        if ((rc = up(S.self_src[p], ssrc[p]))) return rc;
+        if ((rc = up(S.self_dst[p], sdst[p]))) return rc;
+    }
+    S.plan = std::move(plan);
+    S.Lv = Lv; S.TXT = TXT;
+    S.plan_gen = geom_gen_;
+    return OK;
+}
+
+static int shard_txt_reduce(void* ctx, cudaStream_t s) {
+    auto* S = static_cast<DitB200::ShardState*>(ctx);
+    const ncclResult_t r = S->nl->AllReduce(S->TXTSUM.p, S->TXTSUM.p, (size_t)S->TXT * DIM, ncclFloat32, ncclSum,
+                                            S->comm, s);
+    return r == ncclSuccess ? OK : ERR_NCCL;
+}
+
+int DitB200::shard_exchange(int p, cudaStream_t s) {
+    ShardState& S = *shard_;
+    const int q1 = 1 - p, me = S.rank, TXT = S.TXT;
+    float* src = S.X[p].as<float>();
+    float* dst = S.X[q1].as<float>();
+    const int np = S.plan.n_local(p), nq = S.plan.n_local(q1);
+    const int nsend = S.send_ns_off[p][S.world], nrecv = S.recv_ns_off[p][S.world];
+    float* xs = S.XSEND.as<float>();
+    float* xr = S.XRECV.as<float>();
+    copy_rows_f32(src, DIM, S.send_ns[p].as<int>(), xs, DIM, nullptr, nsend, DIM, s);
+    copy_rows_f32(src, DIM, S.self_src[p].as<int>(), dst, DIM, S.self_dst[p].as<int>(), S.n_self[p], DIM, s);
+    copy_rows_f32(src + (size_t)np * DIM, DIM, nullptr, dst + (size_t)nq * DIM, DIM, nullptr, TXT, DIM, s);
+    launches_ += 3;
+    if (nsend || nrecv) {
+        int rc = S.nccl_check(S.nl->GroupStart(), "ncclGroupStart", err);
+        for (int q = 0; q < S.world && !rc; q++) {
+            if (q == me) continue;
+            const int so = S.send_ns_off[p][q], sc = S.send_ns_off[p][q + 1] - so;
+            const int ro = S.recv_ns_off[p][q], rcnt = S.recv_ns_off[p][q + 1] - ro;
+            if (sc) rc = S.nccl_check(S.nl->Send(xs + (size_t)so * DIM, (size_t)sc * DIM, ncclFloat32, q, S.comm, s), "ncclSend", err);
+            if (!rc && rcnt) rc = S.nccl_check(S.nl->Recv(xr + (size_t)ro * DIM, (size_t)rcnt * DIM, ncclFloat32, q, S.comm, s), "ncclRecv", err);
+        }
+        const int rc_end = S.nccl_check(S.nl->GroupEnd(), "ncclGroupEnd", err);
+        if (rc || rc_end) return ERR_NCCL;
+        copy_rows_f32(xr, DIM, nullptr, dst, DIM, S.recv_ns[p].as<int>(), nrecv, DIM, s);
+        launches_++;
+    }
+    return OK;
+}
+
+int DitB200::shard_enqueue(cudaStream_t s) {
+    ShardState& S = *shard_;
+    const int TXT = S.TXT, n0 = S.plan.n_local(0);
+    launches_ = 0;
+    // vid_in (this rank's patches of the layer-0 layout) and txt_in, src/dit_vk.cpp:494-497
+    copy_rows_f32(S.VIDIN.as<float>(), PATCH_IN, S.tok0.as<int>(), S.VIDLOC.as<float>(), PATCH_IN, nullptr, n0,
+                  PATCH_IN, s);
+    pad_convert_rows(S.VIDLOC.as<float>(), n0, PATCH_IN, S.VPIN.p, PATCH_IN_PAD, act_, s);
+    pad_convert_rows(S.TXTIN.as<float>(), TXT, TXT_IN, S.TIN.p, TXT_IN, act_, s);
+    launches_ += 3;
+    GemmEpi e; e.mode = EPI_STORE; e.out_t = ACT_F32; e.ldo = DIM;
+    e.bias = vid_in_.bias(); e.out = S.X[0].p;
+    gemm(S.VPIN.p, PATCH_IN_PAD, vid_in_, n0, e, s);
+    e.bias = txt_in_.bias(); e.out = S.X[0].as<float>() + (size_t)n0 * DIM;
+    gemm(S.TIN.p, TXT_IN, txt_in_, TXT, e, s);
+    enqueue_temb(s);
+    for (int i = 0; i < NUM_LAYERS; i++) {
+        const int p = i % 2;
+        LayerBufs B;
+        B.X = S.X[p].as<float>(); B.Xn = S.Xn.p; B.QKV = S.QKV.p; B.ATT = S.ATT.p; B.Hs = S.Hs.p;
+        B.Qp = S.Qp.p; B.Kp = S.Kp.p; B.Vp = S.Vp.p; B.TOUTW = S.TOUTW.as<float>();
+        B.geom[0] = &S.geom[0]; B.geom[1] = &S.geom[1];
+        B.txt_sum = S.TXTSUM.as<float>(); B.txt_reduce = shard_txt_reduce; B.reduce_ctx = &S;
+        B.nwin_global[0] = S.nwin_global[0]; B.nwin_global[1] = S.nwin_global[1];
+        if (int rc = enqueue_layer_on(i, S.plan.n_local(p), TXT, s, B)) {
+            if (rc == ERR_NCCL) err = "ncclAllReduce of the txt attention sums failed";
+            return rc;
+        }
+        if (i + 1 < NUM_LAYERS)
+            if (int rc = shard_exchange(p, s)) return rc;
+    }
+    // final norm + vid_out_proj on this rank's rows (src/dit_vk.cpp:657-675),
+    // then every rank assembles the whole [Lv, 64] output
+    const int pl = (NUM_LAYERS - 1) % 2, nl = S.plan.n_local(pl);
+    const float* fin_sc = ada_.as<float>() + (size_t)(NUM_LAYERS * 12) * DIM;
+    rmsnorm_mod(S.X[pl].as<float>(), DIM, nl, nl, fin_sc, fin_sc + DIM, nullptr, nullptr, von_w_.as<float>(),
+                NORM_EPS, S.Xn.p, DIM, act_, s);
+    launches_++;
+    GemmEpi f; f.mode = EPI_STORE; f.out_t = ACT_F32; f.ldo = OUT_CH; f.bias = vid_out_.bias(); f.out = S.SRLOC.p;
+    gemm(S.Xn.p, DIM, vid_out_, nl, f, s);
+    cudaMemsetAsync(S.SRFULL.p, 0, (size_t)S.Lv * OUT_CH * 4, s);
+    copy_rows_f32(S.SRLOC.as<float>(), OUT_CH, nullptr, S.SRFULL.as<float>(), OUT_CH, S.tok1.as<int>(), nl, OUT_CH, s);
+    launches_++;
+    return S.nccl_check(S.nl->AllReduce(S.SRFULL.p, S.SRFULL.p, (size_t)S.Lv * OUT_CH, ncclFloat32, ncclSum, S.comm, s),
+                        "ncclAllReduce(sr)", err);
 }
 
 int DitB200::shard_forward(const float* vid_patch, int Lv, const float* txt, int TXT, float t, float* sr_out) {
-    (void)vid_patch; (void)Lv; (void)txt; (void)TXT; (void)t; (void)sr_out;
-    return fail(ERR_UNSUPPORTED, "window-sharded mode is not built yet");
+    if (!vid_patch || !txt || !sr_out) return fail(ERR_ARG, "null buffer");
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    cudaSetDevice(dev_);
+    if (int rc = shard_prepare(Lv, TXT)) return rc;
+    ShardState& S = *shard_;
+    float temb[TEMB_IN];
+    sinusoidal256(t, temb);
+    cudaMemcpyAsync(temb_in_.p, temb, sizeof temb, cudaMemcpyHostToDevice, stream_);
+    cudaMemcpyAsync(S.VIDIN.p, vid_patch, (size_t)Lv * PATCH_IN * 4, cudaMemcpyHostToDevice, stream_);
+    cudaMemcpyAsync(S.TXTIN.p, txt, (size_t)TXT * TXT_IN * 4, cudaMemcpyHostToDevice, stream_);
+    if (int rc = shard_enqueue(stream_)) {
+        cudaStreamSynchronize(stream_);
+        return rc;
+    }
+    cudaMemcpyAsync(sr_out, S.SRFULL.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToHost, stream_);
+    last_launches_ = launches_;
+    if (int rc = cuda_check(cudaGetLastError(), "kernel launch")) return rc;
+    return cuda_check(cudaStreamSynchronize(stream_), "shard_forward");
+}
+
+int DitB200::shard_forward_dev(const float* d_vid, int Lv, const float* d_txt, int TXT, float t, float* d_sr,
+                               cudaStream_t user) {
+    if (!d_vid || !d_txt || !d_sr) return fail(ERR_ARG, "null buffer");
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    cudaSetDevice(dev_);
+    if (int rc = shard_prepare(Lv, TXT)) return rc;
+    ShardState& S = *shard_;
+    cudaEvent_t ev_in, ev_out;
+    cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
+    cudaEventRecord(ev_in, user);
+    cudaStreamWaitEvent(stream_, ev_in, 0);
+    float temb[TEMB_IN];
+    sinusoidal256(t, temb);
+    cudaMemcpyAsync(temb_in_.p, temb, sizeof temb, cudaMemcpyHostToDevice, stream_);
+    cudaMemcpyAsync(S.VIDIN.p, d_vid, (size_t)Lv * PATCH_IN * 4, cudaMemcpyDeviceToDevice, stream_);
+    cudaMemcpyAsync(S.TXTIN.p, d_txt, (size_t)TXT * TXT_IN * 4, cudaMemcpyDeviceToDevice, stream_);
+    const int rc = shard_enqueue(stream_);
+    if (!rc) cudaMemcpyAsync(d_sr, S.SRFULL.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToDevice, stream_);
+    cudaEventRecord(ev_out, stream_);
+    cudaStreamWaitEvent(user, ev_out, 0);
+    cudaEventDestroy(ev_in);
+    cudaEventDestroy(ev_out);
+    last_launches_ = launches_;
+    if (rc) return rc;
+    return cuda_check(cudaGetLastError(), "shard_forward_dev");
 }
 
 }  // namespace s2b
 
 extern "C" int s2b_nccl_unique_id(uint8_t id[128]) {
-    (void)id;
-    return s2b::ERR_UNSUPPORTED;
+    if (!id) return s2b::ERR_ARG;
+    const s2b::NcclLib* nl = s2b::nccl_lib(nullptr);
+    if (!nl) return s2b::ERR_NCCL;
+    ncclUniqueId uid;
+    if (nl->GetUniqueId(&uid) != ncclSuccess) return s2b::ERR_NCCL;
+    std::memcpy(id, uid.internal, 128);
+    return s2b::OK;
 }

@@ -179,12 +179,14 @@ k_awa_attn_simt(const TP* __restrict__ Qp, const TP* __restrict__ Kp, const TP* 
 }
 
 template <typename TO>
-__global__ void k_coalesce(const float* __restrict__ toutw, int nwin, int TXT, TO* __restrict__ out, int ld) {
+__global__ void k_coalesce(const float* __restrict__ toutw, int nwin, int TXT, TO* __restrict__ out, int ld,
+                           float divisor) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= TXT * 2560) return;
     float s = 0.f;
     for (int w = 0; w < nwin; w++) s = __fadd_rn(s, toutw[(size_t)w * TXT * 2560 + i]);
-    out[(size_t)(i / 2560) * ld + (i % 2560)] = Cvt<TO>::from_f(__fdiv_rn(s, (float)nwin));
+    if (divisor > 0.f) s = __fdiv_rn(s, divisor);
+    out[(size_t)(i / 2560) * ld + (i % 2560)] = Cvt<TO>::from_f(s);
 }
 
 }  // namespace
@@ -242,10 +244,15 @@ int awa_init_device() {
 }
 
 void awa_coalesce(const float* toutw, int nwin, int TXT, void* att_txt, int ld_att, ActT at, cudaStream_t s) {
+    awa_coalesce_div(toutw, nwin, TXT, att_txt, ld_att, at, (float)nwin, s);
+}
+
+void awa_coalesce_div(const float* toutw, int nwin, int TXT, void* att_txt, int ld_att, ActT at, float divisor,
+                      cudaStream_t s) {
     const int n = TXT * 2560;
     if (n <= 0 || nwin <= 0) return;
-    if (at == ACT_F32) k_coalesce<float><<<(n + 255) / 256, 256, 0, s>>>(toutw, nwin, TXT, (float*)att_txt, ld_att);
-    else k_coalesce<bf16><<<(n + 255) / 256, 256, 0, s>>>(toutw, nwin, TXT, (bf16*)att_txt, ld_att);
+    if (at == ACT_F32) k_coalesce<float><<<(n + 255) / 256, 256, 0, s>>>(toutw, nwin, TXT, (float*)att_txt, ld_att, divisor);
+    else k_coalesce<bf16><<<(n + 255) / 256, 256, 0, s>>>(toutw, nwin, TXT, (bf16*)att_txt, ld_att, divisor);
 }
 
 }  // namespace s2b

@@ -59,6 +59,54 @@ k_rmsnorm_mod(const float* __restrict__ X, int ldx, int split, const float* __re
     store4(Y + (size_t)r * ldy + c1, yb);
 }
 
+// The same arithmetic with one warp per row: every lane keeps 20 float4 of
+// its row in registers (80 B of loads in flight per lane before the first
+// use), the sum of squares is reduced with warp shuffles only, and the
+// modulation vectors are read as float4.
+constexpr int NORM_ROWS = 4;   // rows (warps) per block
+template <typename TO>
+__global__ void __launch_bounds__(NORM_ROWS * 32, 3)
+k_rmsnorm_mod_w(const float* __restrict__ X, int ldx, int rows, int split, const float* __restrict__ sc0,
+                const float* __restrict__ sh0, const float* __restrict__ sc1, const float* __restrict__ sh1,
+                const float* __restrict__ affine, float eps, TO* __restrict__ Y, int ldy) {
+    constexpr int D = 2560, V = D / 128;
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * NORM_ROWS + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    const float4* x = reinterpret_cast<const float4*>(X + (size_t)r * ldx);
+    float4 v[V];
+    #pragma unroll
+    for (int k = 0; k < V; k++) v[k] = x[k * 32 + lane];
+    double s = 0;
+    #pragma unroll
+    for (int k = 0; k < V; k++)
+        s += (double)v[k].x * v[k].x + (double)v[k].y * v[k].y + (double)v[k].z * v[k].z + (double)v[k].w * v[k].w;
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float rr = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float)(s / D), eps)));
+    const float* sc = (r < split) ? sc0 : sc1;
+    const float* sh = (r < split) ? sh0 : sh1;
+    TO* y = Y + (size_t)r * ldy;
+    #pragma unroll
+    for (int k = 0; k < V; k++) {
+        const int c = (k * 32 + lane) * 4;
+        float u[4] = {__fmul_rn(v[k].x, rr), __fmul_rn(v[k].y, rr), __fmul_rn(v[k].z, rr), __fmul_rn(v[k].w, rr)};
+        if (affine) {
+            const float4 a = __ldg(reinterpret_cast<const float4*>(affine + c));
+            u[0] = __fmul_rn(u[0], a.x); u[1] = __fmul_rn(u[1], a.y); u[2] = __fmul_rn(u[2], a.z); u[3] = __fmul_rn(u[3], a.w);
+        }
+        if (sc) {
+            const float4 m = __ldg(reinterpret_cast<const float4*>(sc + c));
+            const float4 b = __ldg(reinterpret_cast<const float4*>(sh + c));
+            u[0] = __fadd_rn(__fmul_rn(u[0], m.x), b.x);
+            u[1] = __fadd_rn(__fmul_rn(u[1], m.y), b.y);
+            u[2] = __fadd_rn(__fmul_rn(u[2], m.z), b.z);
+            u[3] = __fadd_rn(__fmul_rn(u[3], m.w), b.w);
+        }
+        store4(y + c, u);
+    }
+}
+
 template <typename TO>
 __global__ void k_swiglu(const float* __restrict__ HG, int M, int ldhg, TO* __restrict__ Hs, int ldh) {
     // one thread per 4 outputs; HG column block b holds [h 128 | g 128]
@@ -114,6 +162,16 @@ __global__ void k_ingest(const void* __restrict__ src, bool f16, int out, int in
     dst[(size_t)dr * ld + c] = Cvt<TO>::from_f(v);
 }
 
+__global__ void k_copy_rows(const float* __restrict__ src, int ld_src, const int* __restrict__ src_idx,
+                            float* __restrict__ dst, int ld_dst, const int* __restrict__ dst_idx, int n, int width) {
+    const int r = blockIdx.x;
+    if (r >= n) return;
+    const int sr = src_idx ? src_idx[r] : r, dr = dst_idx ? dst_idx[r] : r;
+    const float4* a = reinterpret_cast<const float4*>(src + (size_t)sr * ld_src);
+    float4* b = reinterpret_cast<float4*>(dst + (size_t)dr * ld_dst);
+    for (int c = threadIdx.x; c < width / 4; c += blockDim.x) b[c] = a[c];
+}
+
 template <typename TI>
 __global__ void k_to_f32(const TI* __restrict__ src, size_t n, float* __restrict__ dst) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -126,6 +184,19 @@ void rmsnorm_mod(const float* X, int ldx, int rows, int split, const float* sc0,
                  const float* sc1, const float* sh1, const float* affine, float eps, void* Y, int ldy,
                  ActT yt, cudaStream_t s) {
     if (rows <= 0) return;
+    // float4 paths need 16-byte aligned rows and vectors (always true for the
+    // 2560-wide buffers this library allocates)
+    const bool vec = ((uintptr_t)X % 16 == 0) && ldx % 4 == 0 && ldy % 4 == 0 && ((uintptr_t)Y % 16 == 0) &&
+                     ((uintptr_t)sc0 % 16 == 0) && ((uintptr_t)sh0 % 16 == 0) && ((uintptr_t)sc1 % 16 == 0) &&
+                     ((uintptr_t)sh1 % 16 == 0) && ((uintptr_t)affine % 16 == 0);
+    if (vec) {
+        const int blocks = (rows + NORM_ROWS - 1) / NORM_ROWS;
+        if (yt == ACT_F32)
+            k_rmsnorm_mod_w<float><<<blocks, NORM_ROWS * 32, 0, s>>>(X, ldx, rows, split, sc0, sh0, sc1, sh1, affine, eps, (float*)Y, ldy);
+        else
+            k_rmsnorm_mod_w<bf16><<<blocks, NORM_ROWS * 32, 0, s>>>(X, ldx, rows, split, sc0, sh0, sc1, sh1, affine, eps, (bf16*)Y, ldy);
+        return;
+    }
     if (yt == ACT_F32)
         k_rmsnorm_mod<float><<<rows, NORM_THREADS, 0, s>>>(X, ldx, split, sc0, sh0, sc1, sh1, affine, eps, (float*)Y, ldy);
     else
@@ -163,6 +234,12 @@ void convert_to_f32(const void* src, ActT t, size_t n, float* dst, cudaStream_t 
     const int blocks = (int)((n + 255) / 256);
     if (t == ACT_F32) cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToDevice, s);
     else k_to_f32<bf16><<<blocks, 256, 0, s>>>((const bf16*)src, n, dst);
+}
+
+void copy_rows_f32(const float* src, int ld_src, const int* src_idx, float* dst, int ld_dst, const int* dst_idx,
+                   int n, int width, cudaStream_t s) {
+    if (n <= 0) return;
+    k_copy_rows<<<n, 160, 0, s>>>(src, ld_src, src_idx, dst, ld_dst, dst_idx, n, width);
 }
 
 void ingest_weight(const void* src, bool src_f16, int out, int in, void* dst, ActT t, int ld, int blk_rows,

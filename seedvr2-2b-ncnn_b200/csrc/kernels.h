@@ -111,5 +111,13 @@ void awa_attend(const void* Qp, const void* Kp, const void* Vp, ActT pt, const A
                 void* att, int ld_att, ActT at, float* toutw, cudaStream_t s, int* launches);
 // att_txt[i, d] = sum_w toutw[w][i][d] / nwin
 void awa_coalesce(const float* toutw, int nwin, int TXT, void* att_txt, int ld_att, ActT at, cudaStream_t s);
+// att_txt = sum_w toutw[w] / divisor (divisor <= 0: the plain sum)
+void awa_coalesce_div(const float* toutw, int nwin, int TXT, void* att_txt, int ld_att, ActT at, float divisor,
+                      cudaStream_t s);
+// dst rows (stride ld_dst) = src rows (stride ld_src), element gather/scatter of
+// whole 2560-wide fp32 rows: dst[dst_idx[i]] = src[src_idx[i]] for i < n
+// (a null index array means the identity).
+void copy_rows_f32(const float* src, int ld_src, const int* src_idx, float* dst, int ld_dst, const int* dst_idx,
+                   int n, int width, cudaStream_t s);
 
 }  // namespace s2b

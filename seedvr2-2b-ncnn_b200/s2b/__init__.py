@@ -87,6 +87,11 @@ def lib() -> ctypes.CDLL:
         "s2b_nccl_unique_id": [ctypes.POINTER(ctypes.c_uint8)],
         "s2b_shard_init": [vp, ctypes.POINTER(ctypes.c_uint8), ip, ip],
         "s2b_shard_forward": [vp, _F32P, ip, _F32P, ip, ctypes.c_float, _F32P],
+        "s2b_shard_forward_dev": [vp, vp, ip, vp, ip, ctypes.c_float, vp, vp],
+        "s2b_shard_forward_profile": [vp, _F32P, ip, _F32P, ip, ctypes.c_float, ctypes.POINTER(ctypes.c_double),
+                                      ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), _I32P],
+        "s2b_shard_plan": [ctypes.POINTER(s2b_win), ctypes.POINTER(s2b_win), ip, ip, _I32P, _I32P, _I32P, _I32P,
+                           _I32P, _I32P, _I32P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -165,6 +170,58 @@ def make_win(t: int, h: int, w: int, num_windows=(4, 3, 3), txt_len: int = 58, s
 
 
 # ---------------------------------------------------------------- synthetic data
+def _same_nccl_as_torch():
+    """The library resolves libnccl.so.2 at run time; importing torch first
+    makes that the copy torch.distributed uses, so every process of a job
+    (and torch's own process group) runs one NCCL version."""
+    try:
+        import torch  # noqa: F401
+    except ImportError:
+        pass
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh ncclUniqueId (rank 0 creates it and shares it with the others)."""
+    _same_nccl_as_torch()
+    buf = (ctypes.c_uint8 * 128)()
+    rc = lib().s2b_nccl_unique_id(buf)
+    if rc != 0:
+        raise S2BError(rc, "ncclGetUniqueId failed (is libnccl.so.2 loadable?)")
+    return bytes(buf)
+
+
+@dataclass
+class ShardPlan:
+    """Window ownership / residual exchange plan of one rank (s2b_shard_plan)."""
+    bounds: list        # [2] arrays of world+1 window boundaries
+    tokens: list        # [2] grid token of every local row
+    send_off: list
+    send_idx: list
+    recv_off: list
+    recv_idx: list
+
+
+def shard_plan(ns: Win, sh: Win, world: int, rank: int) -> ShardPlan:
+    Lv = ns.t * ns.h * ns.w
+    a, b = ns.as_c(), sh.as_c()
+    bounds = np.zeros((2, world + 1), np.int32)
+    n_local = np.zeros(2, np.int32)
+    tokens = np.zeros((2, Lv), np.int32)
+    soff, roff = np.zeros((2, world + 1), np.int32), np.zeros((2, world + 1), np.int32)
+    sidx, ridx = np.zeros((2, Lv), np.int32), np.zeros((2, Lv), np.int32)
+    P = lambda x: x.ctypes.data_as(_I32P)
+    rc = lib().s2b_shard_plan(ctypes.byref(a), ctypes.byref(b), world, rank, P(bounds), P(n_local), P(tokens),
+                              P(soff), P(sidx), P(roff), P(ridx))
+    if rc != 0:
+        raise S2BError(rc, "s2b_shard_plan rejected the geometry")
+    n = [int(n_local[0]), int(n_local[1])]
+    return ShardPlan(bounds=[bounds[p].copy() for p in range(2)], tokens=[tokens[p, :n[p]].copy() for p in range(2)],
+                     send_off=[soff[p].copy() for p in range(2)],
+                     send_idx=[sidx[p, :soff[p, -1]].copy() for p in range(2)],
+                     recv_off=[roff[p].copy() for p in range(2)],
+                     recv_idx=[ridx[p, :roff[p, -1]].copy() for p in range(2)])
+
+
 def synth_write_m5(path: str, seed: int, layer_lo: int = 0, layer_hi: int = NUM_LAYERS):
     _check(None, lib().s2b_synth_write_m5(path.encode(), seed, layer_lo, layer_hi))
 
@@ -296,13 +353,33 @@ class DitB200:
 
     KERNEL_KINDS = ("gemm_tcgen05", "gemm_fp32", "attention", "awa_pack", "norm_convert", "other")
 
-    def forward_profile(self, vid_patch, Lv, txt, TXT, timestep=1000.0) -> dict:
-        """Per kernel class: device ms, algorithmic FLOPs / bytes, launches (CUDA events)."""
+    def forward_profile(self, vid_patch, Lv, txt, TXT, timestep=1000.0, sharded=False) -> dict:
+        """Per kernel class: device ms, algorithmic FLOPs / bytes, launches (CUDA events).
+        sharded: this rank's part of the window-sharded forward."""
         v, t = _f32(vid_patch), _f32(txt)
         D6 = ctypes.c_double * 6
         ms, fl, by, n = D6(), D6(), D6(), (ctypes.c_int * 6)()
-        self._c(lib().s2b_forward_profile(self._ctx, _p(v), Lv, _p(t), TXT, timestep, ms, fl, by, n))
+        fn = lib().s2b_shard_forward_profile if sharded else lib().s2b_forward_profile
+        self._c(fn(self._ctx, _p(v), Lv, _p(t), TXT, timestep, ms, fl, by, n))
         return {k: dict(ms=ms[i], flops=fl[i], bytes=by[i], launches=n[i]) for i, k in enumerate(self.KERNEL_KINDS)}
+
+    # ---- window-sharded image mode (one rank per GPU, NCCL)
+    def shard_init(self, nccl_id: bytes, world: int, rank: int):
+        """Joins the window-sharded group (every rank calls it together)."""
+        if len(nccl_id) != 128:
+            raise ValueError("nccl_id must be 128 bytes")
+        _same_nccl_as_torch()
+        buf = (ctypes.c_uint8 * 128).from_buffer_copy(nccl_id)
+        self._c(lib().s2b_shard_init(self._ctx, buf, world, rank))
+
+    def shard_forward(self, vid_patch, Lv, txt, TXT, timestep=1000.0):
+        v, t = _f32(vid_patch), _f32(txt)
+        sr = np.zeros((Lv, OUT_CH), np.float32)
+        self._c(lib().s2b_shard_forward(self._ctx, _p(v), Lv, _p(t), TXT, timestep, _p(sr)))
+        return sr
+
+    def shard_forward_dev(self, d_vid: int, Lv: int, d_txt: int, TXT: int, timestep: float, d_sr: int, stream: int):
+        self._c(lib().s2b_shard_forward_dev(self._ctx, d_vid, Lv, d_txt, TXT, timestep, d_sr, stream))
 
     def last_launches(self) -> int:
         n = ctypes.c_int()

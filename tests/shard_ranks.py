@@ -1,0 +1,97 @@
+"""Per-rank bodies of the window-sharded tests (run in spawned processes).
+
+gloo_exchange: replays the residual exchange of the library's shard plan
+(s2b_shard_plan) between CPU ranks over gloo, for both layer-parity
+transitions, plus the txt partial-sum all-reduce, and records what each rank
+ends up holding.
+
+nccl_forward: one rank per GPU, the library's own window-sharded forward
+(s2b_shard_init / s2b_shard_forward) on synthetic weights; rank 0 also runs
+the single-GPU forward of the same inputs for comparison.
+"""
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+for _p in (os.path.join(ROOT, "seedvr2-2b-ncnn_b200"), ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+
+def gloo_exchange(rank: int, world: int, port: int, grid, out_dir: str):
+    import torch
+    import torch.distributed as dist
+    import s2b
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        T, H, W = grid
+        Lv, width = T * H * W, 8
+        ns = s2b.make_win(T, H, W, (4, 3, 3), 58, False)
+        sh = s2b.make_win(T, H, W, (4, 3, 3), 58, True)
+        plan = s2b.shard_plan(ns, sh, world, rank)
+        # global residual: row tok holds (tok, tok * 0.5, ...) so misplaced rows show
+        glob = (np.arange(Lv, dtype=np.float32)[:, None] * np.linspace(1, 2, width, dtype=np.float32)[None, :])
+        cur = torch.from_numpy(glob[plan.tokens[0]].copy())
+        held = []
+        for p in (0, 1):
+            q1 = 1 - p
+            nxt = torch.full((len(plan.tokens[q1]), width), -1.0)
+            so, si, ro, ri = plan.send_off[p], plan.send_idx[p], plan.recv_off[p], plan.recv_idx[p]
+            reqs = []
+            for q in range(world):
+                rows = torch.from_numpy(si[so[q]:so[q + 1]].astype(np.int64))
+                dst = torch.from_numpy(ri[ro[q]:ro[q + 1]].astype(np.int64))
+                if q == rank:
+                    nxt[dst] = cur[rows]
+                    continue
+                if len(rows):
+                    reqs.append(dist.isend(cur[rows].contiguous(), q))
+            for q in range(world):
+                if q == rank:
+                    continue
+                dst = torch.from_numpy(ri[ro[q]:ro[q + 1]].astype(np.int64))
+                if len(dst):
+                    buf = torch.empty((len(dst), width))
+                    dist.recv(buf, q)
+                    nxt[dst] = buf
+            for r in reqs:
+                r.wait()
+            held.append(nxt.numpy().copy())
+            cur = nxt
+        # txt partial sums: each rank sums its windows' contributions, one all-reduce
+        nwin0 = int(plan.bounds[0][-1])
+        contrib = np.stack([np.full((4,), w + 1.0, np.float32) for w in range(nwin0)])
+        a, b = int(plan.bounds[0][rank]), int(plan.bounds[0][rank + 1])
+        part = torch.from_numpy(contrib[a:b].sum(0))
+        dist.all_reduce(part)
+        np.savez(os.path.join(out_dir, f"rank{rank}.npz"), after0=held[0], after1=held[1],
+                 tok0=plan.tokens[0], tok1=plan.tokens[1], txt=part.numpy(), glob=glob)
+    finally:
+        dist.destroy_process_group()
+
+
+def nccl_forward(rank: int, world: int, uid: bytes, prec: int, grid, out_dir: str):
+    import s2b
+    T, H, W = grid
+    Lv, TXT = T * H * W, 58
+    ctx = s2b.DitB200(rank, prec)
+    try:
+        ctx.init_synth(1234)
+        ns = s2b.make_win(T, H, W, (4, 3, 3), TXT, False)
+        sh = s2b.make_win(T, H, W, (4, 3, 3), TXT, True)
+        ctx.set_windows(ns, sh)
+        vid = s2b.patchify_grid(s2b.synth_vid_grid(T, 2 * H, 2 * W, 42))
+        txt = s2b.synth_txt(TXT, 7)
+        ctx.shard_init(uid, world, rank)
+        sr = ctx.shard_forward(vid, Lv, txt, TXT, 1000.0)
+        sr2 = ctx.shard_forward(vid, Lv, txt, TXT, 1000.0)
+        out = dict(sr=sr, sr2=sr2)
+        if rank == 0:
+            out["single"] = ctx.forward(vid, Lv, txt, TXT, 1000.0)
+        np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **out)
+    finally:
+        ctx.close()
