@@ -24,10 +24,13 @@
 #include "kcommon.cuh"
 #include "sm100.cuh"
 #include <cuda.h>
+#include <cstdlib>
 
 namespace s2b {
 
 bool make_tmap_bf16(CUtensorMap* m, const void* base, int rows, int cols, int ld, int box_rows, int box_cols);
+int awa_tc_kernel_version();
+int awa_tc_poly_exp();
 
 namespace {
 
@@ -291,6 +294,333 @@ k_awa_attn_tc(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CU
     }
 }
 
+
+// ---------------------------------------------------------------- two-tile kernel
+// One CTA per SM = one (window, head) and two 128-query tiles that share every
+// K/V tile.  TMEM holds S_0, S_1 (128 columns each) and O_0, O_1 (128 each):
+// all 512 columns.  P_t is written back over S_t's first 64 columns as packed
+// bf16 pairs and is the TMEM A operand of O_t += P_t V.  K and V stream
+// through two-stage TMA rings.  Roles:
+//   warps 0-3 / 4-7  softmax + epilogue of tile 0 / tile 1 (thread = query row)
+//   warp 8 lane 0    TMA producer
+//   warp 9 lane 0    MMA issuer; order per key tile j:
+//                      PV_0(j), S_0(j+1), PV_1(j), S_1(j+1)
+//                    so tile 0's next scores run while tile 1's softmax does
+//                    and the other way round.  S_t(j+1) is issued only after
+//                    PV_t(j) has completed (it reads P_t from S_t's columns).
+// Running max: a row keeps the max its exponentials use until a tile's max
+// exceeds it by more than 8 (log2 units); only then O and l are rescaled, so
+// P <= 2^8 and most tiles skip the O read-modify-write in TMEM.
+constexpr int T2_THREADS = 320;
+constexpr int T2_SMEM = 6 * TILE_BYTES + 1024 + 512;
+constexpr float T2_RESCALE = 8.f;
+
+struct Attn2Ctl {
+    uint64_t q_full, k_full[2], v_full[2], k_empty[2], v_empty[2];
+    uint64_t s_full[2], p_ready[2], pv_done[2], drain;
+    uint32_t tmem_slot;
+    int abort;
+};
+
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t r[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+          "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+          "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+// 2^x with the hardware approximation (MUFU, flush-to-zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// 2^x on the FMA/ALU pipes, for x <= ~8 (softmax exponents): Cody-Waite
+// split x = j + f with j = round(x) (adding 1.5 * 2^23 rounds to an integer
+// in the low mantissa bits) and |f| <= 1/2, 2^f by a cubic fitted here by
+// relative least squares on Chebyshev nodes of [-1/2, 1/2] (max relative
+// error 7.7e-5, below bf16's 2^-9 rounding of P), and 2^j added to the
+// exponent field.  x is clamped at -120 so the exponent stays normal.
+__device__ __forceinline__ float ex2_poly(float x) {
+    x = fmaxf(x, -120.f);
+    const float t = __fadd_rn(x, 12582912.f);
+    const int j = __float_as_int(t) - 0x4B400000;
+    const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
+    float p = fmaf(f, 0.05508868396282196f, 0.24260404706001282f);
+    p = fmaf(f, p, 0.6932762265205383f);
+    p = fmaf(f, p, 0.9999289512634277f);
+    return __int_as_float(__float_as_int(p) + (j << 23));
+}
+
+template <bool POLY>
+__global__ void __launch_bounds__(T2_THREADS, 1)
+k_awa_attn_tc2(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
+               const __grid_constant__ CUtensorMap tV, const AttnParams p) {
+    const int wi = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * 2 * QT;
+    const int f = p.g.cumf[wi + 1] - p.g.cumf[wi];
+    const int S = f + p.g.TXT;
+    if (q0 >= S) return;                       // uniform across the CTA, before any barrier
+    const int nt = (q0 + QT < S) ? 2 : 1;      // query tiles of this CTA
+    const int nkt = (S + KT - 1) / KT;
+    const int row_base = h * p.g.sumS + p.g.cums[wi];
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;                        // [2] tiles
+    uint8_t* sK = smem + 2 * TILE_BYTES;       // [2] stages
+    uint8_t* sV = smem + 4 * TILE_BYTES;       // [2] stages
+    Attn2Ctl* ctl = reinterpret_cast<Attn2Ctl*>(smem + 6 * TILE_BYTES);
+    volatile int* abort_flag = &ctl->abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(&ctl->q_full, 1);
+        for (int i = 0; i < 2; i++) {
+            sm100::mbar_init(&ctl->k_full[i], 1);
+            sm100::mbar_init(&ctl->v_full[i], 1);
+            sm100::mbar_init(&ctl->k_empty[i], 1);
+            sm100::mbar_init(&ctl->v_empty[i], 1);
+            sm100::mbar_init(&ctl->s_full[i], 1);
+            sm100::mbar_init(&ctl->p_ready[i], 4);
+            sm100::mbar_init(&ctl->pv_done[i], 1);
+        }
+        sm100::mbar_init(&ctl->drain, 1);
+        ctl->abort = 0;
+        sm100::fence_barrier_init();
+    }
+    if (warp == 9) {
+        sm100::tmem_alloc(&ctl->tmem_slot, 512);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = ctl->tmem_slot;
+
+    if (warp == 8) {
+        if (lane == 0) {
+            // ---- TMA producer
+            int issued = 0;
+            bool ok = true;
+            sm100::mbar_arrive_expect_tx(&ctl->q_full, nt * TILE_BYTES);
+            for (int t = 0; t < nt; t++) {
+                sm100::tma_load_2d(sQ + t * TILE_BYTES, &tQ, &ctl->q_full, 0, row_base + q0 + t * QT);
+                sm100::tma_load_2d(sQ + t * TILE_BYTES + HALF_BYTES, &tQ, &ctl->q_full, 64, row_base + q0 + t * QT);
+            }
+            for (int j = 0; j < nkt && ok; j++) {
+                const int st = j & 1;
+                const uint32_t eph = (uint32_t)((j >> 1) - 1) & 1;
+                const int r = row_base + j * KT;
+                if (j >= 2 && !(ok = wait_bar(&ctl->k_empty[st], eph, abort_flag))) break;
+                sm100::mbar_arrive_expect_tx(&ctl->k_full[st], TILE_BYTES);
+                sm100::tma_load_2d(sK + st * TILE_BYTES, &tK, &ctl->k_full[st], 0, r);
+                sm100::tma_load_2d(sK + st * TILE_BYTES + HALF_BYTES, &tK, &ctl->k_full[st], 64, r);
+                if (j >= 2 && !(ok = wait_bar(&ctl->v_empty[st], eph, abort_flag))) { issued = 2 * j + 1; break; }
+                sm100::mbar_arrive_expect_tx(&ctl->v_full[st], TILE_BYTES);
+                sm100::tma_load_2d(sV + st * TILE_BYTES, &tV, &ctl->v_full[st], 0, r);
+                sm100::tma_load_2d(sV + st * TILE_BYTES + HALF_BYTES, &tV, &ctl->v_full[st], 64, r);
+                issued = 2 * j + 2;
+            }
+            if (!ok) {
+                // drain this thread's own TMA loads (bounded) before shared memory is released
+                for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->q_full, 0); w++) {}
+                for (int k = (issued > 4 ? issued - 4 : 0); k < issued; k++) {
+                    const int j = k >> 1, st = j & 1;
+                    uint64_t* b = (k & 1) ? &ctl->v_full[st] : &ctl->k_full[st];
+                    for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(b, (uint32_t)(j >> 1) & 1); w++) {}
+                }
+            }
+        }
+    } else if (warp == 9) {
+        if (lane == 0) {
+            // ---- MMA issuer
+            bool ok = wait_bar(&ctl->q_full, 0, abort_flag);
+            auto issue_s = [&](int t, int j) {
+                const uint8_t* k = sK + (j & 1) * TILE_BYTES;
+                const uint8_t* q = sQ + t * TILE_BYTES;
+                #pragma unroll
+                for (int kk = 0; kk < D / 16; kk++) {
+                    const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
+                    sm100::mma_bf16(tmem + t * 128, sm100::desc_kmajor_sw128(q, off), sm100::desc_kmajor_sw128(k, off),
+                                    IDESC_QK, kk != 0);
+                }
+                sm100::mma_commit(&ctl->s_full[t]);
+            };
+            auto issue_pv = [&](int t, int j) {
+                const uint8_t* v = sV + (j & 1) * TILE_BYTES;
+                #pragma unroll
+                for (int kk = 0; kk < KT / 16; kk++)
+                    sm100::mma_bf16_tmem_a(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, desc_mnmajor_sw128(v, kk * 2048),
+                                           IDESC_PV, (j | kk) != 0);
+                sm100::mma_commit(&ctl->pv_done[t]);
+            };
+            if (ok && (ok = wait_bar(&ctl->k_full[0], 0, abort_flag))) {
+                sm100::tc_fence_after();
+                for (int t = 0; t < nt; t++) issue_s(t, 0);
+                sm100::mma_commit(&ctl->k_empty[0]);
+            }
+            for (int j = 0; j < nkt && ok; j++) {
+                const int st = j & 1;
+                const uint32_t ph = (uint32_t)(j >> 1) & 1;
+                const bool more = j + 1 < nkt;
+                if (!(ok = wait_bar(&ctl->v_full[st], ph, abort_flag))) break;
+                if (more && !(ok = wait_bar(&ctl->k_full[st ^ 1], (uint32_t)((j + 1) >> 1) & 1, abort_flag))) break;
+                for (int t = 0; t < nt && ok; t++) {
+                    if (!(ok = wait_bar(&ctl->p_ready[t], (uint32_t)j & 1, abort_flag))) break;
+                    sm100::tc_fence_after();
+                    issue_pv(t, j);
+                    if (more) {
+                        // S_t(j+1) overwrites P_t(j): wait for PV_t(j) to finish reading it
+                        if (!(ok = wait_bar(&ctl->pv_done[t], (uint32_t)j & 1, abort_flag))) break;
+                        sm100::tc_fence_after();
+                        issue_s(t, j + 1);
+                    }
+                }
+                if (!ok) break;
+                if (more) sm100::mma_commit(&ctl->k_empty[st ^ 1]);
+                sm100::mma_commit(&ctl->v_empty[st]);
+            }
+            // all of this thread's MMAs done before TMEM / shared memory go away
+            sm100::mma_commit(&ctl->drain);
+            for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->drain, 0); w++) {}
+        }
+    } else {
+        // ---- softmax + epilogue: tile t = warp / 4, row r of the tile
+        const int t = warp >> 2;
+        const int r = (warp & 3) * 32 + lane;
+        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t tS = tmem + t * 128 + lane_off, tO = tmem + 256 + t * 128 + lane_off;
+        if (t < nt) {
+            float m = -INFINITY, l = 0.f;
+            bool ok = true;
+            // tcgen05.ld / st are warp-collective: control flow stays warp-uniform
+            for (int j = 0; j < nkt; j++) {
+                ok = __all_sync(0xffffffffu, wait_bar(&ctl->s_full[t], (uint32_t)j & 1, abort_flag));
+                if (!ok) break;
+                sm100::tc_fence_after();
+                const int kvalid = S - j * KT;
+                const bool full = kvalid >= KT;        // CTA-uniform
+                const float sl = p.scale_log2;
+                // pass 1: row max of the scaled, masked scores (scale > 0)
+                float mr = -INFINITY;
+                #pragma unroll
+                for (int c = 0; c < 2; c++) {
+                    float v[64];
+                    sm100::tmem_ld64(tS + c * 64, v);
+                    if (full) {
+                        #pragma unroll
+                        for (int u = 0; u < 64; u++) mr = fmaxf(mr, v[u]);
+                    } else {
+                        #pragma unroll
+                        for (int u = 0; u < 64; u++)
+                            if (c * 64 + u < kvalid) mr = fmaxf(mr, v[u]);
+                    }
+                }
+                const float mx = mr * sl;
+                if (j == 0) {
+                    m = mx;
+                } else {
+                    const bool grow = mx > m + T2_RESCALE;
+                    if (__any_sync(0xffffffffu, grow)) {
+                        // PV_t(j-1) is complete: S_t(j) was issued after it finished
+                        const float mn = grow ? mx : m;
+                        const float corr = exp2f(m - mn);
+                        #pragma unroll 1
+                        for (int c = 0; c < 4; c++) {
+                            float o[32];
+                            sm100::tmem_ld32(tO + c * 32, o);
+                            #pragma unroll
+                            for (int u = 0; u < 32; u++) o[u] *= corr;
+                            tmem_st32(tO + c * 32, o);
+                        }
+                        l *= corr;
+                        m = mn;
+                    }
+                }
+                // pass 2: P_t(j) as packed bf16 pairs over S_t's columns [0, 64);
+                // keys [64h, 64h+64) land in columns [32h, 32h+32), which
+                // pass 2 has already read
+                const float nm = -m;
+                #pragma unroll
+                for (int hlf = 0; hlf < 2; hlf++) {
+                    float v[64];
+                    sm100::tmem_ld64(tS + hlf * 64, v);
+                    uint32_t pk[32];
+                    if (full) {
+                        #pragma unroll
+                        for (int u = 0; u < 32; u++) {
+                            const float xa = fmaf(v[2 * u], sl, nm), xb = fmaf(v[2 * u + 1], sl, nm);
+                            float a, b;
+                            if (POLY && (u & 3) == 3) { a = ex2_poly(xa); b = ex2_poly(xb); }
+                            else { a = ex2_approx(xa); b = ex2_approx(xb); }
+                            l += a + b;
+                            __nv_bfloat162 v2 = __floats2bfloat162_rn(a, b);
+                            pk[u] = *reinterpret_cast<uint32_t*>(&v2);
+                        }
+                    } else {
+                        #pragma unroll
+                        for (int u = 0; u < 32; u++) {
+                            const int k = hlf * 64 + 2 * u;
+                            const float a = (k < kvalid) ? ex2_approx(fmaf(v[2 * u], sl, nm)) : 0.f;
+                            const float b = (k + 1 < kvalid) ? ex2_approx(fmaf(v[2 * u + 1], sl, nm)) : 0.f;
+                            l += a + b;
+                            __nv_bfloat162 v2 = __floats2bfloat162_rn(a, b);
+                            pk[u] = *reinterpret_cast<uint32_t*>(&v2);
+                        }
+                    }
+                    tmem_st32u(tS + hlf * 32, pk);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                sm100::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) sm100::mbar_arrive(&ctl->p_ready[t]);
+            }
+            if (ok) ok = __all_sync(0xffffffffu, wait_bar(&ctl->pv_done[t], (uint32_t)(nkt - 1) & 1, abort_flag));
+            if (ok) {
+                sm100::tc_fence_after();
+                const int q = q0 + t * QT + r;
+                const float inv = 1.f / l;
+                const bool is_vid = q < f, is_txt = (q >= f) && (q < S);
+                float* tdst = p.toutw + ((size_t)wi * p.g.TXT + (is_txt ? q - f : 0)) * 2560 + h * D;
+                const size_t tok = is_vid ? (size_t)p.g.vidx[p.g.cumf[wi] + q] : 0;
+                #pragma unroll 1
+                for (int c = 0; c < 4; c++) {
+                    float o[32];
+                    sm100::tmem_ld32(tO + c * 32, o);
+                    #pragma unroll
+                    for (int u = 0; u < 32; u++) o[u] *= inv;
+                    if (is_vid) {
+                        if (p.att_bf16) {
+                            bf16* dst = (bf16*)p.att + tok * p.ld_att + h * D + c * 32;
+                            #pragma unroll
+                            for (int u = 0; u < 32; u += 4) store4(dst + u, o + u);
+                        } else {
+                            float* dst = (float*)p.att + tok * p.ld_att + h * D + c * 32;
+                            #pragma unroll
+                            for (int u = 0; u < 32; u += 4) store4(dst + u, o + u);
+                        }
+                    } else if (is_txt) {
+                        #pragma unroll
+                        for (int u = 0; u < 32; u += 4) store4(tdst + c * 32 + u, o + u);
+                    }
+                }
+            }
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (warp == 9) {
+        sm100::tc_fence_after();
+        sm100::tmem_dealloc(tmem, 512);
+    }
+}
+
 }  // namespace
 
 bool awa_tc_available() { return true; }
@@ -309,13 +639,45 @@ int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, const AwaDev& 
     p.ld_att = ld_att;
     p.att_bf16 = (at == ACT_BF16);
     p.toutw = toutw;
-    dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
-    k_awa_attn_tc<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(tq, tk, tv, p);
+    if (awa_tc_kernel_version() == 1) {
+        dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
+        k_awa_attn_tc<<<grid, NUM_THREADS, SMEM_BYTES, s>>>(tq, tk, tv, p);
+    } else {
+        dim3 grid((g.maxS + 2 * QT - 1) / (2 * QT), 20, g.nwin);
+        if (awa_tc_poly_exp())
+            k_awa_attn_tc2<true><<<grid, T2_THREADS, T2_SMEM, s>>>(tq, tk, tv, p);
+        else
+            k_awa_attn_tc2<false><<<grid, T2_THREADS, T2_SMEM, s>>>(tq, tk, tv, p);
+    }
     return 0;
 }
 
 int awa_tc_init_device() {
-    return (int)cudaFuncSetAttribute(k_awa_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES))
+        return (int)e;
+    if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc2<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, T2_SMEM))
+        return (int)e;
+    return (int)cudaFuncSetAttribute(k_awa_attn_tc2<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, T2_SMEM);
+}
+
+// A quarter of the softmax exponentials on the FMA pipe (ex2_poly) unless
+// S2B_ATTN_POLY=0.
+int awa_tc_poly_exp() {
+    static const int v = [] {
+        const char* e = std::getenv("S2B_ATTN_POLY");
+        return (e && e[0] == '0') ? 0 : 1;
+    }();
+    return v;
+}
+
+// 1 = one 128-query tile per CTA, two CTAs per SM (default); 2 = the
+// two-tile kernel (S2B_ATTN_KERNEL=2).
+int awa_tc_kernel_version() {
+    static const int v = [] {
+        const char* e = std::getenv("S2B_ATTN_KERNEL");
+        return (e && e[0] == '2') ? 2 : 1;
+    }();
+    return v;
 }
 
 int awa_tc_error_reset(int* had_error) {

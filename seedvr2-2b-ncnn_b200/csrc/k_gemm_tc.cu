@@ -31,6 +31,7 @@
 #include "kcommon.cuh"
 #include "sm100.cuh"
 #include <cuda.h>
+#include <cstring>
 #include <mutex>
 
 namespace s2b {
@@ -42,25 +43,29 @@ constexpr int ACC_COLS = 256, NUM_ACC = 2, TMEM_COLS = ACC_COLS * NUM_ACC;
 // single-CTA kernel
 constexpr int BM1 = 128, BN1 = 256, STAGES1 = 4;
 constexpr int A1_BYTES = BM1 * BK * 2, B1_BYTES = BN1 * BK * 2, STAGE1_BYTES = A1_BYTES + B1_BYTES;
-constexpr int SMEM1_BYTES = STAGES1 * STAGE1_BYTES + 1024 + 256;
+// gate/residual epilogue staging: per epilogue warp two 32x32 fp32 boxes
+constexpr int RBOX_BYTES = 32 * 32 * 4, RES_BYTES = 4 * 2 * RBOX_BYTES;
+constexpr int SMEM1_BYTES = STAGES1 * STAGE1_BYTES + RES_BYTES + 1024 + 512;
 constexpr uint32_t IDESC1 = sm100::idesc_bf16_f32(BM1, BN1);
 
 // CTA-pair kernel: per CTA 128 rows of A and 128 rows of B per stage
 constexpr int BM2 = 256, BN2 = 256, STAGES2 = 6;
 constexpr int A2_BYTES = 128 * BK * 2, B2_BYTES = 128 * BK * 2, STAGE2_BYTES = A2_BYTES + B2_BYTES;
-constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + RES_BYTES + 1024 + 512;
 constexpr uint32_t IDESC2 = sm100::idesc_bf16_f32(BM2, BN2);
 
 __device__ int g_tc_err;
 
 struct TcParams {
     int M, N, num_m, num_n, num_kb;
+    int resid_tma;       // EPI_GATE_RESID through TMA-staged residual boxes
     GemmEpi e;
 };
 
 template <int STAGES>
 struct Ctl {
     uint64_t full[STAGES], empty[STAGES], tfull[NUM_ACC], tempty[NUM_ACC];
+    uint64_t rfull[4][2];      // residual boxes, per epilogue warp
     uint32_t tmem_slot;
     int abort;
 };
@@ -93,8 +98,9 @@ __device__ __forceinline__ void store32(bf16* dst, const float v[32]) {
 
 // Pull this thread's residual row segment of a tile into L2 ahead of its
 // epilogue (8 x 128-B lines of fp32).
+template <int MODE>
 __device__ __forceinline__ void prefetch_resid(const TcParams& p, int row, int n0) {
-    if (p.e.mode != EPI_GATE_RESID || row >= p.M) return;
+    if (MODE != EPI_GATE_RESID || row >= p.M) return;
     const float* base = p.e.resid + (size_t)row * p.e.ldr + n0;
     #pragma unroll
     for (int j = 0; j < 8; j++)
@@ -203,11 +209,12 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
 // Epilogue of one accumulator row (thread = TMEM lane = output row) over the
 // tile's 256 columns starting at n0.  The tcgen05.ld are warp-collective and
 // executed by every lane; only the stores depend on the row.
+template <int MODE>
 __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, int row, int n0) {
     const GemmEpi& e = p.e;
-    if (e.mode == EPI_QKV_PACK) { epilogue_qkv_pack(p, taddr, row, n0); return; }
+    if constexpr (MODE == EPI_QKV_PACK) { epilogue_qkv_pack(p, taddr, row, n0); return; }
     const bool row_ok = row < p.M;
-    if (e.mode == EPI_SWIGLU) {
+    if constexpr (MODE == EPI_SWIGLU) {
         // column block [h 128 | g 128] -> 128 outputs at n0 / 2
         #pragma unroll 1
         for (int jc = 0; jc < 4; jc++) {
@@ -224,7 +231,7 @@ __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, 
         return;
     }
     const float* gate = (row < e.gate_split) ? e.gate0 : e.gate1;
-    if (e.mode == EPI_GATE_RESID) {
+    if constexpr (MODE == EPI_GATE_RESID) {
         // residual read-modify-write: the chunk's 8 residual loads are issued
         // together, before the TMEM load, so their latency overlaps it and the
         // loads never queue behind the previous chunk's stores.
@@ -279,7 +286,7 @@ __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, 
             #pragma unroll
             for (int j = 0; j < 32; j++) v[j] = __fadd_rn(v[j], (full || col + j < p.N) ? e.bias[col + j] : 0.f);
         }
-        if (e.mode == EPI_GATE_RESID) {
+        if constexpr (MODE == EPI_GATE_RESID) {
             float* dst = e.resid + (size_t)row * e.ldr + col;
             if (full) {
                 #pragma unroll
@@ -314,14 +321,96 @@ __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, 
     }
 }
 
+
+// EPI_GATE_RESID with the residual moved by TMA: for each 32-column chunk of
+// the warp's 32 rows, the residual box (32 x 32 fp32, 128-B swizzle) is
+// loaded one chunk ahead into one of two shared-memory buffers, each lane
+// updates its row in place (resid += (acc + bias) * gate, the same rounding
+// steps as epilogue_row), and one TMA store writes the box back.  Global
+// traffic is whole 128-B lines instead of 16-B pieces of 32 rows per
+// instruction.  Lane 0 issues every TMA operation of the warp.
+struct ResidPipe {
+    uint8_t* buf;        // this warp's two 4 KB boxes
+    uint64_t* full;      // their barriers
+    uint32_t k;          // chunks consumed so far (all lanes)
+    uint32_t issued;     // box loads issued so far (lane 0)
+};
+
+// Lane 0: load the residual box of chunk `issued` into its buffer.
+__device__ __forceinline__ void resid_load(const CUtensorMap* tR, ResidPipe& rp, int col, int row) {
+    uint64_t* b = &rp.full[rp.issued & 1];
+    sm100::mbar_arrive_expect_tx(b, RBOX_BYTES);
+    sm100::tma_load_2d(rp.buf + (rp.issued & 1) * RBOX_BYTES, tR, b, col, row);
+    rp.issued++;
+}
+
+// One tile's 32 rows x up to 256 columns.  next_n0 < 0: no tile follows.
+// Returns false when a wait expired (the tile is abandoned).
+__device__ __forceinline__ bool epilogue_resid_tma(const TcParams& p, const CUtensorMap* tR, uint32_t taddr, int r0,
+                                                   int n0, int next_r0, int next_n0, ResidPipe& rp,
+                                                   volatile int* abort_flag) {
+    const GemmEpi& e = p.e;
+    const int lane = threadIdx.x & 31;
+    const int row = r0 + lane;
+    const float* gate = (row < e.gate_split) ? e.gate0 : e.gate1;
+    const int nch = min(8, (p.N - n0) / 32);
+    for (int c = 0; c < nch; c++) {
+        const int col = n0 + 32 * c;
+        float v[32];
+        sm100::tmem_ld32(taddr + 32 * c, v);
+        if (lane == 0) {
+            // the other buffer was last stored from one chunk ago
+            sm100::bulk_wait_read_all();
+            if (c + 1 < nch) resid_load(tR, rp, col + 32, r0);
+            else if (next_n0 >= 0) resid_load(tR, rp, next_n0, next_r0);
+        }
+        __syncwarp();
+        if (!__all_sync(0xffffffffu, wait_or_abort(&rp.full[rp.k & 1], (rp.k >> 1) & 1, abort_flag))) return false;
+        uint8_t* box = rp.buf + (rp.k & 1) * RBOX_BYTES + lane * 128;
+        #pragma unroll
+        for (int j = 0; j < 8; j++) {
+            float4* q = reinterpret_cast<float4*>(box + ((j ^ (lane & 7)) << 4));
+            float4 r = *q;
+            float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f), g4 = make_float4(1.f, 1.f, 1.f, 1.f);
+            if (e.bias) b4 = __ldg(reinterpret_cast<const float4*>(e.bias + col) + j);
+            if (gate) g4 = __ldg(reinterpret_cast<const float4*>(gate + col) + j);
+            float t0 = __fadd_rn(v[4 * j], b4.x), t1 = __fadd_rn(v[4 * j + 1], b4.y);
+            float t2 = __fadd_rn(v[4 * j + 2], b4.z), t3 = __fadd_rn(v[4 * j + 3], b4.w);
+            if (gate) { t0 = __fmul_rn(t0, g4.x); t1 = __fmul_rn(t1, g4.y); t2 = __fmul_rn(t2, g4.z); t3 = __fmul_rn(t3, g4.w); }
+            r.x = __fadd_rn(t0, r.x); r.y = __fadd_rn(t1, r.y); r.z = __fadd_rn(t2, r.z); r.w = __fadd_rn(t3, r.w);
+            *q = r;
+        }
+        sm100::fence_proxy_async_smem();      // generic-proxy writes -> the TMA store's reads
+        __syncwarp();
+        if (lane == 0) {
+            sm100::tma_store_2d(tR, rp.buf + (rp.k & 1) * RBOX_BYTES, col, r0);
+            sm100::bulk_commit_group();
+        }
+        rp.k++;
+    }
+    return true;
+}
+
+// Lane 0: let every issued box load land (bounded) and the warp's stores
+// complete before the CTA's shared memory goes away.
+__device__ __forceinline__ void resid_finish(ResidPipe& rp) {
+    if ((threadIdx.x & 31) != 0) return;
+    for (uint32_t kk = rp.k; kk < rp.issued; kk++)
+        for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&rp.full[kk & 1], (kk >> 1) & 1); w++) {}
+    sm100::bulk_wait_all();
+}
+
 // ------------------------------------------------------------ single CTA
+template <int MODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB, const TcParams p) {
+k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
+          const __grid_constant__ CUtensorMap tR, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES1 * A1_BYTES;
-    Ctl<STAGES1>* ctl = reinterpret_cast<Ctl<STAGES1>*>(smem + STAGES1 * STAGE1_BYTES);
+    uint8_t* sR = smem + STAGES1 * STAGE1_BYTES;            // residual boxes (1024-B aligned)
+    Ctl<STAGES1>* ctl = reinterpret_cast<Ctl<STAGES1>*>(sR + RES_BYTES);
     volatile int* abort_flag = &ctl->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int num_tiles = p.num_m * p.num_n;
@@ -329,6 +418,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES1; s++) { sm100::mbar_init(&ctl->full[s], 1); sm100::mbar_init(&ctl->empty[s], 1); }
         for (int a = 0; a < NUM_ACC; a++) { sm100::mbar_init(&ctl->tfull[a], 1); sm100::mbar_init(&ctl->tempty[a], 4); }
+        for (int w = 0; w < 4; w++) { sm100::mbar_init(&ctl->rfull[w][0], 1); sm100::mbar_init(&ctl->rfull[w][1], 1); }
         ctl->abort = 0;
         sm100::fence_barrier_init();
         sm100::tma_prefetch_desc(&tA);
@@ -396,6 +486,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
         }
     } else {
         const int q = warp & 3;                 // TMEM lane quadrant this warp may access
+        ResidPipe rp{sR + q * 2 * RBOX_BYTES, ctl->rfull[q], 0u, 0u};
+        const bool rt = MODE == EPI_GATE_RESID && p.resid_tma;
+        if (rt && lane == 0 && (int)blockIdx.x < num_tiles)
+            resid_load(&tR, rp, ((int)blockIdx.x / p.num_m) * BN1, ((int)blockIdx.x % p.num_m) * BM1 + q * 32);
         int it = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, it++) {
             const int acc = it & 1;
@@ -406,12 +500,21 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
             const int mb = tile % p.num_m, nb = tile / p.num_m;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * ACC_COLS;
             const int nt = tile + gridDim.x;
-            if (nt < num_tiles) prefetch_resid(p, (nt % p.num_m) * BM1 + q * 32 + lane, (nt / p.num_m) * BN1);
-            epilogue_row(p, taddr, mb * BM1 + q * 32 + lane, nb * BN1);
+            if (rt) {
+                const bool more = nt < num_tiles;
+                if (!epilogue_resid_tma(p, &tR, taddr, mb * BM1 + q * 32, nb * BN1,
+                                        more ? (nt % p.num_m) * BM1 + q * 32 : 0, more ? (nt / p.num_m) * BN1 : -1,
+                                        rp, abort_flag))
+                    break;
+            } else {
+                if (nt < num_tiles) prefetch_resid<MODE>(p, (nt % p.num_m) * BM1 + q * 32 + lane, (nt / p.num_m) * BN1);
+                epilogue_row<MODE>(p, taddr, mb * BM1 + q * 32 + lane, nb * BN1);
+            }
             sm100::tc_fence_before();
             __syncwarp();
             if (lane == 0) sm100::mbar_arrive(&ctl->tempty[acc]);
         }
+        if (rt) resid_finish(rp);
     }
     __syncthreads();
     if (warp == 1) {
@@ -421,13 +524,16 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
 }
 
 // ------------------------------------------------------------ CTA pair
+template <int MODE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
-k_gemm_tc_pair(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB, const TcParams p) {
+k_gemm_tc_pair(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
+               const __grid_constant__ CUtensorMap tR, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES2 * A2_BYTES;
-    Ctl<STAGES2>* ctl = reinterpret_cast<Ctl<STAGES2>*>(smem + STAGES2 * STAGE2_BYTES);
+    uint8_t* sR = smem + STAGES2 * STAGE2_BYTES;            // residual boxes (1024-B aligned)
+    Ctl<STAGES2>* ctl = reinterpret_cast<Ctl<STAGES2>*>(sR + RES_BYTES);
     volatile int* abort_flag = &ctl->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = sm100::cluster_ctarank();        // 0: issues the MMAs
@@ -437,6 +543,7 @@ k_gemm_tc_pair(const __grid_constant__ CUtensorMap tA, const __grid_constant__ C
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES2; s++) { sm100::mbar_init(&ctl->full[s], 1); sm100::mbar_init(&ctl->empty[s], 1); }
         for (int a = 0; a < NUM_ACC; a++) { sm100::mbar_init(&ctl->tfull[a], 1); sm100::mbar_init(&ctl->tempty[a], 8); }
+        for (int w = 0; w < 4; w++) { sm100::mbar_init(&ctl->rfull[w][0], 1); sm100::mbar_init(&ctl->rfull[w][1], 1); }
         ctl->abort = 0;
         sm100::fence_barrier_init();
         sm100::tma_prefetch_desc(&tA);
@@ -512,6 +619,11 @@ k_gemm_tc_pair(const __grid_constant__ CUtensorMap tA, const __grid_constant__ C
         }
     } else {
         const int q = warp & 3;
+        const int rbase = (int)rank * 128 + q * 32;           // this warp's rows within a 256-row tile
+        ResidPipe rp{sR + q * 2 * RBOX_BYTES, ctl->rfull[q], 0u, 0u};
+        const bool rt = MODE == EPI_GATE_RESID && p.resid_tma;
+        if (rt && lane == 0 && pair < num_tiles)
+            resid_load(&tR, rp, (pair / p.num_m) * BN2, (pair % p.num_m) * BM2 + rbase);
         int it = 0;
         for (int tile = pair; tile < num_tiles; tile += npairs, it++) {
             const int acc = it & 1;
@@ -521,14 +633,22 @@ k_gemm_tc_pair(const __grid_constant__ CUtensorMap tA, const __grid_constant__ C
             const int mb = tile % p.num_m, nb = tile / p.num_m;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * ACC_COLS;
             const int nt = tile + npairs;
-            if (nt < num_tiles)
-                prefetch_resid(p, (nt % p.num_m) * BM2 + (int)rank * 128 + q * 32 + lane, (nt / p.num_m) * BN2);
-            epilogue_row(p, taddr, mb * BM2 + (int)rank * 128 + q * 32 + lane, nb * BN2);
+            if (rt) {
+                const bool more = nt < num_tiles;
+                if (!epilogue_resid_tma(p, &tR, taddr, mb * BM2 + rbase, nb * BN2,
+                                        more ? (nt % p.num_m) * BM2 + rbase : 0, more ? (nt / p.num_m) * BN2 : -1,
+                                        rp, abort_flag))
+                    break;
+            } else {
+                if (nt < num_tiles) prefetch_resid<MODE>(p, (nt % p.num_m) * BM2 + rbase + lane, (nt / p.num_m) * BN2);
+                epilogue_row<MODE>(p, taddr, mb * BM2 + rbase + lane, nb * BN2);
+            }
             sm100::tc_fence_before();
             __syncwarp();
             // the accumulator is free once both CTAs' epilogue warps are done with it
             if (lane == 0) sm100::mbar_arrive_cluster(sm100::map_to_rank(&ctl->tempty[acc], 0));
         }
+        if (rt) resid_finish(rp);
     }
     sm100::tc_fence_before();
     sm100::cluster_sync();                 // no CTA leaves while its pair still signals it
@@ -574,6 +694,20 @@ bool make_tmap_bf16(CUtensorMap* m, const void* base, int rows, int cols, int ld
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// fp32 [rows][cols] (row stride ld elements), 32 x 32 boxes, 128-B swizzle:
+// the residual boxes of the gate/residual epilogue.
+static bool make_tmap_resid(CUtensorMap* m, const float* base, int rows, int cols, int ld) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+    const cuuint32_t box[2] = {32, 32};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool gemm_tc_supported(int M, int N, int K, int lda, int ldw) {
     return M > 0 && N > 0 && K > 0 && N % 32 == 0 && lda % 8 == 0 && ldw % 8 == 0 && encode_fn() != nullptr;
 }
@@ -591,7 +725,11 @@ int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K,
     p.M = M; p.N = N;
     p.num_kb = (K + BK - 1) / BK;
     p.e = e;
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, tr;
+    // gate/residual epilogue through TMA boxes when the residual is 16-B aligned
+    p.resid_tma = e.mode == EPI_GATE_RESID && e.resid && ((uintptr_t)e.resid & 15) == 0 && e.ldr % 4 == 0 &&
+                  make_tmap_resid(&tr, e.resid, M, N, e.ldr);
+    if (!p.resid_tma) std::memset(&tr, 0, sizeof tr);
     if (M > 128) {
         // CTA pairs: 256 x 256 tiles, grid = one cluster of 2 per SM pair
         if (!make_tmap_bf16(&ta, A, M, K, lda, 128, BK) || !make_tmap_bf16(&tb, W, N, K, ldw, 128, BK)) return -1;
@@ -600,13 +738,24 @@ int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K,
         const int tiles = p.num_m * p.num_n;
         int pairs = sms / 2;
         if (tiles < pairs) pairs = tiles;
-        k_gemm_tc_pair<<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(ta, tb, p);
+        switch (e.mode) {
+            case EPI_STORE: k_gemm_tc_pair<EPI_STORE><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(ta, tb, tr, p); break;
+            case EPI_GATE_RESID: k_gemm_tc_pair<EPI_GATE_RESID><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(ta, tb, tr, p); break;
+            case EPI_SWIGLU: k_gemm_tc_pair<EPI_SWIGLU><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(ta, tb, tr, p); break;
+            case EPI_QKV_PACK: k_gemm_tc_pair<EPI_QKV_PACK><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(ta, tb, tr, p); break;
+        }
     } else {
         if (!make_tmap_bf16(&ta, A, M, K, lda, BM1, BK) || !make_tmap_bf16(&tb, W, N, K, ldw, BN1, BK)) return -1;
         p.num_m = (M + BM1 - 1) / BM1;
         p.num_n = (N + BN1 - 1) / BN1;
         const int tiles = p.num_m * p.num_n;
-        k_gemm_tc<<<tiles < sms ? tiles : sms, NUM_THREADS, SMEM1_BYTES, s>>>(ta, tb, p);
+        const int grid = tiles < sms ? tiles : sms;
+        switch (e.mode) {
+            case EPI_STORE: k_gemm_tc<EPI_STORE><<<grid, NUM_THREADS, SMEM1_BYTES, s>>>(ta, tb, tr, p); break;
+            case EPI_GATE_RESID: k_gemm_tc<EPI_GATE_RESID><<<grid, NUM_THREADS, SMEM1_BYTES, s>>>(ta, tb, tr, p); break;
+            case EPI_SWIGLU: k_gemm_tc<EPI_SWIGLU><<<grid, NUM_THREADS, SMEM1_BYTES, s>>>(ta, tb, tr, p); break;
+            case EPI_QKV_PACK: k_gemm_tc<EPI_QKV_PACK><<<grid, NUM_THREADS, SMEM1_BYTES, s>>>(ta, tb, tr, p); break;
+        }
     }
     if (launches) (*launches)++;
     return 0;
@@ -628,10 +777,15 @@ int kernels_init_device() {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64) cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    cudaError_t e = cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1_BYTES);
-    if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_gemm_tc_pair, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
-    if (e != cudaSuccess) return (int)e;
+    const void* single[4] = {(const void*)k_gemm_tc<EPI_STORE>, (const void*)k_gemm_tc<EPI_GATE_RESID>,
+                             (const void*)k_gemm_tc<EPI_SWIGLU>, (const void*)k_gemm_tc<EPI_QKV_PACK>};
+    const void* pairk[4] = {(const void*)k_gemm_tc_pair<EPI_STORE>, (const void*)k_gemm_tc_pair<EPI_GATE_RESID>,
+                            (const void*)k_gemm_tc_pair<EPI_SWIGLU>, (const void*)k_gemm_tc_pair<EPI_QKV_PACK>};
+    for (int i = 0; i < 4; i++) {
+        cudaError_t e = cudaFuncSetAttribute(single[i], cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1_BYTES);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(pairk[i], cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
+        if (e != cudaSuccess) return (int)e;
+    }
     if (int rc = awa_tc_init_device()) return rc;
     return awa_init_device();
 }

@@ -121,3 +121,26 @@ def test_awa_dev_matches_host(ctx):
                         ov.data_ptr(), ot.data_ptr(), s.cuda_stream)
     torch.cuda.synchronize()
     assert np.array_equal(ov.cpu().numpy(), vo) and np.array_equal(ot.cpu().numpy(), to)
+
+
+@pytest.mark.parametrize("shifted", [False, True], ids=["nonshifted", "shifted"])
+def test_awa_1080p_bf16_vs_fp32(shifted):
+    """1080p windows (up to 476 rows: four key tiles, two query-tile pairs per
+    window) on the bf16 tensor-core kernel against the library's fp32 path,
+    which the tests above pin to the oracle."""
+    T, H, W, TXT = 1, 68, 80, 58
+    Lv = T * H * W
+    win = s2b.make_win(T, H, W, (4, 3, 3), TXT, shifted)
+    vqkv = s2b.synth_normal((Lv, 7680), 11, "vqkv")
+    tqkv = s2b.synth_normal((TXT, 7680), 11, "tqkv")
+    nq = [s2b.synth_normal((128,), 11, n, 1.0, 0.02) for n in ("a", "b", "c", "d")]
+    out = {}
+    for prec in (s2b.PREC_FP32, s2b.PREC_BF16):
+        c = s2b.DitB200(0, prec)
+        try:
+            out[prec] = c.awa_forward(vqkv, tqkv, win, *nq, Lv, TXT, 1e-5)
+        finally:
+            c.close()
+    for a, b in zip(out[s2b.PREC_BF16], out[s2b.PREC_FP32]):
+        cos, rel = cases.compare(a, b)
+        assert cos >= 0.9995 and rel <= 2e-2, (cos, rel)
