@@ -178,15 +178,39 @@ k_awa_attn_simt(const TP* __restrict__ Qp, const TP* __restrict__ Kp, const TP* 
     }
 }
 
+// One thread per 4 consecutive outputs; the windows are added in window
+// order (as the reference's loop, src/dit_vk.cpp:440-444) with the loads of
+// 8 windows issued together ahead of their adds.
 template <typename TO>
 __global__ void k_coalesce(const float* __restrict__ toutw, int nwin, int TXT, TO* __restrict__ out, int ld,
                            float divisor) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= TXT * 2560) return;
-    float s = 0.f;
-    for (int w = 0; w < nwin; w++) s = __fadd_rn(s, toutw[(size_t)w * TXT * 2560 + i]);
-    if (divisor > 0.f) s = __fdiv_rn(s, divisor);
-    out[(size_t)(i / 2560) * ld + (i % 2560)] = Cvt<TO>::from_f(s);
+    const int i4 = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i4 >= TXT * 640) return;
+    const float4* src = reinterpret_cast<const float4*>(toutw) + i4;
+    const size_t ws = (size_t)TXT * 640;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+    int w = 0;
+    for (; w + 8 <= nwin; w += 8) {
+        float4 v[8];
+        #pragma unroll
+        for (int k = 0; k < 8; k++) v[k] = __ldcs(src + (size_t)(w + k) * ws);
+        #pragma unroll
+        for (int k = 0; k < 8; k++) {
+            a[0] = __fadd_rn(a[0], v[k].x); a[1] = __fadd_rn(a[1], v[k].y);
+            a[2] = __fadd_rn(a[2], v[k].z); a[3] = __fadd_rn(a[3], v[k].w);
+        }
+    }
+    for (; w < nwin; w++) {
+        const float4 v = __ldcs(src + (size_t)w * ws);
+        a[0] = __fadd_rn(a[0], v.x); a[1] = __fadd_rn(a[1], v.y);
+        a[2] = __fadd_rn(a[2], v.z); a[3] = __fadd_rn(a[3], v.w);
+    }
+    if (divisor > 0.f) {
+        #pragma unroll
+        for (int k = 0; k < 4; k++) a[k] = __fdiv_rn(a[k], divisor);
+    }
+    const int i = i4 * 4;
+    store4(out + (size_t)(i / 2560) * ld + (i % 2560), a);
 }
 
 }  // namespace
@@ -251,8 +275,9 @@ void awa_coalesce_div(const float* toutw, int nwin, int TXT, void* att_txt, int 
                       cudaStream_t s) {
     const int n = TXT * 2560;
     if (n <= 0 || nwin <= 0) return;
-    if (at == ACT_F32) k_coalesce<float><<<(n + 255) / 256, 256, 0, s>>>(toutw, nwin, TXT, (float*)att_txt, ld_att, divisor);
-    else k_coalesce<bf16><<<(n + 255) / 256, 256, 0, s>>>(toutw, nwin, TXT, (bf16*)att_txt, ld_att, divisor);
+    const int n4 = n / 4;
+    if (at == ACT_F32) k_coalesce<float><<<(n4 + 127) / 128, 128, 0, s>>>(toutw, nwin, TXT, (float*)att_txt, ld_att, divisor);
+    else k_coalesce<bf16><<<(n4 + 127) / 128, 128, 0, s>>>(toutw, nwin, TXT, (bf16*)att_txt, ld_att, divisor);
 }
 
 }  // namespace s2b

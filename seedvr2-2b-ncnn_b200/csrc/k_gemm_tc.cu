@@ -107,36 +107,22 @@ __device__ __forceinline__ void prefetch_resid(const TcParams& p, int row, int n
         if (n0 + 32 * j < p.N) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + 32 * j));
 }
 
-// 128 values of one head as bf16 to a packed row (256 B, 16-B stores).
-__device__ __forceinline__ void store_head_bf16(bf16* dst, const float* x) {
+// RoPE in place on dims [d0, d0 + 64) of one normalised head: dims 0..125
+// rotate in adjacent pairs (src/dit_vk.cpp:62-71), pair i with the angle of
+// position pos[i / 21] and frequency i % 21 (cos/sin from the [pos][21]
+// table); dims 126..127 pass through.
+__device__ __forceinline__ void rope64(float* x, int d0, const float2* __restrict__ cs, int p0, int p1, int p2) {
     #pragma unroll
-    for (int c = 0; c < 4; c++) store32(dst + 32 * c, x + 32 * c);
-}
-
-// RoPE of one normalised head: dims 0..125 rotate in adjacent pairs
-// (src/dit_vk.cpp:62-71), pair i with the angle of position pos[i / 21] and
-// frequency i % 21 (cos/sin from the [pos][21] table), dims 126..127 pass
-// through; the result is stored as bf16.
-__device__ __forceinline__ void rope_store(bf16* dst, const float* x, const float2* __restrict__ cs, int p0, int p1,
-                                           int p2) {
-    #pragma unroll
-    for (int c = 0; c < 4; c++) {
-        float o[32];
-        #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-            const int k = 32 * c + j;
-            if (k < 126) {
-                const int i = k >> 1, ax = i / 21, f = i % 21;
-                const int pos = ax == 0 ? p0 : (ax == 1 ? p1 : p2);
-                const float2 t = __ldg(cs + pos * 21 + f);
-                const float a = x[k], b = x[k + 1];
-                o[j] = __fadd_rn(__fmul_rn(a, t.x), __fmul_rn(-b, t.y));
-                o[j + 1] = __fadd_rn(__fmul_rn(b, t.x), __fmul_rn(a, t.y));
-            } else {
-                o[j] = x[k]; o[j + 1] = x[k + 1];
-            }
+    for (int j = 0; j < 64; j += 2) {
+        const int kd = d0 + j;
+        if (kd < 126) {
+            const int i = kd >> 1, ax = i / 21, f = i % 21;
+            const int pos = ax == 0 ? p0 : (ax == 1 ? p1 : p2);
+            const float2 t = __ldg(cs + pos * 21 + f);
+            const float a = x[j], b = x[j + 1];
+            x[j] = __fadd_rn(__fmul_rn(a, t.x), __fmul_rn(-b, t.y));
+            x[j + 1] = __fadd_rn(__fmul_rn(b, t.x), __fmul_rn(a, t.y));
         }
-        store32(dst + 32 * c, o);
     }
 }
 
@@ -162,46 +148,53 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
     if (!vid) { ti = gr - k.Lv; p0 = p1 = p2 = ti; }
     const float* w = nullptr;
     if (sec < 2) w = vid ? (sec == 0 ? k.nq0 : k.nk0) : (sec == 0 ? k.nq1 : k.nk1);
+    // two passes over each head's 128 TMEM columns (sum of squares, then
+    // normalise + rotate + store 64 dims at a time) keep 64 values live
     #pragma unroll 1
     for (int hh = 0; hh < 2; hh++) {
-        float x[128];
-        #pragma unroll
-        for (int c = 0; c < 4; c++) sm100::tmem_ld32(taddr + hh * 128 + c * 32, x + c * 32);
-        if (!row_ok) continue;
-        const int h = h0 + hh;
+        const uint32_t th = taddr + hh * 128;
+        float inv = 1.f;
         if (sec < 2) {
             float sq = 0.f;
             #pragma unroll
-            for (int d = 0; d < 128; d++) sq = fmaf(x[d], x[d], sq);
-            const float inv = 1.f / sqrtf(__fadd_rn(sq * (1.f / 128.f), k.eps));
-            #pragma unroll
-            for (int d = 0; d < 128; d += 4) {
-                const float4 w4 = __ldg(reinterpret_cast<const float4*>(w + d));
-                x[d] = x[d] * inv * w4.x; x[d + 1] = x[d + 1] * inv * w4.y;
-                x[d + 2] = x[d + 2] * inv * w4.z; x[d + 3] = x[d + 3] * inv * w4.w;
+            for (int c = 0; c < 2; c++) {
+                float x[64];
+                sm100::tmem_ld64(th + c * 64, x);
+                #pragma unroll
+                for (int d = 0; d < 64; d++) sq = fmaf(x[d], x[d], sq);
             }
+            inv = 1.f / sqrtf(__fadd_rn(sq * (1.f / 128.f), k.eps));
         }
-        if (vid) {
-            bf16* dst = base + ((size_t)h * k.sumS + gi + (size_t)wi * k.TXT) * 128;
-            if (sec < 2) rope_store(dst, x, k.cs, p0, p1, p2);
-            else store_head_bf16(dst, x);
-        } else {
-            // rotate once (txt angles do not depend on the window), store per window
+        const int h = h0 + hh;
+        // destination of this row: one packed slot (vid) or the first window's (txt)
+        bf16* dst0 = nullptr;
+        if (vid) dst0 = base + ((size_t)h * k.sumS + gi + (size_t)wi * k.TXT) * 128;
+        else dst0 = base + ((size_t)h * k.sumS + k.cums[1] - k.TXT + ti) * 128;
+        #pragma unroll 1
+        for (int c = 0; c < 2; c++) {
+            float x[64];
+            sm100::tmem_ld64(th + c * 64, x);
+            if (!row_ok) continue;
             if (sec < 2) {
-                bf16* first = base + ((size_t)h * k.sumS + k.cums[1] - k.TXT + ti) * 128;
-                rope_store(first, x, k.cs, p0, p1, p2);
-                #pragma unroll 1
-                for (int wj = 1; wj < k.nwin; wj++) {
-                    bf16* dst = base + ((size_t)h * k.sumS + k.cums[wj + 1] - k.TXT + ti) * 128;
-                    #pragma unroll
-                    for (int c = 0; c < 16; c++)
-                        reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(first)[c];
+                #pragma unroll
+                for (int d = 0; d < 64; d += 4) {
+                    const float4 w4 = __ldg(reinterpret_cast<const float4*>(w + c * 64 + d));
+                    x[d] = x[d] * inv * w4.x; x[d + 1] = x[d + 1] * inv * w4.y;
+                    x[d + 2] = x[d + 2] * inv * w4.z; x[d + 3] = x[d + 3] * inv * w4.w;
                 }
-            } else {
-                #pragma unroll 1
-                for (int wj = 0; wj < k.nwin; wj++)
-                    store_head_bf16(base + ((size_t)h * k.sumS + k.cums[wj + 1] - k.TXT + ti) * 128, x);
+                rope64(x, c * 64, k.cs, p0, p1, p2);
             }
+            store32(dst0 + c * 64, x);
+            store32(dst0 + c * 64 + 32, x + 32);
+        }
+        if (!row_ok || vid) continue;
+        // txt row: the same rotated head in every window's slot
+        #pragma unroll 1
+        for (int wj = 1; wj < k.nwin; wj++) {
+            bf16* dst = base + ((size_t)h * k.sumS + k.cums[wj + 1] - k.TXT + ti) * 128;
+            #pragma unroll
+            for (int c = 0; c < 16; c++)
+                reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(dst0)[c];
         }
     }
 }
