@@ -356,6 +356,17 @@ def run_kernel_case(case: str):
         t = s2b.synth_normal((TXT, 2560), 1, "t")
         for _ in range(2):
             c.forward_latent(v, Lv, t, TXT, TIMESTEP, 12, 13, False, False)
+    elif case == "forward_1080p":
+        # two full 32-layer forwards through forward_latent (no graph), one kernel per launch
+        T, H, W = GRID
+        Lv = T * H * W
+        c.init_synth(WEIGHT_SEED, 0, 32)
+        c.set_windows(s2b.make_win(T, H, W, (4, 3, 3), TXT, False), s2b.make_win(T, H, W, (4, 3, 3), TXT, True))
+        vid = s2b.patchify_grid(s2b.synth_vid_grid(T, 2 * H, 2 * W, 42))
+        txt = s2b.synth_txt(TXT, 42)
+        for _ in range(2):
+            c.forward_latent(vid, Lv, txt, TXT, TIMESTEP, 0, 32, True, True)
+        print("launches per forward", c.last_launches())
     elif case == "attn_1080p":
         T, H, W = GRID
         Lv = T * H * W
@@ -374,7 +385,7 @@ def run_kernel_case(case: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel-case", choices=sorted(list(KERNEL_CASES) + ["attn_1080p", "layer_1080p"]),
+    ap.add_argument("--kernel-case", choices=sorted(list(KERNEL_CASES) + ["attn_1080p", "layer_1080p", "forward_1080p"]),
                     help="run one small single-kernel workload (for ncu captures) instead of the bench")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)

@@ -436,6 +436,27 @@ void DitB200::gemm(const void* A, int lda, const Linear& L, int M, const GemmEpi
     pend(s);
 }
 
+// The vid and txt GEMMs of an MM-DiT block (separate weights, same shape and
+// epilogue) as one launch when both suit the tcgen05 pair kernel; otherwise
+// two launches.
+void DitB200::gemm2(const void* A0, int lda0, const Linear& L0, int M0, const GemmEpi& e0, const void* A1, int lda1,
+                    const Linear& L1, int M1, const GemmEpi& e1, cudaStream_t s) {
+    if (act_ == ACT_BF16 && L0.t == ACT_BF16 && L1.t == ACT_BF16 && M0 > 128 && M1 > 0 && L0.out == L1.out &&
+        L0.in == L1.in && gemm_tc_supported(M0, L0.out, L0.in, lda0, L0.ld) &&
+        gemm_tc_supported(M1, L1.out, L1.in, lda1, L1.ld)) {
+        const double flops = 2.0 * (M0 + M1) * L0.out * L0.in;
+        const double bytes = (double)(M0 + M1) * L0.in * act_bytes(act_) + 2.0 * L0.out * L0.in * act_bytes(L0.t) +
+                             (double)(M0 + M1) * L0.out * (e0.mode == EPI_GATE_RESID ? 8 : e0.mode == EPI_SWIGLU ? act_bytes(e0.out_t) / 2.0 : act_bytes(e0.out_t));
+        pbeg(KK_GEMM_TC, flops, bytes, s);
+        const int rc = gemm_tc_grouped(A0, lda0, L0.w.p, L0.ld, M0, e0, A1, lda1, L1.w.p, L1.ld, M1, e1, L0.out,
+                                       L0.in, s, &launches_);
+        pend(s);
+        if (rc == 0) return;
+    }
+    gemm(A0, lda0, L0, M0, e0, s);
+    gemm(A1, lda1, L1, M1, e1, s);
+}
+
 void sinusoidal256(float t, float* e) {   // src/dit_vk.cpp:295-302
     const int half = 128;
     for (int j = 0; j < 256; j++) {
@@ -447,17 +468,29 @@ void sinusoidal256(float t, float* e) {   // src/dit_vk.cpp:295-302
 int DitB200::enqueue_temb(cudaStream_t s) {
     // time embedding (src/dit_vk.cpp:303-309) in fp32, then AdaCompose.
     pbeg(KK_OTHER, 2.0 * (TEMB_IN * DIM + DIM * DIM + (double)DIM * EMB_DIM), 4.0 * (TEMB_IN * DIM + DIM * DIM + (double)DIM * EMB_DIM), s);
-    GemmEpi e; e.mode = EPI_STORE; e.out_t = ACT_F32;
-    e.bias = emb_in_.bias(); e.out = temb_h1_.p; e.ldo = DIM;
-    gemm_simt(temb_in_.p, ACT_F32, TEMB_IN, emb_in_.w.p, ACT_F32, emb_in_.ld, 1, DIM, TEMB_IN, e, s);
-    silu_inplace(temb_h1_.as<float>(), DIM, s);
-    e.bias = emb_hid_.bias(); e.out = temb_h2_.p;
-    gemm_simt(temb_h1_.p, ACT_F32, DIM, emb_hid_.w.p, ACT_F32, emb_hid_.ld, 1, DIM, DIM, e, s);
-    silu_inplace(temb_h2_.as<float>(), DIM, s);
-    e.bias = emb_out_.bias(); e.out = emb_.p; e.ldo = EMB_DIM;
-    gemm_simt(temb_h2_.p, ACT_F32, DIM, emb_out_.w.p, ACT_F32, emb_out_.ld, 1, EMB_DIM, DIM, e, s);
+    // one-row GEMVs (bias and SiLU fused) when the fp32 weights allow float4 rows
+    const bool gv = gemv_f32(temb_in_.as<float>(), TEMB_IN, emb_in_.w.as<float>(), emb_in_.ld, DIM, emb_in_.bias(),
+                             temb_h1_.as<float>(), true, s);
+    if (gv) {
+        gemv_f32(temb_h1_.as<float>(), DIM, emb_hid_.w.as<float>(), emb_hid_.ld, DIM, emb_hid_.bias(),
+                 temb_h2_.as<float>(), true, s);
+        gemv_f32(temb_h2_.as<float>(), DIM, emb_out_.w.as<float>(), emb_out_.ld, EMB_DIM, emb_out_.bias(),
+                 emb_.as<float>(), false, s);
+        launches_ += 3;
+    } else {
+        GemmEpi e; e.mode = EPI_STORE; e.out_t = ACT_F32;
+        e.bias = emb_in_.bias(); e.out = temb_h1_.p; e.ldo = DIM;
+        gemm_simt(temb_in_.p, ACT_F32, TEMB_IN, emb_in_.w.p, ACT_F32, emb_in_.ld, 1, DIM, TEMB_IN, e, s);
+        silu_inplace(temb_h1_.as<float>(), DIM, s);
+        e.bias = emb_hid_.bias(); e.out = temb_h2_.p;
+        gemm_simt(temb_h1_.p, ACT_F32, DIM, emb_hid_.w.p, ACT_F32, emb_hid_.ld, 1, DIM, DIM, e, s);
+        silu_inplace(temb_h2_.as<float>(), DIM, s);
+        e.bias = emb_out_.bias(); e.out = emb_.p; e.ldo = EMB_DIM;
+        gemm_simt(temb_h2_.p, ACT_F32, DIM, emb_out_.w.p, ACT_F32, emb_out_.ld, 1, EMB_DIM, DIM, e, s);
+        launches_ += 5;
+    }
     s2b::ada_compose(emb_.as<float>(), branch_.as<float>(), NUM_LAYERS * 12 + 2, ada_.as<float>(), s);
-    launches_ += 6;
+    launches_ += 1;
     pend(s);
     return OK;
 }
@@ -521,8 +554,9 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
         k.eps = NORM_EPS; k.Lv = Lv; k.TXT = TXT; k.nwin = G.view.nwin; k.sumS = G.view.sumS;
         k.Qp = B.Qp; k.Kp = B.Kp; k.Vp = B.Vp;
         if (dual) {
-            k.row_base = 0; gemm(xn, DIM, BV.qkv, Lv, e, s);
-            k.row_base = Lv; gemm(xn + (size_t)Lv * DIM * ab, DIM, BT.qkv, TXT, e, s);
+            GemmEpi et = e;
+            k.row_base = 0; et.pk.row_base = Lv;
+            gemm2(xn, DIM, BV.qkv, Lv, e, xn + (size_t)Lv * DIM * ab, DIM, BT.qkv, TXT, et, s);
         } else {
             k.row_base = 0; gemm(xn, DIM, BV.qkv, M, e, s);
         }
@@ -566,10 +600,11 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
     // 4. out projection (+bias), gate, residual (src/dit_vk.cpp:461-462, 558-575)
     GemmEpi g; g.mode = EPI_GATE_RESID; g.ldr = DIM;
     if (dual) {
+        GemmEpi gt = g;
         g.resid = X; g.bias = BV.out.bias(); g.gate0 = ada(i, 0, 2); g.gate_split = M;
-        gemm(att, DIM, BV.out, Lv, g, s);
-        g.resid = X + (size_t)Lv * DIM; g.bias = BT.out.bias(); g.gate0 = last ? nullptr : ada(i, 1, 2);
-        gemm(att + (size_t)Lv * DIM * ab, DIM, BT.out, TXT, g, s);
+        gt.resid = X + (size_t)Lv * DIM; gt.bias = BT.out.bias(); gt.gate0 = last ? nullptr : ada(i, 1, 2);
+        gt.gate_split = M;
+        gemm2(att, DIM, BV.out, Lv, g, att + (size_t)Lv * DIM * ab, DIM, BT.out, TXT, gt, s);
     } else {
         g.resid = X; g.bias = BV.out.bias(); g.gate0 = ada(i, 0, 2); g.gate1 = last ? nullptr : ada(i, 1, 2);
         g.gate_split = Lv;
@@ -585,15 +620,18 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
     // 6. SwiGLU: proj_out(silu(proj_in_gate x) * proj_in x)
     GemmEpi sw; sw.mode = EPI_SWIGLU; sw.out_t = act_; sw.ldo = MLP_DIM;
     GemmEpi mo; mo.mode = EPI_GATE_RESID; mo.ldr = DIM;
-    if (dual) {
+    if (dual && !last) {
+        GemmEpi swt = sw, mot = mo;
+        sw.out = hs;
+        swt.out = hs + (size_t)Lv * MLP_DIM * ab;
+        gemm2(xn, DIM, BV.mlp_hg, Lv, sw, xn + (size_t)Lv * DIM * ab, DIM, BT.mlp_hg, TXT, swt, s);
+        mo.resid = X; mo.gate0 = ada(i, 0, 5); mo.gate_split = M;
+        mot.resid = X + (size_t)Lv * DIM; mot.gate0 = ada(i, 1, 5); mot.gate_split = M;
+        gemm2(hs, MLP_DIM, BV.mlp_out, Lv, mo, hs + (size_t)Lv * MLP_DIM * ab, MLP_DIM, BT.mlp_out, TXT, mot, s);
+    } else if (dual) {
         sw.out = hs; gemm(xn, DIM, BV.mlp_hg, Lv, sw, s);
         mo.resid = X; mo.gate0 = ada(i, 0, 5); mo.gate_split = M;
         gemm(hs, MLP_DIM, BV.mlp_out, Lv, mo, s);
-        if (!last) {
-            sw.out = hs + (size_t)Lv * MLP_DIM * ab; gemm(xn + (size_t)Lv * DIM * ab, DIM, BT.mlp_hg, TXT, sw, s);
-            mo.resid = X + (size_t)Lv * DIM; mo.gate0 = ada(i, 1, 5);
-            gemm(hs + (size_t)Lv * MLP_DIM * ab, MLP_DIM, BT.mlp_out, TXT, mo, s);
-        }
     } else {
         sw.out = hs; gemm(xn, DIM, BV.mlp_hg, Mm, sw, s);
         mo.resid = X; mo.gate0 = ada(i, 0, 5); mo.gate1 = ada(i, 1, 5); mo.gate_split = Lv;

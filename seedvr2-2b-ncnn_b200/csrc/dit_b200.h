@@ -146,6 +146,8 @@ private:
     int upload_geom_with(GeomDev& g, const WinGeom& w, const WinTables& tab, const std::vector<int>& tokpos4,
                          bool structured, int npos, int Lv);
     void gemm(const void* A, int lda, const Linear& L, int M, const GemmEpi& e, cudaStream_t s);
+    void gemm2(const void* A0, int lda0, const Linear& L0, int M0, const GemmEpi& e0, const void* A1, int lda1,
+               const Linear& L1, int M1, const GemmEpi& e1, cudaStream_t s);
     // Enqueue the pieces of forward_latent on stream s (device inputs already staged).
     int enqueue_init(int Lv, int TXT, cudaStream_t s);
     int enqueue_temb(cudaStream_t s);

@@ -97,7 +97,43 @@ k_gemm(const TA* __restrict__ A, int lda, const TW* __restrict__ W, int ldw, int
     }
 }
 
+// y[n] = act(sum_k x[k] W[n][k] + b[n]) for one input row (the time-embedding
+// MLP): one warp per output, float4 loads of the weight row, x staged in
+// shared memory, a fixed-order shuffle reduction.
+constexpr int GEMV_WARPS = 8;
+__global__ void __launch_bounds__(GEMV_WARPS * 32)
+k_gemv_f32(const float* __restrict__ x, int K, const float* __restrict__ W, int ldw, int N,
+           const float* __restrict__ bias, float* __restrict__ y, int silu) {
+    extern __shared__ float xs[];
+    for (int k = threadIdx.x; k < K; k += blockDim.x) xs[k] = x[k];
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int n = blockIdx.x * GEMV_WARPS + (threadIdx.x >> 5);
+    if (n >= N) return;
+    const float4* w = reinterpret_cast<const float4*>(W + (size_t)n * ldw);
+    float acc = 0.f;
+    for (int c = lane; c < K / 4; c += 32) {
+        const float4 a = __ldcs(w + c);
+        const float4 b = *reinterpret_cast<const float4*>(xs + 4 * c);
+        acc = fmaf(a.x, b.x, acc); acc = fmaf(a.y, b.y, acc);
+        acc = fmaf(a.z, b.z, acc); acc = fmaf(a.w, b.w, acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+        float v = bias ? __fadd_rn(acc, bias[n]) : acc;
+        y[n] = silu ? silu_f(v) : v;
+    }
+}
+
 }  // namespace
+
+bool gemv_f32(const float* x, int K, const float* W, int ldw, int N, const float* bias, float* y, bool silu,
+              cudaStream_t s) {
+    if (K % 4 || ldw % 4 || ((uintptr_t)W & 15) || ((uintptr_t)x & 15) || K > 12288) return false;
+    k_gemv_f32<<<(N + GEMV_WARPS - 1) / GEMV_WARPS, GEMV_WARPS * 32, K * sizeof(float), s>>>(x, K, W, ldw, N, bias, y,
+                                                                                             silu ? 1 : 0);
+    return true;
+}
 
 void gemm_simt(const void* A, ActT at, int lda, const void* W, ActT wt, int ldw, int M, int N, int K,
                const GemmEpi& e, cudaStream_t s) {

@@ -266,54 +266,34 @@ __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, 
             }
         }
         return;
-    }
-    #pragma unroll 1
-    for (int c0 = 0; c0 < 256; c0 += 32) {
-        if (n0 + c0 >= p.N) break;             // warp-uniform
-        float v[32];
-        sm100::tmem_ld32(taddr + c0, v);
-        if (!row_ok) continue;
-        const int col = n0 + c0;
-        const bool full = col + 32 <= p.N;
-        if (e.bias) {
-            #pragma unroll
-            for (int j = 0; j < 32; j++) v[j] = __fadd_rn(v[j], (full || col + j < p.N) ? e.bias[col + j] : 0.f);
-        }
-        if constexpr (MODE == EPI_GATE_RESID) {
-            float* dst = e.resid + (size_t)row * e.ldr + col;
-            if (full) {
+    } else {
+        #pragma unroll 1
+        for (int c0 = 0; c0 < 256; c0 += 32) {
+            if (n0 + c0 >= p.N) break;             // warp-uniform
+            float v[32];
+            sm100::tmem_ld32(taddr + c0, v);
+            if (!row_ok) continue;
+            const int col = n0 + c0;
+            const bool full = col + 32 <= p.N;
+            if (e.bias) {
                 #pragma unroll
-                for (int j = 0; j < 32; j += 4) {
-                    float4 r = *reinterpret_cast<const float4*>(dst + j);
-                    float g0 = gate ? gate[col + j] : 1.f, g1 = gate ? gate[col + j + 1] : 1.f;
-                    float g2 = gate ? gate[col + j + 2] : 1.f, g3 = gate ? gate[col + j + 3] : 1.f;
-                    r.x = __fadd_rn(gate ? __fmul_rn(v[j], g0) : v[j], r.x);
-                    r.y = __fadd_rn(gate ? __fmul_rn(v[j + 1], g1) : v[j + 1], r.y);
-                    r.z = __fadd_rn(gate ? __fmul_rn(v[j + 2], g2) : v[j + 2], r.z);
-                    r.w = __fadd_rn(gate ? __fmul_rn(v[j + 3], g3) : v[j + 3], r.w);
-                    *reinterpret_cast<float4*>(dst + j) = r;
-                }
-            } else {
-                for (int j = 0; j < 32 && col + j < p.N; j++) {
-                    const float t = gate ? __fmul_rn(v[j], gate[col + j]) : v[j];
-                    dst[j] = __fadd_rn(t, dst[j]);
-                }
+                for (int j = 0; j < 32; j++) v[j] = __fadd_rn(v[j], (full || col + j < p.N) ? e.bias[col + j] : 0.f);
             }
-        } else {
-            const size_t off = (size_t)row * e.ldo + col;
-            if (full) {
-                if (e.out_t == ACT_BF16) store32((bf16*)e.out + off, v);
-                else store32((float*)e.out + off, v);
-            } else {
-                for (int j = 0; j < 32 && col + j < p.N; j++) {
-                    if (e.out_t == ACT_BF16) ((bf16*)e.out)[off + j] = __float2bfloat16_rn(v[j]);
-                    else ((float*)e.out)[off + j] = v[j];
+            {
+                const size_t off = (size_t)row * e.ldo + col;
+                if (full) {
+                    if (e.out_t == ACT_BF16) store32((bf16*)e.out + off, v);
+                    else store32((float*)e.out + off, v);
+                } else {
+                    for (int j = 0; j < 32 && col + j < p.N; j++) {
+                        if (e.out_t == ACT_BF16) ((bf16*)e.out)[off + j] = __float2bfloat16_rn(v[j]);
+                        else ((float*)e.out)[off + j] = v[j];
+                    }
                 }
             }
         }
     }
 }
-
 
 // EPI_GATE_RESID with the residual moved by TMA: for each 32-column chunk of
 // the warp's 32 rows, the residual box (32 x 32 fp32, 128-B swizzle) is
@@ -340,8 +320,8 @@ __device__ __forceinline__ void resid_load(const CUtensorMap* tR, ResidPipe& rp,
 // One tile's 32 rows x up to 256 columns.  next_n0 < 0: no tile follows.
 // Returns false when a wait expired (the tile is abandoned).
 __device__ __forceinline__ bool epilogue_resid_tma(const TcParams& p, const CUtensorMap* tR, uint32_t taddr, int r0,
-                                                   int n0, int next_r0, int next_n0, ResidPipe& rp,
-                                                   volatile int* abort_flag) {
+                                                   int n0, const CUtensorMap* tR_next, int next_r0, int next_n0,
+                                                   ResidPipe& rp, volatile int* abort_flag) {
     const GemmEpi& e = p.e;
     const int lane = threadIdx.x & 31;
     const int row = r0 + lane;
@@ -355,7 +335,7 @@ __device__ __forceinline__ bool epilogue_resid_tma(const TcParams& p, const CUte
             // the other buffer was last stored from one chunk ago
             sm100::bulk_wait_read_all();
             if (c + 1 < nch) resid_load(tR, rp, col + 32, r0);
-            else if (next_n0 >= 0) resid_load(tR, rp, next_n0, next_r0);
+            else if (next_n0 >= 0) resid_load(tR_next, rp, next_n0, next_r0);
         }
         __syncwarp();
         if (!__all_sync(0xffffffffu, wait_or_abort(&rp.full[rp.k & 1], (rp.k >> 1) & 1, abort_flag))) return false;
@@ -495,7 +475,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
             const int nt = tile + gridDim.x;
             if (rt) {
                 const bool more = nt < num_tiles;
-                if (!epilogue_resid_tma(p, &tR, taddr, mb * BM1 + q * 32, nb * BN1,
+                if (!epilogue_resid_tma(p, &tR, taddr, mb * BM1 + q * 32, nb * BN1, &tR,
                                         more ? (nt % p.num_m) * BM1 + q * 32 : 0, more ? (nt / p.num_m) * BN1 : -1,
                                         rp, abort_flag))
                     break;
@@ -517,10 +497,31 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
 }
 
 // ------------------------------------------------------------ CTA pair
+// Tensor maps of up to two GEMM groups that share N, K and the epilogue mode
+// (the vid and txt Linears of layers 0..9): A, B and the residual boxes.
+struct PairMaps {
+    CUtensorMap a[2], b[2], r[2];
+};
+
+// Tiles of group 0 come first, then group 1's; a tile's group picks its
+// maps and epilogue parameters.
+struct TileRef {
+    int grp, mb, nb;
+};
+__device__ __forceinline__ TileRef tile_ref(const TcParams& p0, const TcParams& p1, int tiles0, int tile) {
+    TileRef t;
+    t.grp = tile >= tiles0;
+    const int lt = t.grp ? tile - tiles0 : tile;
+    const int nm = t.grp ? p1.num_m : p0.num_m;
+    t.mb = lt % nm;
+    t.nb = lt / nm;
+    return t;
+}
+
 template <int MODE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
-k_gemm_tc_pair(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
-               const __grid_constant__ CUtensorMap tR, const TcParams p) {
+k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ TcParams p0,
+               const __grid_constant__ TcParams p1, int ngroups) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -531,7 +532,9 @@ k_gemm_tc_pair(const __grid_constant__ CUtensorMap tA, const __grid_constant__ C
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = sm100::cluster_ctarank();        // 0: issues the MMAs
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-    const int num_tiles = p.num_m * p.num_n;
+    const int tiles0 = p0.num_m * p0.num_n;
+    const int num_tiles = tiles0 + (ngroups > 1 ? p1.num_m * p1.num_n : 0);
+    const int num_kb = p0.num_kb;                           // groups share K
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES2; s++) { sm100::mbar_init(&ctl->full[s], 1); sm100::mbar_init(&ctl->empty[s], 1); }
@@ -539,8 +542,10 @@ k_gemm_tc_pair(const __grid_constant__ CUtensorMap tA, const __grid_constant__ C
         for (int w = 0; w < 4; w++) { sm100::mbar_init(&ctl->rfull[w][0], 1); sm100::mbar_init(&ctl->rfull[w][1], 1); }
         ctl->abort = 0;
         sm100::fence_barrier_init();
-        sm100::tma_prefetch_desc(&tA);
-        sm100::tma_prefetch_desc(&tB);
+        for (int g = 0; g < ngroups; g++) {
+            sm100::tma_prefetch_desc(&maps.a[g]);
+            sm100::tma_prefetch_desc(&maps.b[g]);
+        }
     }
     if (warp == 1) {
         sm100::tmem_alloc_pair(&ctl->tmem_slot, TMEM_COLS);
@@ -557,14 +562,16 @@ k_gemm_tc_pair(const __grid_constant__ CUtensorMap tA, const __grid_constant__ C
             long issued = 0;
             bool ok = true;
             for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-                const int mb = tile % p.num_m, nb = tile / p.num_m;
-                for (int kb = 0; kb < p.num_kb; kb++) {
+                const TileRef t = tile_ref(p0, p1, tiles0, tile);
+                const CUtensorMap* ta = &maps.a[t.grp];
+                const CUtensorMap* tb = &maps.b[t.grp];
+                for (int kb = 0; kb < num_kb; kb++) {
                     if (!wait_or_abort(&ctl->empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
                     // both CTAs' bytes complete on the even CTA's full barrier
                     if (rank == 0) sm100::mbar_arrive_expect_tx(&ctl->full[stage], 2 * STAGE2_BYTES);
                     const uint32_t fb = sm100::map_to_rank(&ctl->full[stage], 0);
-                    sm100::tma_load_2d_pair(sA + stage * A2_BYTES, &tA, fb, kb * BK, mb * BM2 + (int)rank * 128);
-                    sm100::tma_load_2d_pair(sB + stage * B2_BYTES, &tB, fb, kb * BK, nb * BN2 + (int)rank * 128);
+                    sm100::tma_load_2d_pair(sA + stage * A2_BYTES, ta, fb, kb * BK, t.mb * BM2 + (int)rank * 128);
+                    sm100::tma_load_2d_pair(sB + stage * B2_BYTES, tb, fb, kb * BK, t.nb * BN2 + (int)rank * 128);
                     issued++;
                     if (++stage == STAGES2) { stage = 0; phase ^= 1; }
                 }
@@ -590,7 +597,7 @@ k_gemm_tc_pair(const __grid_constant__ CUtensorMap tA, const __grid_constant__ C
                 if (!wait_or_abort(&ctl->tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
                 sm100::tc_fence_after();
                 const uint32_t d = tmem_base + acc * ACC_COLS;
-                for (int kb = 0; kb < p.num_kb; kb++) {
+                for (int kb = 0; kb < num_kb; kb++) {
                     if (!wait_or_abort(&ctl->full[stage], phase, abort_flag)) { ok = false; break; }
                     sm100::tc_fence_after();
                     const uint8_t* a = sA + stage * A2_BYTES;
@@ -614,27 +621,31 @@ k_gemm_tc_pair(const __grid_constant__ CUtensorMap tA, const __grid_constant__ C
         const int q = warp & 3;
         const int rbase = (int)rank * 128 + q * 32;           // this warp's rows within a 256-row tile
         ResidPipe rp{sR + q * 2 * RBOX_BYTES, ctl->rfull[q], 0u, 0u};
-        const bool rt = MODE == EPI_GATE_RESID && p.resid_tma;
-        if (rt && lane == 0 && pair < num_tiles)
-            resid_load(&tR, rp, (pair / p.num_m) * BN2, (pair % p.num_m) * BM2 + rbase);
+        // TMA residual boxes only when every group has them (checked on the host)
+        const bool rt = MODE == EPI_GATE_RESID && p0.resid_tma;
+        if (rt && lane == 0 && pair < num_tiles) {
+            const TileRef t = tile_ref(p0, p1, tiles0, pair);
+            resid_load(&maps.r[t.grp], rp, t.nb * BN2, t.mb * BM2 + rbase);
+        }
         int it = 0;
         for (int tile = pair; tile < num_tiles; tile += npairs, it++) {
             const int acc = it & 1;
             const uint32_t acc_phase = (it >> 1) & 1;
             if (!__all_sync(0xffffffffu, wait_or_abort(&ctl->tfull[acc], acc_phase, abort_flag))) break;
             sm100::tc_fence_after();
-            const int mb = tile % p.num_m, nb = tile / p.num_m;
+            const TileRef t = tile_ref(p0, p1, tiles0, tile);
+            const TcParams& p = t.grp ? p1 : p0;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * ACC_COLS;
             const int nt = tile + npairs;
+            const bool more = nt < num_tiles;
+            const TileRef u = tile_ref(p0, p1, tiles0, more ? nt : tile);
             if (rt) {
-                const bool more = nt < num_tiles;
-                if (!epilogue_resid_tma(p, &tR, taddr, mb * BM2 + rbase, nb * BN2,
-                                        more ? (nt % p.num_m) * BM2 + rbase : 0, more ? (nt / p.num_m) * BN2 : -1,
-                                        rp, abort_flag))
+                if (!epilogue_resid_tma(p, &maps.r[t.grp], taddr, t.mb * BM2 + rbase, t.nb * BN2, &maps.r[u.grp],
+                                        u.mb * BM2 + rbase, more ? u.nb * BN2 : -1, rp, abort_flag))
                     break;
             } else {
-                if (nt < num_tiles) prefetch_resid<MODE>(p, (nt % p.num_m) * BM2 + rbase + lane, (nt / p.num_m) * BN2);
-                epilogue_row<MODE>(p, taddr, mb * BM2 + rbase + lane, nb * BN2);
+                if (more) prefetch_resid<MODE>(u.grp ? p1 : p0, u.mb * BM2 + rbase + lane, u.nb * BN2);
+                epilogue_row<MODE>(p, taddr, t.mb * BM2 + rbase + lane, t.nb * BN2);
             }
             sm100::tc_fence_before();
             __syncwarp();
@@ -705,43 +716,71 @@ bool gemm_tc_supported(int M, int N, int K, int lda, int ldw) {
     return M > 0 && N > 0 && K > 0 && N % 32 == 0 && lda % 8 == 0 && ldw % 8 == 0 && encode_fn() != nullptr;
 }
 
-int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K, const GemmEpi& e, cudaStream_t s,
-            int* launches) {
-    if (!gemm_tc_supported(M, N, K, lda, ldw)) return -1;
-    if (((uintptr_t)A & 15) || ((uintptr_t)W & 15)) return -1;
-    if (e.mode == EPI_SWIGLU && N % 256) return -1;
-    if (e.mode == EPI_QKV_PACK && N != 3 * 2560) return -1;
+static int num_sms() {
     int dev = 0;
     cudaGetDevice(&dev);
-    const int sms = (dev < 64 && g_num_sms[dev] > 0) ? g_num_sms[dev] : 148;
-    TcParams p;
+    return (dev < 64 && g_num_sms[dev] > 0) ? g_num_sms[dev] : 148;
+}
+
+static bool gemm_args_ok(const void* A, int lda, const void* W, int ldw, int M, int N, int K, const GemmEpi& e) {
+    if (!gemm_tc_supported(M, N, K, lda, ldw)) return false;
+    if (((uintptr_t)A & 15) || ((uintptr_t)W & 15)) return false;
+    if (e.mode == EPI_SWIGLU && N % 256) return false;
+    if (e.mode == EPI_QKV_PACK && N != 3 * 2560) return false;
+    return true;
+}
+
+// Parameters and tensor maps of one pair-kernel group (256-row A boxes).
+static bool pair_group(const void* A, int lda, const void* W, int ldw, int M, int N, int K, const GemmEpi& e,
+                       TcParams& p, CUtensorMap& ta, CUtensorMap& tb, CUtensorMap& tr) {
     p.M = M; p.N = N;
     p.num_kb = (K + BK - 1) / BK;
     p.e = e;
-    CUtensorMap ta, tb, tr;
     // gate/residual epilogue through TMA boxes when the residual is 16-B aligned
     p.resid_tma = e.mode == EPI_GATE_RESID && e.resid && ((uintptr_t)e.resid & 15) == 0 && e.ldr % 4 == 0 &&
                   make_tmap_resid(&tr, e.resid, M, N, e.ldr);
     if (!p.resid_tma) std::memset(&tr, 0, sizeof tr);
+    if (!make_tmap_bf16(&ta, A, M, K, lda, 128, BK) || !make_tmap_bf16(&tb, W, N, K, ldw, 128, BK)) return false;
+    p.num_m = (M + BM2 - 1) / BM2;
+    p.num_n = (N + BN2 - 1) / BN2;
+    return true;
+}
+
+static void launch_pair(const PairMaps& maps, const TcParams& p0, const TcParams& p1, int ngroups, cudaStream_t s) {
+    const int tiles = p0.num_m * p0.num_n + (ngroups > 1 ? p1.num_m * p1.num_n : 0);
+    int pairs = num_sms() / 2;
+    if (tiles < pairs) pairs = tiles;
+    switch (p0.e.mode) {
+        case EPI_STORE: k_gemm_tc_pair<EPI_STORE><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(maps, p0, p1, ngroups); break;
+        case EPI_GATE_RESID: k_gemm_tc_pair<EPI_GATE_RESID><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(maps, p0, p1, ngroups); break;
+        case EPI_SWIGLU: k_gemm_tc_pair<EPI_SWIGLU><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(maps, p0, p1, ngroups); break;
+        case EPI_QKV_PACK: k_gemm_tc_pair<EPI_QKV_PACK><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(maps, p0, p1, ngroups); break;
+    }
+}
+
+int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K, const GemmEpi& e, cudaStream_t s,
+            int* launches) {
+    if (!gemm_args_ok(A, lda, W, ldw, M, N, K, e)) return -1;
     if (M > 128) {
         // CTA pairs: 256 x 256 tiles, grid = one cluster of 2 per SM pair
-        if (!make_tmap_bf16(&ta, A, M, K, lda, 128, BK) || !make_tmap_bf16(&tb, W, N, K, ldw, 128, BK)) return -1;
-        p.num_m = (M + BM2 - 1) / BM2;
-        p.num_n = (N + BN2 - 1) / BN2;
-        const int tiles = p.num_m * p.num_n;
-        int pairs = sms / 2;
-        if (tiles < pairs) pairs = tiles;
-        switch (e.mode) {
-            case EPI_STORE: k_gemm_tc_pair<EPI_STORE><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(ta, tb, tr, p); break;
-            case EPI_GATE_RESID: k_gemm_tc_pair<EPI_GATE_RESID><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(ta, tb, tr, p); break;
-            case EPI_SWIGLU: k_gemm_tc_pair<EPI_SWIGLU><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(ta, tb, tr, p); break;
-            case EPI_QKV_PACK: k_gemm_tc_pair<EPI_QKV_PACK><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(ta, tb, tr, p); break;
-        }
+        PairMaps maps;
+        TcParams p;
+        if (!pair_group(A, lda, W, ldw, M, N, K, e, p, maps.a[0], maps.b[0], maps.r[0])) return -1;
+        launch_pair(maps, p, p, 1, s);
     } else {
+        TcParams p;
+        p.M = M; p.N = N;
+        p.num_kb = (K + BK - 1) / BK;
+        p.e = e;
+        CUtensorMap ta, tb, tr;
+        p.resid_tma = e.mode == EPI_GATE_RESID && e.resid && ((uintptr_t)e.resid & 15) == 0 && e.ldr % 4 == 0 &&
+                      make_tmap_resid(&tr, e.resid, M, N, e.ldr);
+        if (!p.resid_tma) std::memset(&tr, 0, sizeof tr);
         if (!make_tmap_bf16(&ta, A, M, K, lda, BM1, BK) || !make_tmap_bf16(&tb, W, N, K, ldw, BN1, BK)) return -1;
         p.num_m = (M + BM1 - 1) / BM1;
         p.num_n = (N + BN1 - 1) / BN1;
         const int tiles = p.num_m * p.num_n;
+        const int sms = num_sms();
         const int grid = tiles < sms ? tiles : sms;
         switch (e.mode) {
             case EPI_STORE: k_gemm_tc<EPI_STORE><<<grid, NUM_THREADS, SMEM1_BYTES, s>>>(ta, tb, tr, p); break;
@@ -750,6 +789,22 @@ int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K,
             case EPI_QKV_PACK: k_gemm_tc<EPI_QKV_PACK><<<grid, NUM_THREADS, SMEM1_BYTES, s>>>(ta, tb, tr, p); break;
         }
     }
+    if (launches) (*launches)++;
+    return 0;
+}
+
+int gemm_tc_grouped(const void* A0, int lda0, const void* W0, int ldw0, int M0, const GemmEpi& e0, const void* A1,
+                    int lda1, const void* W1, int ldw1, int M1, const GemmEpi& e1, int N, int K, cudaStream_t s,
+                    int* launches) {
+    if (e0.mode != e1.mode || M0 <= 0 || M1 <= 0) return -1;
+    if (!gemm_args_ok(A0, lda0, W0, ldw0, M0, N, K, e0) || !gemm_args_ok(A1, lda1, W1, ldw1, M1, N, K, e1)) return -1;
+    PairMaps maps;
+    TcParams p0, p1;
+    if (!pair_group(A0, lda0, W0, ldw0, M0, N, K, e0, p0, maps.a[0], maps.b[0], maps.r[0]) ||
+        !pair_group(A1, lda1, W1, ldw1, M1, N, K, e1, p1, maps.a[1], maps.b[1], maps.r[1]))
+        return -1;
+    if (p0.resid_tma != p1.resid_tma) return -1;    // one residual path for the whole launch
+    launch_pair(maps, p0, p1, 2, s);
     if (launches) (*launches)++;
     return 0;
 }

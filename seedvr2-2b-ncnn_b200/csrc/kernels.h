@@ -55,12 +55,23 @@ struct GemmEpi {
 void gemm_simt(const void* A, ActT at, int lda, const void* W, ActT wt, int ldw, int M, int N, int K,
                const GemmEpi& e, cudaStream_t s);
 
+// One-row fp32 GEMV y = act(x W^T + b) (act = SiLU when silu); false when
+// the shapes do not suit it (K and ldw multiples of 4, 16-B aligned x / W).
+bool gemv_f32(const float* x, int K, const float* W, int ldw, int N, const float* bias, float* y, bool silu,
+              cudaStream_t s);
+
 // tcgen05 (5th-gen tensor core) BF16 GEMM, TMA-staged, TMEM accumulators.
 // Requirements: A, W bf16, K % 64 == 0 (the TMA maps zero-fill ragged M/N),
 // lda/ldw multiples of 8 elements, 16-byte aligned bases.
 bool gemm_tc_supported(int M, int N, int K, int lda, int ldw);
 int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K, const GemmEpi& e,
             cudaStream_t s, int* launches);
+// Two GEMMs with the same N, K and epilogue mode (the vid and txt Linears of
+// an MM-DiT block) in one launch of the CTA-pair kernel; their tiles share
+// the persistent grid.  Returns -1 when either does not suit the kernel.
+int gemm_tc_grouped(const void* A0, int lda0, const void* W0, int ldw0, int M0, const GemmEpi& e0, const void* A1,
+                    int lda1, const void* W1, int ldw1, int M1, const GemmEpi& e1, int N, int K, cudaStream_t s,
+                    int* launches);
 // Reads and clears the current device's tcgen05-kernel error flag (set when a
 // bounded wait expired).  Returns a cudaError_t value.
 int gemm_tc_error_reset(int* had_error);
