@@ -158,6 +158,8 @@ private:
     int shard_prepare(int Lv, int TXT);
     int shard_enqueue(cudaStream_t s);
     int shard_exchange(int p, cudaStream_t s);
+    int shard_capture();
+    cudaStream_t capture_stream() const { return stream_; }
     const float* ada(int layer, int flow, int k) const {
         return ada_.as<float>() + ((size_t)(layer * 12 + flow * 6 + k)) * DIM;
     }

@@ -71,10 +71,10 @@ int DitB200::ShardState::nccl_check(ncclResult_t r, const char* what, std::strin
 }
 
 DitB200::ShardState::~ShardState() {
-    if (comm && nl) {
-        if (dev >= 0) cudaSetDevice(dev);
-        nl->CommDestroy(comm);
-    }
+    if (dev >= 0) cudaSetDevice(dev);
+    // a graph holding NCCL calls goes before its communicator
+    if (gexec) cudaGraphExecDestroy(gexec);
+    if (comm && nl) nl->CommDestroy(comm);
 }
 
 int DitB200::shard_init(const uint8_t id[128], int world, int rank) {
@@ -317,12 +317,15 @@ int DitB200::shard_forward(const float* vid_patch, int Lv, const float* txt, int
     cudaMemcpyAsync(temb_in_.p, temb, sizeof temb, cudaMemcpyHostToDevice, stream_);
     cudaMemcpyAsync(S.VIDIN.p, vid_patch, (size_t)Lv * PATCH_IN * 4, cudaMemcpyHostToDevice, stream_);
     cudaMemcpyAsync(S.TXTIN.p, txt, (size_t)TXT * TXT_IN * 4, cudaMemcpyHostToDevice, stream_);
-    if (int rc = shard_enqueue(stream_)) {
+    // the per-kernel profile records events around each launch: no graph then
+    int rc = prof_on_ ? shard_enqueue(stream_) : shard_capture();
+    if (!rc && !prof_on_) rc = cuda_check(cudaGraphLaunch(S.gexec, stream_), "shard graph launch");
+    if (rc) {
         cudaStreamSynchronize(stream_);
         return rc;
     }
     cudaMemcpyAsync(sr_out, S.SRFULL.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToHost, stream_);
-    last_launches_ = launches_;
+    last_launches_ = prof_on_ ? launches_ : S.graph_launches;
     if (int rc = cuda_check(cudaGetLastError(), "kernel launch")) return rc;
     return cuda_check(cudaStreamSynchronize(stream_), "shard_forward");
 }
@@ -344,15 +347,37 @@ int DitB200::shard_forward_dev(const float* d_vid, int Lv, const float* d_txt, i
     cudaMemcpyAsync(temb_in_.p, temb, sizeof temb, cudaMemcpyHostToDevice, stream_);
     cudaMemcpyAsync(S.VIDIN.p, d_vid, (size_t)Lv * PATCH_IN * 4, cudaMemcpyDeviceToDevice, stream_);
     cudaMemcpyAsync(S.TXTIN.p, d_txt, (size_t)TXT * TXT_IN * 4, cudaMemcpyDeviceToDevice, stream_);
-    const int rc = shard_enqueue(stream_);
+    int rc = shard_capture();
+    if (!rc) rc = cuda_check(cudaGraphLaunch(S.gexec, stream_), "shard graph launch");
     if (!rc) cudaMemcpyAsync(d_sr, S.SRFULL.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToDevice, stream_);
     cudaEventRecord(ev_out, stream_);
     cudaStreamWaitEvent(user, ev_out, 0);
     cudaEventDestroy(ev_in);
     cudaEventDestroy(ev_out);
-    last_launches_ = launches_;
+    last_launches_ = S.graph_launches;
     if (rc) return rc;
     return cuda_check(cudaGetLastError(), "shard_forward_dev");
+}
+
+// Captures shard_enqueue (kernels and NCCL calls) once per plan; every rank
+// captures the same sequence, so replays stay in step across ranks.
+int DitB200::shard_capture() {
+    ShardState& S = *shard_;
+    if (S.gexec && S.graph_gen == S.plan_gen) return OK;
+    if (S.gexec) { cudaGraphExecDestroy(S.gexec); S.gexec = nullptr; }
+    cudaGraph_t graph = nullptr;
+    if (int rc = cuda_check(cudaStreamBeginCapture(capture_stream(), cudaStreamCaptureModeRelaxed), "begin capture"))
+        return rc;
+    const int rc = shard_enqueue(capture_stream());
+    cudaError_t ce = cudaStreamEndCapture(capture_stream(), &graph);
+    if (rc) { if (graph) cudaGraphDestroy(graph); return rc; }
+    if (int r = cuda_check(ce, "end capture")) return r;
+    ce = cudaGraphInstantiate(&S.gexec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (int r = cuda_check(ce, "graph instantiate")) { S.gexec = nullptr; return r; }
+    S.graph_gen = S.plan_gen;
+    S.graph_launches = launches_;
+    return OK;
 }
 
 }  // namespace s2b

@@ -50,6 +50,10 @@ struct DitB200::ShardState {
     int n_self[2] = {0, 0};
     DevBuf XSEND, XRECV;
 
+    // the captured shard forward (kernels + NCCL calls) of the current plan
+    cudaGraphExec_t gexec = nullptr;
+    int graph_gen = -1, graph_launches = 0;
+
     int nccl_check(ncclResult_t r, const char* what, std::string& err) const;
     ~ShardState();
 };

@@ -706,6 +706,272 @@ k_awa_attn_tc2(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
     }
 }
 
+
+// ---------------------------------------------------------------- 64-key kernel
+// One CTA = one (window, head, 128-query tile), two CTAs per SM, keys in
+// 64-key tiles through two-stage K and V rings.  TMEM per CTA (256 columns):
+// S in two 64-column slots (S_{j+1} is computed while the softmax reads
+// S_j), O in 128 columns.  The softmax writes P_j back into its S slot as
+// packed bf16 pairs, and P_j is the TMEM A operand of O += P_j V_j, so a K
+// stage is free as soon as its scores are computed and the next loads are
+// issued one key tile ahead.  Roles:
+//   warps 0-3  softmax + epilogue (thread = query row)
+//   warp 4     TMEM allocation; lane 0 issues the MMAs:
+//                S_0; per j: S_{j+1} (once K_{j+1} is in and PV_{j-1} has
+//                read the slot), then PV_j (once P_j is ready)
+//   warp 5     lane 0 issues the TMA loads (Q; K_j, V_j as stages free up)
+// The softmax rescales O only when a row's max grows by more than 2^8, and
+// then waits for the PV in flight first.
+constexpr int KT4 = 64;
+constexpr int KV4_BYTES = KT4 * D * 2;             // 16 KB: two 64-column halves of 8 KB
+constexpr int KV4_HALF = KV4_BYTES / 2;
+constexpr int T4_THREADS = 192;
+constexpr int T4_SMEM = TILE_BYTES + 4 * KV4_BYTES + 1024 + 256;
+constexpr uint32_t IDESC_QK4 = sm100::idesc_bf16_f32(QT, KT4);
+
+struct Attn4Ctl {
+    uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2];
+    uint64_t s_full[2], p_ready[2], pv_done, drain;
+    uint32_t tmem_slot;
+    int abort;
+};
+
+// MN-major V tile of 64 keys: two 64-dim halves KV4_HALF apart, 8-key groups 1 KB apart.
+__device__ __forceinline__ uint64_t desc_v64(const void* tile, uint32_t k_group_bytes) {
+    const uint32_t addr = sm100::smem_u32(tile) + k_group_bytes;
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)(KV4_HALF >> 4) << 16;
+    d |= (uint64_t)(1024u >> 4) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)2u << 61;
+    return d;
+}
+
+__global__ void __launch_bounds__(T4_THREADS, 2)
+k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
+               const __grid_constant__ CUtensorMap tV, const AttnParams p) {
+    const int wi = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * QT;
+    const int f = p.g.cumf[wi + 1] - p.g.cumf[wi];
+    const int S = f + p.g.TXT;
+    if (q0 >= S) return;                       // uniform across the CTA, before any barrier
+    const int nkt = (S + KT4 - 1) / KT4;
+    const int row_base = h * p.g.sumS + p.g.cums[wi];
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;
+    uint8_t* sK = smem + TILE_BYTES;                 // [2] stages
+    uint8_t* sV = smem + TILE_BYTES + 2 * KV4_BYTES; // [2] stages
+    Attn4Ctl* ctl = reinterpret_cast<Attn4Ctl*>(smem + TILE_BYTES + 4 * KV4_BYTES);
+    volatile int* abort_flag = &ctl->abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(&ctl->q_full, 1);
+        for (int i = 0; i < 2; i++) {
+            sm100::mbar_init(&ctl->k_full[i], 1);
+            sm100::mbar_init(&ctl->k_empty[i], 1);
+            sm100::mbar_init(&ctl->v_full[i], 1);
+            sm100::mbar_init(&ctl->v_empty[i], 1);
+            sm100::mbar_init(&ctl->s_full[i], 1);
+            sm100::mbar_init(&ctl->p_ready[i], 4);
+        }
+        sm100::mbar_init(&ctl->pv_done, 1);
+        sm100::mbar_init(&ctl->drain, 1);
+        ctl->abort = 0;
+        sm100::fence_barrier_init();
+    }
+    if (warp == 4) {
+        sm100::tmem_alloc(&ctl->tmem_slot, TMEM_COLS);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = ctl->tmem_slot;
+    const uint32_t tO = tmem + 128;            // S slots at [0, 64) and [64, 128)
+
+    if (warp == 5) {
+        if (lane == 0) {
+            // ---- TMA producer
+            bool ok = true;
+            int kq = 0, vq = 0;                // K / V tiles issued
+            sm100::mbar_arrive_expect_tx(&ctl->q_full, TILE_BYTES);
+            sm100::tma_load_2d(sQ, &tQ, &ctl->q_full, 0, row_base + q0);
+            sm100::tma_load_2d(sQ + HALF_BYTES, &tQ, &ctl->q_full, 64, row_base + q0);
+            for (int j = 0; j < nkt && ok; j++) {
+                const int st = j & 1, r = row_base + j * KT4;
+                const uint32_t eph = (uint32_t)((j >> 1) - 1) & 1;
+                if (j >= 2 && !(ok = wait_bar(&ctl->k_empty[st], eph, abort_flag))) break;
+                sm100::mbar_arrive_expect_tx(&ctl->k_full[st], KV4_BYTES);
+                sm100::tma_load_2d(sK + st * KV4_BYTES, &tK, &ctl->k_full[st], 0, r);
+                sm100::tma_load_2d(sK + st * KV4_BYTES + KV4_HALF, &tK, &ctl->k_full[st], 64, r);
+                kq++;
+                if (j >= 2 && !(ok = wait_bar(&ctl->v_empty[st], eph, abort_flag))) break;
+                sm100::mbar_arrive_expect_tx(&ctl->v_full[st], KV4_BYTES);
+                sm100::tma_load_2d(sV + st * KV4_BYTES, &tV, &ctl->v_full[st], 0, r);
+                sm100::tma_load_2d(sV + st * KV4_BYTES + KV4_HALF, &tV, &ctl->v_full[st], 64, r);
+                vq++;
+            }
+            if (!ok) {
+                // drain this thread's own TMA loads (bounded) before shared memory is released
+                for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->q_full, 0); w++) {}
+                for (int k = (kq > 2 ? kq - 2 : 0); k < kq; k++)
+                    for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->k_full[k & 1], (uint32_t)(k >> 1) & 1); w++) {}
+                for (int k = (vq > 2 ? vq - 2 : 0); k < vq; k++)
+                    for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->v_full[k & 1], (uint32_t)(k >> 1) & 1); w++) {}
+            }
+        }
+    } else if (warp == 4) {
+        if (lane == 0) {
+            // ---- MMA issuer
+            auto issue_s = [&](int j) {
+                const uint8_t* k = sK + (j & 1) * KV4_BYTES;
+                #pragma unroll
+                for (int kk = 0; kk < D / 16; kk++) {
+                    const uint32_t aoff = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
+                    const uint32_t boff = (kk >> 2) * KV4_HALF + (kk & 3) * 32;
+                    sm100::mma_bf16(tmem + (j & 1) * 64, sm100::desc_kmajor_sw128(sQ, aoff),
+                                    sm100::desc_kmajor_sw128(k, boff), IDESC_QK4, kk != 0);
+                }
+                sm100::mma_commit(&ctl->s_full[j & 1]);
+                sm100::mma_commit(&ctl->k_empty[j & 1]);
+            };
+            bool ok = wait_bar(&ctl->q_full, 0, abort_flag);
+            if (ok && (ok = wait_bar(&ctl->k_full[0], 0, abort_flag))) {
+                sm100::tc_fence_after();
+                issue_s(0);
+            }
+            for (int j = 0; j < nkt && ok; j++) {
+                const int st = j & 1;
+                if (j + 1 < nkt) {
+                    if (!(ok = wait_bar(&ctl->k_full[st ^ 1], (uint32_t)((j + 1) >> 1) & 1, abort_flag))) break;
+                    // slot (j+1)&1 held P_{j-1}: its PV must be done
+                    if (j >= 1 && !(ok = wait_bar(&ctl->pv_done, (uint32_t)(j - 1) & 1, abort_flag))) break;
+                    sm100::tc_fence_after();
+                    issue_s(j + 1);
+                }
+                if (!(ok = wait_bar(&ctl->p_ready[st], (uint32_t)(j >> 1) & 1, abort_flag))) break;
+                if (!(ok = wait_bar(&ctl->v_full[st], (uint32_t)(j >> 1) & 1, abort_flag))) break;
+                sm100::tc_fence_after();
+                const uint8_t* v = sV + st * KV4_BYTES;
+                #pragma unroll
+                for (int kk = 0; kk < KT4 / 16; kk++)
+                    sm100::mma_bf16_tmem_a(tO, tmem + st * 64 + kk * 8, desc_v64(v, kk * 2048), IDESC_PV,
+                                           (j | kk) != 0);
+                sm100::mma_commit(&ctl->pv_done);
+                sm100::mma_commit(&ctl->v_empty[st]);
+            }
+            // all of this thread's MMAs done before TMEM / shared memory go away
+            sm100::mma_commit(&ctl->drain);
+            for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->drain, 0); w++) {}
+        }
+    } else {
+        // ---- softmax + epilogue: thread = query row q0 + r; TMEM lane quadrant = warp
+        const int r = warp * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        const float sl = p.scale_log2;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        // tcgen05.ld / st are warp-collective: control flow stays warp-uniform
+        for (int j = 0; j < nkt; j++) {
+            const int st = j & 1;
+            ok = __all_sync(0xffffffffu, wait_bar(&ctl->s_full[st], (uint32_t)(j >> 1) & 1, abort_flag));
+            if (!ok) break;
+            sm100::tc_fence_after();
+            const int kvalid = S - j * KT4;
+            const bool full = kvalid >= KT4;           // CTA-uniform
+            float v[64];
+            sm100::tmem_ld64(tmem + lane_off + st * 64, v);
+            float mr = -INFINITY;
+            if (full) {
+                #pragma unroll
+                for (int u = 0; u < 64; u++) mr = fmaxf(mr, v[u]);
+            } else {
+                #pragma unroll
+                for (int u = 0; u < 64; u++)
+                    if (u < kvalid) mr = fmaxf(mr, v[u]);
+            }
+            const float mx = mr * sl;
+            if (j == 0) {
+                m = mx;
+            } else {
+                const bool grow = mx > m + T_RESCALE;
+                if (__any_sync(0xffffffffu, grow)) {
+                    // the previous PV accumulates into O: wait for it first
+                    ok = __all_sync(0xffffffffu, wait_bar(&ctl->pv_done, (uint32_t)(j - 1) & 1, abort_flag));
+                    if (!ok) break;
+                    sm100::tc_fence_after();
+                    const float mn = grow ? mx : m;
+                    const float corr = exp2f(m - mn);
+                    #pragma unroll 1
+                    for (int c = 0; c < 4; c++) {
+                        float o[32];
+                        sm100::tmem_ld32(tO + lane_off + c * 32, o);
+                        #pragma unroll
+                        for (int u = 0; u < 32; u++) o[u] *= corr;
+                        tmem_st32(tO + lane_off + c * 32, o);
+                    }
+                    l *= corr;
+                    m = mn;
+                }
+            }
+            // P_j as packed bf16 pairs over the slot's columns [0, 32)
+            const float nm = -m;
+            uint32_t pk[32];
+            #pragma unroll
+            for (int u = 0; u < 32; u++) {
+                float a = ex2_approx(fmaf(v[2 * u], sl, nm)), b = ex2_approx(fmaf(v[2 * u + 1], sl, nm));
+                if (!full) { a = (2 * u < kvalid) ? a : 0.f; b = (2 * u + 1 < kvalid) ? b : 0.f; }
+                l += a + b;
+                pk[u] = pack_bf16x2_rn(a, b);
+            }
+            tmem_st32u(tmem + lane_off + st * 64, pk);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(&ctl->p_ready[st]);
+        }
+        if (ok) ok = __all_sync(0xffffffffu, wait_bar(&ctl->pv_done, (uint32_t)(nkt - 1) & 1, abort_flag));
+        if (ok) {
+            sm100::tc_fence_after();
+            const int q = q0 + r;
+            const float inv = 1.f / l;
+            const bool is_vid = q < f, is_txt = (q >= f) && (q < S);
+            float* tdst = p.toutw + ((size_t)wi * p.g.TXT + (is_txt ? q - f : 0)) * 2560 + h * D;
+            const size_t tok = is_vid ? (size_t)p.g.vidx[p.g.cumf[wi] + q] : 0;
+            #pragma unroll 1
+            for (int c = 0; c < 2; c++) {
+                float o[64];
+                sm100::tmem_ld64(tO + lane_off + c * 64, o);
+                #pragma unroll
+                for (int u = 0; u < 64; u++) o[u] *= inv;
+                if (is_vid) {
+                    if (p.att_bf16) {
+                        bf16* dst = (bf16*)p.att + tok * p.ld_att + h * D + c * 64;
+                        #pragma unroll
+                        for (int u = 0; u < 64; u += 4) store4(dst + u, o + u);
+                    } else {
+                        float* dst = (float*)p.att + tok * p.ld_att + h * D + c * 64;
+                        #pragma unroll
+                        for (int u = 0; u < 64; u += 4) store4(dst + u, o + u);
+                    }
+                } else if (is_txt) {
+                    #pragma unroll
+                    for (int u = 0; u < 64; u += 4) store4(tdst + c * 64 + u, o + u);
+                }
+            }
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        sm100::tc_fence_after();
+        sm100::tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
 }  // namespace
 
 bool awa_tc_available() { return true; }
@@ -724,7 +990,13 @@ int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, const AwaDev& 
     p.ld_att = ld_att;
     p.att_bf16 = (at == ACT_BF16);
     p.toutw = toutw;
-    if (awa_tc_kernel_version() == 1) {
+    if (awa_tc_kernel_version() == 3) {
+        CUtensorMap tk4, tv4;
+        if (!make_tmap_bf16(&tk4, Kp, rows, D, D, KT4, 64) || !make_tmap_bf16(&tv4, Vp, rows, D, D, KT4, 64))
+            return -1;
+        dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
+        k_awa_attn_tc4<<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
+    } else if (awa_tc_kernel_version() == 1) {
         dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
         if (awa_tc_poly_exp())
             k_awa_attn_tc<true><<<grid, NUM_THREADS, SMEM_BYTES, s>>>(tq, tk, tv, p);
@@ -752,6 +1024,8 @@ int awa_tc_init_device() {
         return (int)e;
     if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES))
         return (int)e;
+    if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc4, cudaFuncAttributeMaxDynamicSharedMemorySize, T4_SMEM))
+        return (int)e;
     if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc2<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, T2_SMEM))
         return (int)e;
     return (int)cudaFuncSetAttribute(k_awa_attn_tc2<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, T2_SMEM);
@@ -770,7 +1044,7 @@ int awa_tc_poly_exp() {
 // 3.2 ms per forward, kept for other geometries and further work).
 int awa_tc_kernel_version() {
     const char* e = std::getenv("S2B_ATTN_KERNEL");
-    return (e && e[0] == '2') ? 2 : 1;
+    return (e && e[0] == '2') ? 2 : (e && e[0] == '3') ? 3 : 1;
 }
 
 int awa_tc_error_reset(int* had_error) {

@@ -49,10 +49,19 @@ constexpr int SMEM1_BYTES = STAGES1 * STAGE1_BYTES + RES_BYTES + 1024 + 512;
 constexpr uint32_t IDESC1 = sm100::idesc_bf16_f32(BM1, BN1);
 
 // CTA-pair kernel: per CTA 128 rows of A and 128 rows of B per stage
-constexpr int BM2 = 256, BN2 = 256, STAGES2 = 6;
-constexpr int A2_BYTES = 128 * BK * 2, B2_BYTES = 128 * BK * 2, STAGE2_BYTES = A2_BYTES + B2_BYTES;
-constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + RES_BYTES + 1024 + 512;
-constexpr uint32_t IDESC2 = sm100::idesc_bf16_f32(BM2, BN2);
+// Tiles of BM2 x BN rows per pair (BN = 256, or 128 where 256-wide tiles
+// would leave much of the last wave idle); each CTA stages 128 A rows and
+// BN / 2 B rows per k-block.
+constexpr int BM2 = 256;
+template <int BN>
+struct PairCfg {
+    static constexpr int STAGES = BN == 256 ? 6 : 8;
+    static constexpr int A_BYTES = 128 * BK * 2;
+    static constexpr int B_BYTES = (BN / 2) * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + RES_BYTES + 1024 + 512;
+    static constexpr uint32_t IDESC = sm100::idesc_bf16_f32(BM2, BN);
+};
 
 __device__ int g_tc_err;
 
@@ -131,6 +140,7 @@ __device__ __forceinline__ void rope64(float* x, int d0, const float2* __restric
 // the division as a reciprocal multiply: this epilogue serves the bf16 path)
 // and RoPE, v heads pass through; each row lands in its window-packed slot(s)
 // (a txt row in every window, with the same angles in each).
+template <int BN>
 __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t taddr, int row, int n0) {
     const PackEpi& k = p.e.pk;
     bool row_ok = row < p.M;
@@ -151,7 +161,7 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
     // two passes over each head's 128 TMEM columns (sum of squares, then
     // normalise + rotate + store 64 dims at a time) keep 64 values live
     #pragma unroll 1
-    for (int hh = 0; hh < 2; hh++) {
+    for (int hh = 0; hh < BN / 128; hh++) {
         const uint32_t th = taddr + hh * 128;
         float inv = 1.f;
         if (sec < 2) {
@@ -202,10 +212,10 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
 // Epilogue of one accumulator row (thread = TMEM lane = output row) over the
 // tile's 256 columns starting at n0.  The tcgen05.ld are warp-collective and
 // executed by every lane; only the stores depend on the row.
-template <int MODE>
+template <int MODE, int BN = 256>
 __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, int row, int n0) {
     const GemmEpi& e = p.e;
-    if constexpr (MODE == EPI_QKV_PACK) { epilogue_qkv_pack(p, taddr, row, n0); return; }
+    if constexpr (MODE == EPI_QKV_PACK) { epilogue_qkv_pack<BN>(p, taddr, row, n0); return; }
     const bool row_ok = row < p.M;
     if constexpr (MODE == EPI_SWIGLU) {
         // column block [h 128 | g 128] -> 128 outputs at n0 / 2
@@ -230,7 +240,7 @@ __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, 
         // loads never queue behind the previous chunk's stores.
         float* __restrict__ rrow = e.resid + (size_t)row * e.ldr;
         #pragma unroll 1
-        for (int c0 = 0; c0 < 256; c0 += 32) {
+        for (int c0 = 0; c0 < BN; c0 += 32) {
             if (n0 + c0 >= p.N) break;         // warp-uniform
             const int col = n0 + c0;
             const bool full = col + 32 <= p.N;
@@ -268,7 +278,7 @@ __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, 
         return;
     } else {
         #pragma unroll 1
-        for (int c0 = 0; c0 < 256; c0 += 32) {
+        for (int c0 = 0; c0 < BN; c0 += 32) {
             if (n0 + c0 >= p.N) break;             // warp-uniform
             float v[32];
             sm100::tmem_ld32(taddr + c0, v);
@@ -321,12 +331,12 @@ __device__ __forceinline__ void resid_load(const CUtensorMap* tR, ResidPipe& rp,
 // Returns false when a wait expired (the tile is abandoned).
 __device__ __forceinline__ bool epilogue_resid_tma(const TcParams& p, const CUtensorMap* tR, uint32_t taddr, int r0,
                                                    int n0, const CUtensorMap* tR_next, int next_r0, int next_n0,
-                                                   ResidPipe& rp, volatile int* abort_flag) {
+                                                   ResidPipe& rp, volatile int* abort_flag, int bn = 256) {
     const GemmEpi& e = p.e;
     const int lane = threadIdx.x & 31;
     const int row = r0 + lane;
     const float* gate = (row < e.gate_split) ? e.gate0 : e.gate1;
-    const int nch = min(8, (p.N - n0) / 32);
+    const int nch = min(bn / 32, (p.N - n0) / 32);
     for (int c = 0; c < nch; c++) {
         const int col = n0 + 32 * c;
         float v[32];
@@ -518,10 +528,13 @@ __device__ __forceinline__ TileRef tile_ref(const TcParams& p0, const TcParams& 
     return t;
 }
 
-template <int MODE>
+template <int MODE, int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ TcParams p0,
                const __grid_constant__ TcParams p1, int ngroups) {
+    using C = PairCfg<BN>;
+    constexpr int STAGES2 = C::STAGES, A2_BYTES = C::A_BYTES, B2_BYTES = C::B_BYTES, STAGE2_BYTES = C::STAGE_BYTES;
+    constexpr int ACC = BN;                                 // TMEM columns per accumulator
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -571,7 +584,7 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
                     if (rank == 0) sm100::mbar_arrive_expect_tx(&ctl->full[stage], 2 * STAGE2_BYTES);
                     const uint32_t fb = sm100::map_to_rank(&ctl->full[stage], 0);
                     sm100::tma_load_2d_pair(sA + stage * A2_BYTES, ta, fb, kb * BK, t.mb * BM2 + (int)rank * 128);
-                    sm100::tma_load_2d_pair(sB + stage * B2_BYTES, tb, fb, kb * BK, t.nb * BN2 + (int)rank * 128);
+                    sm100::tma_load_2d_pair(sB + stage * B2_BYTES, tb, fb, kb * BK, t.nb * BN + (int)rank * (BN / 2));
                     issued++;
                     if (++stage == STAGES2) { stage = 0; phase ^= 1; }
                 }
@@ -596,7 +609,7 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
                 const uint32_t acc_phase = (it >> 1) & 1;
                 if (!wait_or_abort(&ctl->tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
                 sm100::tc_fence_after();
-                const uint32_t d = tmem_base + acc * ACC_COLS;
+                const uint32_t d = tmem_base + acc * ACC;
                 for (int kb = 0; kb < num_kb; kb++) {
                     if (!wait_or_abort(&ctl->full[stage], phase, abort_flag)) { ok = false; break; }
                     sm100::tc_fence_after();
@@ -605,7 +618,7 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
                     #pragma unroll
                     for (int kk = 0; kk < BK / 16; kk++)
                         sm100::mma_bf16_pair(d, sm100::desc_kmajor_sw128(a, kk * 32),
-                                             sm100::desc_kmajor_sw128(b, kk * 32), IDESC2, (kb | kk) != 0);
+                                             sm100::desc_kmajor_sw128(b, kk * 32), C::IDESC, (kb | kk) != 0);
                     // release this stage in both CTAs
                     sm100::mma_commit_pair(sm100::map_to_rank(&ctl->empty[stage], 0));
                     sm100::mma_commit_pair(sm100::map_to_rank(&ctl->empty[stage], 1));
@@ -625,7 +638,7 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
         const bool rt = MODE == EPI_GATE_RESID && p0.resid_tma;
         if (rt && lane == 0 && pair < num_tiles) {
             const TileRef t = tile_ref(p0, p1, tiles0, pair);
-            resid_load(&maps.r[t.grp], rp, t.nb * BN2, t.mb * BM2 + rbase);
+            resid_load(&maps.r[t.grp], rp, t.nb * BN, t.mb * BM2 + rbase);
         }
         int it = 0;
         for (int tile = pair; tile < num_tiles; tile += npairs, it++) {
@@ -635,17 +648,17 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
             sm100::tc_fence_after();
             const TileRef t = tile_ref(p0, p1, tiles0, tile);
             const TcParams& p = t.grp ? p1 : p0;
-            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * ACC_COLS;
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + acc * ACC;
             const int nt = tile + npairs;
             const bool more = nt < num_tiles;
             const TileRef u = tile_ref(p0, p1, tiles0, more ? nt : tile);
             if (rt) {
-                if (!epilogue_resid_tma(p, &maps.r[t.grp], taddr, t.mb * BM2 + rbase, t.nb * BN2, &maps.r[u.grp],
-                                        u.mb * BM2 + rbase, more ? u.nb * BN2 : -1, rp, abort_flag))
+                if (!epilogue_resid_tma(p, &maps.r[t.grp], taddr, t.mb * BM2 + rbase, t.nb * BN, &maps.r[u.grp],
+                                        u.mb * BM2 + rbase, more ? u.nb * BN : -1, rp, abort_flag, BN))
                     break;
             } else {
-                if (more) prefetch_resid<MODE>(u.grp ? p1 : p0, u.mb * BM2 + rbase + lane, u.nb * BN2);
-                epilogue_row<MODE>(p, taddr, t.mb * BM2 + rbase + lane, t.nb * BN2);
+                if (more) prefetch_resid<MODE>(u.grp ? p1 : p0, u.mb * BM2 + rbase + lane, u.nb * BN);
+                epilogue_row<MODE, BN>(p, taddr, t.mb * BM2 + rbase + lane, t.nb * BN);
             }
             sm100::tc_fence_before();
             __syncwarp();
@@ -731,7 +744,7 @@ static bool gemm_args_ok(const void* A, int lda, const void* W, int ldw, int M, 
 }
 
 // Parameters and tensor maps of one pair-kernel group (256-row A boxes).
-static bool pair_group(const void* A, int lda, const void* W, int ldw, int M, int N, int K, const GemmEpi& e,
+static bool pair_group(const void* A, int lda, const void* W, int ldw, int M, int N, int K, const GemmEpi& e, int bn,
                        TcParams& p, CUtensorMap& ta, CUtensorMap& tb, CUtensorMap& tr) {
     p.M = M; p.N = N;
     p.num_kb = (K + BK - 1) / BK;
@@ -740,22 +753,45 @@ static bool pair_group(const void* A, int lda, const void* W, int ldw, int M, in
     p.resid_tma = e.mode == EPI_GATE_RESID && e.resid && ((uintptr_t)e.resid & 15) == 0 && e.ldr % 4 == 0 &&
                   make_tmap_resid(&tr, e.resid, M, N, e.ldr);
     if (!p.resid_tma) std::memset(&tr, 0, sizeof tr);
-    if (!make_tmap_bf16(&ta, A, M, K, lda, 128, BK) || !make_tmap_bf16(&tb, W, N, K, ldw, 128, BK)) return false;
+    if (!make_tmap_bf16(&ta, A, M, K, lda, 128, BK) || !make_tmap_bf16(&tb, W, N, K, ldw, bn / 2, BK)) return false;
     p.num_m = (M + BM2 - 1) / BM2;
-    p.num_n = (N + BN2 - 1) / BN2;
+    p.num_n = (N + bn - 1) / bn;
     return true;
 }
 
-static void launch_pair(const PairMaps& maps, const TcParams& p0, const TcParams& p1, int ngroups, cudaStream_t s) {
+// Tile width of the pair kernel: 128 when 256-wide tiles would leave much of
+// the GPU idle, never for SwiGLU (its tiles hold matching [h | g] halves).  A
+// 128-wide tile takes about 2/3 of a 256-wide one's time (half the FLOPs, but
+// TMA writes plus MMA reads of the A tile then exceed the shared-memory
+// bandwidth), so it pays only when it removes whole waves.
+static int pick_bn(int tiles_m, int N, EpiMode mode, int pairs) {
+    if (mode == EPI_SWIGLU || N % 128) return 256;
+    const long t256 = (long)tiles_m * ((N + 255) / 256), t128 = (long)tiles_m * ((N + 127) / 128);
+    const double w256 = (double)((t256 + pairs - 1) / pairs), w128 = (double)((t128 + pairs - 1) / pairs);
+    return (0.67 * w128 < 0.95 * w256) ? 128 : 256;
+}
+
+template <int BN>
+static void launch_pair_bn(const PairMaps& maps, const TcParams& p0, const TcParams& p1, int ngroups, int pairs,
+                           cudaStream_t s) {
+    constexpr int SM = PairCfg<BN>::SMEM;
+    switch (p0.e.mode) {
+        case EPI_STORE: k_gemm_tc_pair<EPI_STORE, BN><<<2 * pairs, NUM_THREADS, SM, s>>>(maps, p0, p1, ngroups); break;
+        case EPI_GATE_RESID: k_gemm_tc_pair<EPI_GATE_RESID, BN><<<2 * pairs, NUM_THREADS, SM, s>>>(maps, p0, p1, ngroups); break;
+        case EPI_SWIGLU:
+            if constexpr (BN == 256) k_gemm_tc_pair<EPI_SWIGLU, 256><<<2 * pairs, NUM_THREADS, SM, s>>>(maps, p0, p1, ngroups);
+            break;
+        case EPI_QKV_PACK: k_gemm_tc_pair<EPI_QKV_PACK, BN><<<2 * pairs, NUM_THREADS, SM, s>>>(maps, p0, p1, ngroups); break;
+    }
+}
+
+static void launch_pair(const PairMaps& maps, const TcParams& p0, const TcParams& p1, int ngroups, int bn,
+                        cudaStream_t s) {
     const int tiles = p0.num_m * p0.num_n + (ngroups > 1 ? p1.num_m * p1.num_n : 0);
     int pairs = num_sms() / 2;
     if (tiles < pairs) pairs = tiles;
-    switch (p0.e.mode) {
-        case EPI_STORE: k_gemm_tc_pair<EPI_STORE><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(maps, p0, p1, ngroups); break;
-        case EPI_GATE_RESID: k_gemm_tc_pair<EPI_GATE_RESID><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(maps, p0, p1, ngroups); break;
-        case EPI_SWIGLU: k_gemm_tc_pair<EPI_SWIGLU><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(maps, p0, p1, ngroups); break;
-        case EPI_QKV_PACK: k_gemm_tc_pair<EPI_QKV_PACK><<<2 * pairs, NUM_THREADS, SMEM2_BYTES, s>>>(maps, p0, p1, ngroups); break;
-    }
+    if (bn == 128) launch_pair_bn<128>(maps, p0, p1, ngroups, pairs, s);
+    else launch_pair_bn<256>(maps, p0, p1, ngroups, pairs, s);
 }
 
 int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K, const GemmEpi& e, cudaStream_t s,
@@ -765,8 +801,9 @@ int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K,
         // CTA pairs: 256 x 256 tiles, grid = one cluster of 2 per SM pair
         PairMaps maps;
         TcParams p;
-        if (!pair_group(A, lda, W, ldw, M, N, K, e, p, maps.a[0], maps.b[0], maps.r[0])) return -1;
-        launch_pair(maps, p, p, 1, s);
+        const int bn = pick_bn((M + BM2 - 1) / BM2, N, e.mode, num_sms() / 2);
+        if (!pair_group(A, lda, W, ldw, M, N, K, e, bn, p, maps.a[0], maps.b[0], maps.r[0])) return -1;
+        launch_pair(maps, p, p, 1, bn, s);
     } else {
         TcParams p;
         p.M = M; p.N = N;
@@ -800,11 +837,12 @@ int gemm_tc_grouped(const void* A0, int lda0, const void* W0, int ldw0, int M0, 
     if (!gemm_args_ok(A0, lda0, W0, ldw0, M0, N, K, e0) || !gemm_args_ok(A1, lda1, W1, ldw1, M1, N, K, e1)) return -1;
     PairMaps maps;
     TcParams p0, p1;
-    if (!pair_group(A0, lda0, W0, ldw0, M0, N, K, e0, p0, maps.a[0], maps.b[0], maps.r[0]) ||
-        !pair_group(A1, lda1, W1, ldw1, M1, N, K, e1, p1, maps.a[1], maps.b[1], maps.r[1]))
+    const int bn = pick_bn((M0 + BM2 - 1) / BM2 + (M1 + BM2 - 1) / BM2, N, e0.mode, num_sms() / 2);
+    if (!pair_group(A0, lda0, W0, ldw0, M0, N, K, e0, bn, p0, maps.a[0], maps.b[0], maps.r[0]) ||
+        !pair_group(A1, lda1, W1, ldw1, M1, N, K, e1, bn, p1, maps.a[1], maps.b[1], maps.r[1]))
         return -1;
     if (p0.resid_tma != p1.resid_tma) return -1;    // one residual path for the whole launch
-    launch_pair(maps, p0, p1, 2, s);
+    launch_pair(maps, p0, p1, 2, bn, s);
     if (launches) (*launches)++;
     return 0;
 }
@@ -827,11 +865,14 @@ int kernels_init_device() {
     if (dev < 64) cudaDeviceGetAttribute(&g_num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
     const void* single[4] = {(const void*)k_gemm_tc<EPI_STORE>, (const void*)k_gemm_tc<EPI_GATE_RESID>,
                              (const void*)k_gemm_tc<EPI_SWIGLU>, (const void*)k_gemm_tc<EPI_QKV_PACK>};
-    const void* pairk[4] = {(const void*)k_gemm_tc_pair<EPI_STORE>, (const void*)k_gemm_tc_pair<EPI_GATE_RESID>,
-                            (const void*)k_gemm_tc_pair<EPI_SWIGLU>, (const void*)k_gemm_tc_pair<EPI_QKV_PACK>};
+    const void* pairk[4] = {(const void*)k_gemm_tc_pair<EPI_STORE, 256>, (const void*)k_gemm_tc_pair<EPI_GATE_RESID, 256>,
+                            (const void*)k_gemm_tc_pair<EPI_SWIGLU, 256>, (const void*)k_gemm_tc_pair<EPI_QKV_PACK, 256>};
+    const void* pairn[3] = {(const void*)k_gemm_tc_pair<EPI_STORE, 128>, (const void*)k_gemm_tc_pair<EPI_GATE_RESID, 128>,
+                            (const void*)k_gemm_tc_pair<EPI_QKV_PACK, 128>};
     for (int i = 0; i < 4; i++) {
         cudaError_t e = cudaFuncSetAttribute(single[i], cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1_BYTES);
-        if (e == cudaSuccess) e = cudaFuncSetAttribute(pairk[i], cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(pairk[i], cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg<256>::SMEM);
+        if (e == cudaSuccess && i < 3) e = cudaFuncSetAttribute(pairn[i], cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg<128>::SMEM);
         if (e != cudaSuccess) return (int)e;
     }
     if (int rc = awa_tc_init_device()) return rc;

@@ -9,8 +9,11 @@ import pytest
 import s2b
 
 pytestmark = pytest.mark.gpu
+# (2750, 2560, 2560) and (700, 2560, 2560) take the 128-wide pair tiles (the 256-wide ones would
+# leave most of a last wave idle); the others the 256-wide or single-CTA kernels.
 SHAPES = [(128, 256, 64), (5498, 7680, 2560), (58, 2560, 2560), (300, 13824, 2560), (1000, 2560, 6912),
-          (77, 64, 2560), (640, 2560, 136), (200, 2560, 132), (1, 2560, 256), (129, 288, 72)]
+          (77, 64, 2560), (640, 2560, 136), (200, 2560, 132), (1, 2560, 256), (129, 288, 72),
+          (2750, 2560, 2560), (700, 2560, 2560)]
 
 
 @pytest.fixture(scope="module", params=[s2b.PREC_FP32, s2b.PREC_BF16], ids=["fp32", "bf16"])
