@@ -117,6 +117,20 @@ __device__ __forceinline__ uint32_t pack_bf16x2_rn(float a, float b) {
     return __byte_perm(ua, ub, 0x7632);
 }
 
+// Max of n (<= 64) leading values of v, -inf for the rest, through 8
+// independent accumulators (a chain of 8 instead of 64 dependent fmaxf).
+__device__ __forceinline__ float max64(const float* v, int nvalid) {
+    float a[8];
+    #pragma unroll
+    for (int i = 0; i < 8; i++) a[i] = -INFINITY;
+    #pragma unroll
+    for (int u = 0; u < 64; u++) a[u & 7] = fmaxf(a[u & 7], (u < nvalid) ? v[u] : -INFINITY);
+    return fmaxf(fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3])), fmaxf(fmaxf(a[4], a[5]), fmaxf(a[6], a[7])));
+}
+__device__ __forceinline__ float sum8(const float* a) {
+    return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+}
+
 // 2^x on the FMA/ALU pipes, for x <= ~8 (softmax exponents): Cody-Waite
 // split x = j + f with j = round(x) (adding 1.5 * 2^23 rounds to an integer
 // in the low mantissa bits) and |f| <= 1/2, 2^f by a cubic fitted here by
@@ -251,14 +265,7 @@ k_awa_attn_tc(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CU
             for (int c = 0; c < 2; c++) {
                 float v[64];
                 sm100::tmem_ld64(tS + lane_off + c * 64, v);
-                if (full) {
-                    #pragma unroll
-                    for (int u = 0; u < 64; u++) mr = fmaxf(mr, v[u]);
-                } else {
-                    #pragma unroll
-                    for (int u = 0; u < 64; u++)
-                        if (c * 64 + u < kvalid) mr = fmaxf(mr, v[u]);
-                }
+                mr = fmaxf(mr, max64(v, full ? 64 : kvalid - c * 64));
             }
             const float mx = mr * p.scale_log2;
             // A row keeps the max its exponentials use until a tile's max
@@ -287,6 +294,7 @@ k_awa_attn_tc(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CU
             }
             // pass 2: P row -> shared memory, K-major 128-B swizzled [128 rows x 128 keys]
             const float sl = p.scale_log2, nm = -m;
+            float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             #pragma unroll
             for (int half = 0; half < 2; half++) {
                 float v[64];
@@ -300,7 +308,7 @@ k_awa_attn_tc(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CU
                         const float x = fmaf(v[chunk * 8 + t], sl, nm);
                         pv[t] = (!full && k >= kvalid) ? 0.f
                               : (POLY && (t & 3) == 3) ? ex2_poly(x) : ex2_approx(x);
-                        l += pv[t];
+                        ls[t] += pv[t];
                     }
                     uint4 u;
                     u.x = pack_bf16x2_rn(pv[0], pv[1]); u.y = pack_bf16x2_rn(pv[2], pv[3]);
@@ -309,6 +317,7 @@ k_awa_attn_tc(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CU
                     *reinterpret_cast<uint4*>(dst) = u;
                 }
             }
+            l += sum8(ls);
             sm100::fence_proxy_async_smem();      // generic-proxy smem writes -> tensor-core reads
             sm100::tc_fence_before();
             __syncwarp();
@@ -606,14 +615,7 @@ k_awa_attn_tc2(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
                 for (int c = 0; c < 2; c++) {
                     float v[64];
                     sm100::tmem_ld64(tS + c * 64, v);
-                    if (full) {
-                        #pragma unroll
-                        for (int u = 0; u < 64; u++) mr = fmaxf(mr, v[u]);
-                    } else {
-                        #pragma unroll
-                        for (int u = 0; u < 64; u++)
-                            if (c * 64 + u < kvalid) mr = fmaxf(mr, v[u]);
-                    }
+                    mr = fmaxf(mr, max64(v, full ? 64 : kvalid - c * 64));
                 }
                 const float mx = mr * sl;
                 if (j == 0) {
@@ -639,6 +641,7 @@ k_awa_attn_tc2(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
                 // pass 2: P_t as packed bf16 pairs over S_t's columns [0, 64);
                 // keys [64h, 64h+64) land in columns [32h, 32h+32), already read
                 const float nm = -m;
+                float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
                 #pragma unroll
                 for (int hlf = 0; hlf < 2; hlf++) {
                     float v[64];
@@ -652,11 +655,12 @@ k_awa_attn_tc2(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
                         if (POLY && (u & 3) == 3) { a = ex2_poly(xa); b = ex2_poly(xb); }
                         else { a = ex2_approx(xa); b = ex2_approx(xb); }
                         if (!full) { a = (k < kvalid) ? a : 0.f; b = (k + 1 < kvalid) ? b : 0.f; }
-                        l += a + b;
+                        ls[u & 7] += a + b;
                         pk[u] = pack_bf16x2_rn(a, b);
                     }
                     tmem_st32u(tS + hlf * 32, pk);
                 }
+                l += sum8(ls);
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 sm100::tc_fence_before();
                 __syncwarp();
@@ -731,7 +735,7 @@ constexpr uint32_t IDESC_QK4 = sm100::idesc_bf16_f32(QT, KT4);
 
 struct Attn4Ctl {
     uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2];
-    uint64_t s_full[2], p_ready[2], pv_done, drain;
+    uint64_t s_full[2], p_ready[2], pv_done, o_full, drain;
     uint32_t tmem_slot;
     int abort;
 };
@@ -778,6 +782,7 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
             sm100::mbar_init(&ctl->p_ready[i], 4);
         }
         sm100::mbar_init(&ctl->pv_done, 1);
+        sm100::mbar_init(&ctl->o_full, 1);
         sm100::mbar_init(&ctl->drain, 1);
         ctl->abort = 0;
         sm100::fence_barrier_init();
@@ -862,6 +867,7 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
                                            (j | kk) != 0);
                 sm100::mma_commit(&ctl->pv_done);
                 sm100::mma_commit(&ctl->v_empty[st]);
+                if (j + 1 == nkt) sm100::mma_commit(&ctl->o_full);
             }
             // all of this thread's MMAs done before TMEM / shared memory go away
             sm100::mma_commit(&ctl->drain);
@@ -884,16 +890,7 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
             const bool full = kvalid >= KT4;           // CTA-uniform
             float v[64];
             sm100::tmem_ld64(tmem + lane_off + st * 64, v);
-            float mr = -INFINITY;
-            if (full) {
-                #pragma unroll
-                for (int u = 0; u < 64; u++) mr = fmaxf(mr, v[u]);
-            } else {
-                #pragma unroll
-                for (int u = 0; u < 64; u++)
-                    if (u < kvalid) mr = fmaxf(mr, v[u]);
-            }
-            const float mx = mr * sl;
+            const float mx = max64(v, full ? 64 : kvalid) * sl;
             if (j == 0) {
                 m = mx;
             } else {
@@ -920,20 +917,24 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
             // P_j as packed bf16 pairs over the slot's columns [0, 32)
             const float nm = -m;
             uint32_t pk[32];
+            float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             #pragma unroll
             for (int u = 0; u < 32; u++) {
                 float a = ex2_approx(fmaf(v[2 * u], sl, nm)), b = ex2_approx(fmaf(v[2 * u + 1], sl, nm));
                 if (!full) { a = (2 * u < kvalid) ? a : 0.f; b = (2 * u + 1 < kvalid) ? b : 0.f; }
-                l += a + b;
+                ls[u & 7] += a + b;
                 pk[u] = pack_bf16x2_rn(a, b);
             }
+            l += sum8(ls);
             tmem_st32u(tmem + lane_off + st * 64, pk);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             sm100::tc_fence_before();
             __syncwarp();
             if (lane == 0) sm100::mbar_arrive(&ctl->p_ready[st]);
         }
-        if (ok) ok = __all_sync(0xffffffffu, wait_bar(&ctl->pv_done, (uint32_t)(nkt - 1) & 1, abort_flag));
+        // O is final once every PV is done (a barrier of its own: pv_done may
+        // still be two phases behind here, which its parity cannot tell apart)
+        if (ok) ok = __all_sync(0xffffffffu, wait_bar(&ctl->o_full, 0, abort_flag));
         if (ok) {
             sm100::tc_fence_after();
             const int q = q0 + r;
