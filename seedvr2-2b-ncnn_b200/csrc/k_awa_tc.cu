@@ -1,25 +1,23 @@
 // k_awa_tc.cu -- AWA window attention on the 5th-gen tensor cores (bf16).
 //
-// One CTA = one (window, head, 128-query tile).  Keys of the window are
-// streamed in 128-key tiles; all operands come from the window-packed,
-// head-major Q/K/V slabs the pack kernel writes (k_awa.cu), so every tile is
-// a plain 2-D TMA box.
-//   S_j  = Q K_j^T        tcgen05.mma, A = Q, B = K_j (both K-major, 128-B
-//                         swizzle), fp32 accumulator in TMEM (128 columns)
-//   softmax (warps 0-3)   thread = query row: tcgen05.ld of its S row,
-//                         online max / sum in fp32 (exp2), O rescaled in
-//                         TMEM when the running max grows, P_j rounded to
-//                         bf16 and written to shared memory in the K-major
-//                         swizzled layout, over K_j's spent tile
-//   O   += P_j V_j        tcgen05.mma, A = P_j (K-major), B = V_j
-//                         (MN-major: head dims contiguous), TMEM 128 columns
-//   epilogue              O / l; vid rows go back to their grid token, txt
-//                         rows to the per-window partials averaged later.
-// Warp 4 lane 0 issues the TMA loads and the MMAs.  Keys past the window's
-// end are masked to -inf (their smem rows hold the neighbouring window's
-// finite data or TMA zero fill).  96 KB shared memory and 256 TMEM columns
-// per CTA, so two CTAs share an SM and one's softmax overlaps the other's
-// MMAs.  Every mbarrier wait is bounded (error flag g_attn_err on expiry).
+// All operands come from the window-packed, head-major Q/K/V slabs the QKV
+// GEMM epilogue (or the pack kernel, k_awa.cu) writes, so every tile is a
+// plain 2-D TMA box; vid outputs go back to their grid token, txt outputs to
+// the per-window partials averaged later.  Keys past the window's end are
+// masked (their shared-memory rows hold the neighbouring window's finite data
+// or TMA zero fill).  Three kernels:
+//   k_awa_attn_tc4 (default)  one CTA per (window, head, 128-query tile), two
+//                             CTAs per SM, 64-key K/V tiles double-buffered;
+//                             S in two TMEM slots, P written back into TMEM
+//                             and used as the A operand of O += P V.
+//   k_awa_attn_tc             128-key tiles, P through shared memory over
+//                             the spent K tile.
+//   k_awa_attn_tc2            persistent, two query tiles per CTA sharing
+//                             every K/V tile (ping-pong softmax warpgroups).
+// Softmax: one query row per thread, ex2.approx, bf16 packing on the integer
+// ALU, lazy O rescale (only when a row's max grows by more than 2^8, so
+// P <= 2^8).  Every mbarrier wait is bounded (error flag g_attn_err on
+// expiry); warp-collective TMEM instructions run under warp-uniform control.
 #include "kernels.h"
 #include "kcommon.cuh"
 #include "sm100.cuh"
@@ -1040,12 +1038,13 @@ int awa_tc_poly_exp() {
     return (e && e[0] == '1') ? 1 : 0;
 }
 
-// 1 = one 128-query tile per CTA, two CTAs per SM (default); 2 = the
-// persistent two-tile kernel (S2B_ATTN_KERNEL=2; at 1080p 4.3 ms against
-// 3.2 ms per forward, kept for other geometries and further work).
+// 3 = 64-key tiles, double-buffered K/V, P in TMEM (default);
+// 1 = 128-key tiles, P in shared memory (S2B_ATTN_KERNEL=1);
+// 2 = the persistent two-tile kernel (S2B_ATTN_KERNEL=2).
+// Per 1080p forward (same process, alternating): 3.0-3.3 ms, 3.0-3.6 ms, 4.7-4.8 ms.
 int awa_tc_kernel_version() {
     const char* e = std::getenv("S2B_ATTN_KERNEL");
-    return (e && e[0] == '2') ? 2 : (e && e[0] == '3') ? 3 : 1;
+    return (e && e[0] == '2') ? 2 : (e && e[0] == '1') ? 1 : 3;
 }
 
 int awa_tc_error_reset(int* had_error) {
