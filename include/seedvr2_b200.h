@@ -21,6 +21,7 @@
  */
 #ifndef SEEDVR2_B200_H
 #define SEEDVR2_B200_H
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -119,6 +120,40 @@ int s2b_forward_grid(s2b_ctx* ctx, const float* vid_grid, int T, int H, int W, c
 int s2b_patchify_grid(const float* vid_grid, int T, int H, int W, float* vid_patch);
 int s2b_unpatchify_latent(const float* sr, int T, int H, int W, float* sr_latent);
 
+/* One file of the m5 model directory held in memory (name as in the
+ * directory, e.g. "b0_vid_qkv.param", "b0_vid_qkv.bin", "b0_vid_nq.bin"). */
+typedef struct s2b_weight_file {
+    const char* name;
+    const void* data;
+    size_t bytes;
+} s2b_weight_file;
+/* s2b_load_weights_dir with the directory's files supplied in memory (for a
+ * host that already holds the model, e.g. from an archive); the same layout
+ * and checks (src/dit_vk.cpp:140-177 reads these files one by one). */
+int s2b_load_weights_mem(s2b_ctx* ctx, const s2b_weight_file* files, int nfiles, int layer_lo, int layer_hi);
+
+/* ---- device-side data formats around the DiT --------------------------- */
+/* DitVk::forward_grid (src/dit_vk.cpp:752-763) on device buffers, ordered on
+ * `stream` (cudaStream_t): patchify, the captured 32-layer forward and
+ * unpatchify run on the GPU.  d_vid_grid (T, H, W, 33), d_txt (TXT, 5120),
+ * d_sr_grid (T, H, W, 16), all fp32; H and W even. */
+int s2b_forward_grid_dev(s2b_ctx* ctx, const float* d_vid_grid, int T, int H, int W, const float* d_txt, int TXT,
+                         float timestep, float* d_sr_grid, void* stream);
+/* patchify_grid / unpatchify_latent (src/dit_vk.cpp:717-750) as kernels on
+ * device buffers; no context needed. */
+int s2b_patchify_grid_dev(const float* d_vid_grid, int T, int H, int W, float* d_vid_patch, void* stream);
+int s2b_unpatchify_latent_dev(const float* d_sr, int T, int H, int W, float* d_sr_grid, void* stream);
+/* The engine's DiT input assembly (src/seedvr2_engine.cpp:154-168): vid_grid
+ * (H8, W8, 33) = [noise | latent * scaling | 1] from channel-first (16, H8,
+ * W8) noise and condition latent (the engine passes scaling 0.9152,
+ * src/seedvr2_engine.cpp:22). */
+int s2b_assemble_vid_grid_dev(const float* d_noise, const float* d_latent, float scaling, int H8, int W8,
+                              float* d_vid_grid, void* stream);
+/* The engine's step after the DiT (src/seedvr2_engine.cpp:298-305): z
+ * (16, H8, W8) = (noise - sr) / scaling with sr channel-last (H8, W8, 16). */
+int s2b_decode_latent_dev(const float* d_noise, const float* d_sr_grid, float scaling, int H8, int W8, float* d_z,
+                          void* stream);
+
 /* ---- AWA operator ---------------------------------------------------- */
 /* Replaces AwaVk::forward (src/awa_vk.h:39-44, src/awa_vk.cpp:114-251) and
  * the CPU attention branch of DitVk::awa_forward (src/dit_vk.cpp:344-455):
@@ -196,6 +231,23 @@ int s2b_synth_txt(float* txt, int TXT, uint64_t seed);
 int s2b_synth_normal(float* out, long n, uint64_t seed, const char* stream, float mean, float stdv);
 
 /* ---- multi-GPU ------------------------------------------------------- */
+/* Frame-sequence mode from one process: one context per GPU (devices, or
+ * 0..ngpu-1 when null), each holding the whole model; frame k of a batch
+ * runs on member k mod ngpu, each member on its own host thread, with no
+ * communication (the engine's frame loop, src/main.cpp:126-147, dealt out;
+ * no counterpart in the reference, which runs one device). */
+typedef struct s2b_group s2b_group;
+int s2b_group_create(int ngpu, const int* devices, int precision, s2b_group** out);
+int s2b_group_destroy(s2b_group* group);
+const char* s2b_group_last_error(const s2b_group* group);
+int s2b_group_load_weights_dir(s2b_group* group, const char* m5_dir);
+int s2b_group_load_weights_synth(s2b_group* group, uint64_t seed);
+int s2b_group_set_windows(s2b_group* group, const s2b_win* ns, const s2b_win* sh);
+/* vid_patches: nframes x (Lv, 132); txt (TXT, 5120) shared by the frames;
+ * sr_out: nframes x (Lv, 64). */
+int s2b_group_forward_frames(s2b_group* group, const float* vid_patches, int nframes, int Lv, const float* txt,
+                             int TXT, float timestep, float* sr_out);
+
 /* Window-sharded image mode: one rank per GPU; each rank owns a subset of
  * the windows of every layer, txt rows are replicated, and the txt partial
  * sums of the attention are summed across ranks with one NCCL all-reduce

@@ -5,6 +5,7 @@
 #include "synth.h"
 #include "shard_plan.h"
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 
@@ -164,6 +165,57 @@ int s2b_forward_grid(s2b_ctx* ctx, const float* grid, int T, int H, int W, const
     s2b_patchify_grid(grid, T, H, W, patch.data());
     if (int rc = ctx->dit.forward(patch.data(), Lv, txt, TXT, t, sr.data())) return rc;
     return s2b_unpatchify_latent(sr.data(), T, H, W, sr_latent);
+}
+
+int s2b_load_weights_mem(s2b_ctx* ctx, const s2b_weight_file* files, int nfiles, int layer_lo, int layer_hi) {
+    if (!ctx || (nfiles > 0 && !files) || nfiles < 0) return S2B_ERR_ARG;
+    s2b::WeightFiles table;
+    for (int i = 0; i < nfiles; i++) {
+        if (!files[i].name || (!files[i].data && files[i].bytes)) return S2B_ERR_ARG;
+        table[files[i].name] = {files[i].data, files[i].bytes};
+    }
+    static std::mutex mem_load_mutex;   // the in-memory table is a process-wide hook during a load
+    std::lock_guard<std::mutex> lk(mem_load_mutex);
+    return ctx->dit.load_weights_mem(table, layer_lo, layer_hi);
+}
+
+int s2b_forward_grid_dev(s2b_ctx* ctx, const float* d_vid_grid, int T, int H, int W, const float* d_txt, int TXT,
+                         float t, float* d_sr_grid, void* stream) {
+    if (!ctx) return S2B_ERR_ARG;
+    return ctx->dit.forward_grid_dev(d_vid_grid, T, H, W, d_txt, TXT, t, d_sr_grid, (cudaStream_t)stream);
+}
+
+static int launch_status(const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) return S2B_OK;
+    g_create_err = std::string(what) + ": " + cudaGetErrorString(e);
+    return S2B_ERR_CUDA;
+}
+
+int s2b_patchify_grid_dev(const float* d_vid_grid, int T, int H, int W, float* d_vid_patch, void* stream) {
+    if (!d_vid_grid || !d_vid_patch || T <= 0 || H <= 0 || W <= 0 || H % 2 || W % 2) return S2B_ERR_ARG;
+    s2b::patchify_dev(d_vid_grid, T, H, W, d_vid_patch, (cudaStream_t)stream);
+    return launch_status("patchify");
+}
+
+int s2b_unpatchify_latent_dev(const float* d_sr, int T, int H, int W, float* d_sr_grid, void* stream) {
+    if (!d_sr || !d_sr_grid || T <= 0 || H <= 0 || W <= 0 || H % 2 || W % 2) return S2B_ERR_ARG;
+    s2b::unpatchify_dev(d_sr, T, H, W, d_sr_grid, (cudaStream_t)stream);
+    return launch_status("unpatchify");
+}
+
+int s2b_assemble_vid_grid_dev(const float* d_noise, const float* d_latent, float scaling, int H8, int W8,
+                              float* d_vid_grid, void* stream) {
+    if (!d_noise || !d_latent || !d_vid_grid || H8 <= 0 || W8 <= 0) return S2B_ERR_ARG;
+    s2b::assemble_grid_dev(d_noise, d_latent, scaling, H8, W8, d_vid_grid, (cudaStream_t)stream);
+    return launch_status("assemble vid_grid");
+}
+
+int s2b_decode_latent_dev(const float* d_noise, const float* d_sr_grid, float scaling, int H8, int W8,
+                          float* d_z, void* stream) {
+    if (!d_noise || !d_sr_grid || !d_z || H8 <= 0 || W8 <= 0 || scaling == 0.f) return S2B_ERR_ARG;
+    s2b::decode_latent_dev(d_noise, d_sr_grid, scaling, H8, W8, d_z, (cudaStream_t)stream);
+    return launch_status("decode latent");
 }
 
 int s2b_awa_forward(s2b_ctx* ctx, const float* vqkv, const float* tqkv, const s2b_win* win, const float* nq_v,

@@ -106,7 +106,19 @@ struct HostLinear {
     const void* data() const { return f16 ? (const void*)w.data() : (const void*)wf.data(); }
 };
 
+// Files of the m5 layout come from a directory or, when `mem` is set, from
+// an in-memory table keyed by file name.
+const WeightFiles* g_mem_files = nullptr;   // set for the duration of one load (context-local call)
+
 bool read_file(const std::string& p, std::vector<unsigned char>& out) {
+    if (g_mem_files) {
+        const size_t slash = p.find_last_of('/');
+        const std::string name = slash == std::string::npos ? p : p.substr(slash + 1);
+        auto it = g_mem_files->find(name);
+        if (it == g_mem_files->end()) return false;
+        out.assign((const unsigned char*)it->second.first, (const unsigned char*)it->second.first + it->second.second);
+        return true;
+    }
     std::ifstream f(p, std::ios::binary);
     if (!f) return false;
     f.seekg(0, std::ios::end);
@@ -118,8 +130,9 @@ bool read_file(const std::string& p, std::vector<unsigned char>& out) {
 
 // ncnn InnerProduct .param/.bin pair (format: src/verify_dit.cpp:62-104).
 bool load_host_linear(const std::string& dir, const std::string& base, HostLinear& L, std::string& err) {
-    std::ifstream pf(dir + base + ".param");
-    if (!pf) { err = "missing " + dir + base + ".param"; return false; }
+    std::vector<unsigned char> ptxt;
+    if (!read_file(dir + base + ".param", ptxt)) { err = "missing " + dir + base + ".param"; return false; }
+    std::istringstream pf(std::string(ptxt.begin(), ptxt.end()));
     std::string line;
     int nout = 0, bias = 0, wsz = 0;
     while (std::getline(pf, line)) {
@@ -174,6 +187,13 @@ bool load_host_vector(const std::string& dir, const std::string& base, std::vect
     return true;
 }
 }  // namespace
+
+int DitB200::load_weights_mem(const WeightFiles& files, int lo, int hi) {
+    g_mem_files = &files;
+    const int rc = load_weights("mem/", false, 0, lo, hi);
+    g_mem_files = nullptr;
+    return rc;
+}
 
 int DitB200::load_weights(const char* dir_c, bool synth, uint64_t seed, int lo, int hi) {
     if (dev_ < 0) return fail(ERR_STATE, "context not created");
@@ -785,6 +805,38 @@ int DitB200::forward_dev(const float* d_vid, int Lv, const float* d_txt, int TXT
     cudaEventDestroy(ev_out);
     last_launches_ = graph_launches_;
     return cuda_check(cudaGetLastError(), "forward_dev");
+}
+
+int DitB200::forward_grid_dev(const float* d_grid, int T, int H, int W, const float* d_txt, int TXT, float t,
+                              float* d_sr_grid, cudaStream_t user) {
+    if (!d_grid || !d_txt || !d_sr_grid) return fail(ERR_ARG, "null buffer");
+    if (T <= 0 || H <= 0 || W <= 0 || H % 2 || W % 2) return fail(ERR_ARG, "grid H and W must be positive and even");
+    if (!weights_) return fail(ERR_STATE, "weights not loaded");
+    if (layer_lo_ != 0 || layer_hi_ != NUM_LAYERS) return fail(ERR_STATE, "full forward needs all 32 layers loaded");
+    if (!geom_[0].ready || !geom_[1].ready) return fail(ERR_STATE, "windows not set");
+    const int Lv = T * (H / 2) * (W / 2);
+    if (Lv != geom_[0].view.Lv || TXT != geom_[0].view.TXT || TXT <= 0) return fail(ERR_ARG, "grid / TXT do not match the windows");
+    cudaSetDevice(dev_);
+    if (int rc = ensure_acts(Lv, TXT)) return rc;
+    if (int rc = capture_full(Lv, TXT)) return rc;
+    cudaEvent_t ev_in, ev_out;
+    cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&ev_out, cudaEventDisableTiming);
+    cudaEventRecord(ev_in, user);
+    cudaStreamWaitEvent(stream_, ev_in, 0);
+    float temb[TEMB_IN];
+    sinusoidal256(t, temb);
+    cudaMemcpyAsync(temb_in_.p, temb, sizeof temb, cudaMemcpyHostToDevice, stream_);
+    patchify_dev(d_grid, T, H, W, VIDIN_F_.as<float>(), stream_);
+    cudaMemcpyAsync(TXTIN_F_.p, d_txt, (size_t)TXT * TXT_IN * 4, cudaMemcpyDeviceToDevice, stream_);
+    cudaGraphLaunch(gexec_, stream_);
+    unpatchify_dev(SR_.as<float>(), T, H, W, d_sr_grid, stream_);
+    cudaEventRecord(ev_out, stream_);
+    cudaStreamWaitEvent(user, ev_out, 0);
+    cudaEventDestroy(ev_in);
+    cudaEventDestroy(ev_out);
+    last_launches_ = graph_launches_ + 2;
+    return cuda_check(cudaGetLastError(), "forward_grid_dev");
 }
 
 int DitB200::forward(const float* vid_patch, int Lv, const float* txt, int TXT, float t, float* sr_out) {

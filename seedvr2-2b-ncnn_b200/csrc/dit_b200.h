@@ -9,8 +9,13 @@
 #include <string>
 #include <vector>
 #include <memory>
+#include <map>
+#include <utility>
 
 namespace s2b {
+
+// m5 weight files held in memory: file name -> (bytes, size).
+using WeightFiles = std::map<std::string, std::pair<const void*, size_t>>;
 
 // Owning device allocation (move-only).
 struct DevBuf {
@@ -89,6 +94,9 @@ public:
     ~DitB200();
     int create(int device, int precision);
     int load_weights(const char* m5_dir, bool synth, uint64_t seed, int layer_lo, int layer_hi);
+    // The same from the m5 directory's files supplied in memory (not thread-safe
+    // against a concurrent load in another context).
+    int load_weights_mem(const WeightFiles& files, int layer_lo, int layer_hi);
     int set_windows(const WinGeom& ns, const WinGeom& sh);
 
     // DitVk::forward_latent (host buffers)
@@ -98,6 +106,10 @@ public:
     int forward(const float* vid_patch, int Lv, const float* txt, int TXT, float t, float* sr_out);
     int forward_dev(const float* d_vid_patch, int Lv, const float* d_txt, int TXT, float t, float* d_sr,
                     cudaStream_t user);
+    // DitVk::forward_grid on device buffers: patchify, the captured forward and
+    // unpatchify, all on the caller's stream.
+    int forward_grid_dev(const float* d_grid, int T, int H, int W, const float* d_txt, int TXT, float t,
+                         float* d_sr_grid, cudaStream_t user);
     int time_embedding(float t, float* emb_host);
     // forward_latent(0, 32, init, final) with CUDA events around every kernel:
     // per KernelKind the summed device ms, algorithmic FLOPs / bytes, launches.

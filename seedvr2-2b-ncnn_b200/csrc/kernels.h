@@ -131,4 +131,14 @@ void awa_coalesce_div(const float* toutw, int nwin, int TXT, void* att_txt, int 
 void copy_rows_f32(const float* src, int ld_src, const int* src_idx, float* dst, int ld_dst, const int* dst_idx,
                    int n, int width, cudaStream_t s);
 
+// ---------------------------------------------------------------- grid / engine formats (k_engine.cu)
+// (T, H, W, 33) -> (T*H/2*W/2, 132) and (T*H/2*W/2, 64) -> (T, H, W, 16), src/dit_vk.cpp:717-750.
+void patchify_dev(const float* grid, int T, int H, int W, float* patch, cudaStream_t s);
+void unpatchify_dev(const float* sr, int T, int H, int W, float* out, cudaStream_t s);
+// vid_grid (H8, W8, 33) from channel-first noise and latent, src/seedvr2_engine.cpp:154-168.
+void assemble_grid_dev(const float* noise, const float* latent, float scale, int H8, int W8, float* grid,
+                       cudaStream_t s);
+// z (16, H8, W8) = (noise - sr) / scale with sr channel-last (H8, W8, 16), src/seedvr2_engine.cpp:298-305.
+void decode_latent_dev(const float* noise, const float* sr, float scale, int H8, int W8, float* z, cudaStream_t s);
+
 }  // namespace s2b

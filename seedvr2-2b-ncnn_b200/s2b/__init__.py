@@ -34,6 +34,10 @@ class S2BError(RuntimeError):
         self.code = code
 
 
+class s2b_weight_file(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char_p), ("data", ctypes.c_void_p), ("bytes", ctypes.c_size_t)]
+
+
 class s2b_win(ctypes.Structure):
     _fields_ = [("t", ctypes.c_int), ("h", ctypes.c_int), ("w", ctypes.c_int), ("nwin", ctypes.c_int),
                 ("txt_len", ctypes.c_int),
@@ -69,6 +73,18 @@ def lib() -> ctypes.CDLL:
         "s2b_forward": [vp, _F32P, ip, _F32P, ip, ctypes.c_float, _F32P],
         "s2b_forward_dev": [vp, vp, ip, vp, ip, ctypes.c_float, vp, vp],
         "s2b_forward_grid": [vp, _F32P, ip, ip, ip, _F32P, ip, ctypes.c_float, _F32P],
+        "s2b_forward_grid_dev": [vp, vp, ip, ip, ip, vp, ip, ctypes.c_float, vp, vp],
+        "s2b_load_weights_mem": [vp, ctypes.POINTER(s2b_weight_file), ip, ip, ip],
+        "s2b_group_create": [ip, _I32P, ip, ctypes.POINTER(vp)],
+        "s2b_group_destroy": [vp],
+        "s2b_group_load_weights_dir": [vp, ctypes.c_char_p],
+        "s2b_group_load_weights_synth": [vp, u64],
+        "s2b_group_set_windows": [vp, ctypes.POINTER(s2b_win), ctypes.POINTER(s2b_win)],
+        "s2b_group_forward_frames": [vp, _F32P, ip, ip, _F32P, ip, ctypes.c_float, _F32P],
+        "s2b_patchify_grid_dev": [vp, ip, ip, ip, vp, vp],
+        "s2b_unpatchify_latent_dev": [vp, ip, ip, ip, vp, vp],
+        "s2b_assemble_vid_grid_dev": [vp, vp, ctypes.c_float, ip, ip, vp, vp],
+        "s2b_decode_latent_dev": [vp, vp, ctypes.c_float, ip, ip, vp, vp],
         "s2b_patchify_grid": [_F32P, ip, ip, ip, _F32P],
         "s2b_unpatchify_latent": [_F32P, ip, ip, ip, _F32P],
         "s2b_awa_forward": [vp, _F32P, _F32P, ctypes.POINTER(s2b_win), _F32P, _F32P, _F32P, _F32P, ip, ip,
@@ -99,6 +115,8 @@ def lib() -> ctypes.CDLL:
         fn.restype = ctypes.c_int
     L.s2b_last_error.argtypes = [vp]
     L.s2b_last_error.restype = ctypes.c_char_p
+    L.s2b_group_last_error.argtypes = [vp]
+    L.s2b_group_last_error.restype = ctypes.c_char_p
     _lib = L
     return L
 
@@ -178,6 +196,50 @@ def _same_nccl_as_torch():
         import torch  # noqa: F401
     except ImportError:
         pass
+
+
+class FrameGroup:
+    """Frame-sequence mode on several GPUs from one process (s2b_group_*)."""
+
+    def __init__(self, ngpu: int, precision: int = PREC_BF16, devices=None):
+        self._g = ctypes.c_void_p()
+        dev = None if devices is None else (ctypes.c_int * ngpu)(*devices)
+        rc = lib().s2b_group_create(ngpu, dev, precision, ctypes.byref(self._g))
+        if rc != 0:
+            raise S2BError(rc, (lib().s2b_last_error(None) or b"").decode())
+        self.ngpu = ngpu
+
+    def _c(self, rc):
+        if rc != 0:
+            raise S2BError(rc, (lib().s2b_group_last_error(self._g) or b"").decode())
+
+    def init_synth(self, seed: int):
+        self._c(lib().s2b_group_load_weights_synth(self._g, seed))
+
+    def init(self, model_dir: str):
+        self._c(lib().s2b_group_load_weights_dir(self._g, model_dir.encode()))
+
+    def set_windows(self, ns: "Win", sh: "Win"):
+        a, b = ns.as_c(), sh.as_c()
+        self._c(lib().s2b_group_set_windows(self._g, ctypes.byref(a), ctypes.byref(b)))
+
+    def forward_frames(self, vid_patches, Lv, txt, TXT, timestep=1000.0):
+        v, t = _f32(vid_patches), _f32(txt)
+        n = v.shape[0]
+        out = np.zeros((n, Lv, OUT_CH), np.float32)
+        self._c(lib().s2b_group_forward_frames(self._g, _p(v), n, Lv, _p(t), TXT, timestep, _p(out)))
+        return out
+
+    def close(self):
+        if self._g:
+            lib().s2b_group_destroy(self._g)
+            self._g = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def nccl_unique_id() -> bytes:
@@ -287,6 +349,16 @@ class DitB200:
         """DitVk::init weight half: the m5 directory layout."""
         self._c(lib().s2b_load_weights_dir(self._ctx, model_dir.encode(), layer_lo, layer_hi))
 
+    def init_mem(self, files: dict, layer_lo: int = 0, layer_hi: int = NUM_LAYERS):
+        """s2b_load_weights_mem: files maps m5 file names to their bytes."""
+        bufs = {k: ctypes.create_string_buffer(v, len(v)) for k, v in files.items()}
+        arr = (s2b_weight_file * len(files))()
+        for i, (k, b) in enumerate(bufs.items()):
+            arr[i].name = k.encode()
+            arr[i].data = ctypes.cast(b, ctypes.c_void_p)
+            arr[i].bytes = len(files[k])
+        self._c(lib().s2b_load_weights_mem(self._ctx, arr, len(files), layer_lo, layer_hi))
+
     def init_synth(self, seed: int, layer_lo: int = 0, layer_hi: int = NUM_LAYERS):
         self._c(lib().s2b_load_weights_synth(self._ctx, seed, layer_lo, layer_hi))
 
@@ -321,6 +393,10 @@ class DitB200:
         out = np.zeros((T, H, W, 16), np.float32)
         self._c(lib().s2b_forward_grid(self._ctx, _p(g), T, H, W, _p(t), TXT, timestep, _p(out)))
         return out
+
+    def forward_grid_dev(self, d_grid: int, T: int, H: int, W: int, d_txt: int, TXT: int, timestep: float,
+                         d_sr_grid: int, stream: int):
+        self._c(lib().s2b_forward_grid_dev(self._ctx, d_grid, T, H, W, d_txt, TXT, timestep, d_sr_grid, stream))
 
     def awa_forward(self, vqkv, tqkv, win: Win, nq_v, nk_v, nq_t, nk_t, Lv, TXT, eps=1e-5):
         """AwaVk::forward (src/awa_vk.h:39-44)."""

@@ -1,6 +1,7 @@
 """The C-ABI library: loads, exports every declared symbol, validates
 arguments and fails loudly (no CPU fallback) when no B200 is present."""
 import ctypes
+import os
 
 import numpy as np
 import pytest
@@ -69,3 +70,31 @@ def test_synth_m5_layout_matches_reference_loader(tmp_path):
     assert int.from_bytes(raw[:8], "little") == 1 and int.from_bytes(raw[8:16], "little") == 2560
     g = np.frombuffer(raw[16:], np.float32)
     assert abs(g.mean() - 1) < 0.01 and abs(g.std() - 0.02) < 0.005
+
+
+def _has_gpu() -> bool:
+    import torch
+    return torch.cuda.is_available()
+
+
+def _build_dropin(tmpdir):
+    """Compiles tests/cpp/dropin_engine.cpp against include/seedvr2_b200.hpp and
+    links it with the library (returns the binary path)."""
+    import subprocess
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    lib_dir = os.path.join(root, "seedvr2-2b-ncnn_b200", "lib")
+    exe = os.path.join(str(tmpdir), "dropin_engine")
+    cmd = ["g++", "-std=c++17", "-O1", "-Wall", "-Werror", "-I", os.path.join(root, "include"),
+           os.path.join(root, "tests", "cpp", "dropin_engine.cpp"), "-L", lib_dir, "-ls2b",
+           f"-Wl,-rpath,{lib_dir}", "-o", exe]
+    subprocess.run(cmd, check=True, capture_output=True, text=True)
+    return exe
+
+
+def test_cpp_dropin_header_compiles_and_links(tmp_path):
+    import subprocess
+    exe = _build_dropin(tmp_path)
+    if not _has_gpu():
+        # without a GPU the wrapper fails loudly (bool + message), never silently
+        r = subprocess.run([exe, str(tmp_path), str(tmp_path / "out.bin")], capture_output=True, text=True)
+        assert r.returncode == 1 and "[DitB200]" in r.stderr

@@ -141,3 +141,59 @@ def test_full_graph_forward_equals_forward_latent(prec):
     assert np.array_equal(sr_graph, sr_lat)
     assert c.last_launches() > 32 * 8
     c.close()
+
+
+def test_weights_from_memory_equal_weights_from_directory(m5_small, inputs):
+    """s2b_load_weights_mem with the directory's files in memory gives the
+    same model as s2b_load_weights_dir (bit-identical forward)."""
+    files = {}
+    for name in os.listdir(m5_small):
+        with open(os.path.join(m5_small, name), "rb") as f:
+            files[name] = f.read()
+    vp, txt = inputs[0], inputs[1]
+    outs = []
+    for from_mem in (False, True):
+        c = s2b.DitB200(0, s2b.PREC_BF16)
+        try:
+            if from_mem:
+                c.init_mem(files, 0, 2)
+            else:
+                c.init(m5_small, 0, 2)
+            c.set_windows(inputs[4], inputs[5])
+            vl, tl, _ = c.forward_latent(vp, Lv, txt, TXT, TS, 0, 2, True, False)
+            outs.append((vl, tl, c.time_embedding(TS)))
+        finally:
+            c.close()
+    for a, b in zip(outs[0], outs[1]):
+        np.testing.assert_array_equal(a, b)
+    # a missing file is reported, not skipped
+    c = s2b.DitB200(0, s2b.PREC_BF16)
+    try:
+        partial = {k: v for k, v in files.items() if not k.startswith("b1_vid_qkv")}
+        with pytest.raises(s2b.S2BError):
+            c.init_mem(partial, 0, 2)
+    finally:
+        c.close()
+
+
+def test_cpp_dropin_engine_matches_python(m5_small, inputs, tmp_path):
+    """The reference-shaped C++ interface (include/seedvr2_b200.hpp) driven
+    like the engine drives DitVk gives the same latents as the Python API."""
+    import subprocess
+    import test_capi
+    exe = test_capi._build_dropin(tmp_path)
+    out = tmp_path / "lat.bin"
+    r = subprocess.run([exe, m5_small, str(out)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    Tq, Hq, Wq, TXTq = 1, 24, 28, 58
+    Lq = Tq * Hq * Wq
+    got = np.fromfile(out, np.float32)
+    c = s2b.DitB200(0, s2b.PREC_BF16)
+    try:
+        c.init(m5_small, 0, 2)
+        c.set_windows(s2b.make_win(Tq, Hq, Wq, (4, 3, 3), TXTq, False), s2b.make_win(Tq, Hq, Wq, (4, 3, 3), TXTq, True))
+        vp = s2b.patchify_grid(s2b.synth_vid_grid(Tq, 2 * Hq, 2 * Wq, 42))
+        vl, tl, _ = c.forward_latent(vp, Lq, s2b.synth_txt(TXTq, 42), TXTq, 1000.0, 0, 2, True, False)
+    finally:
+        c.close()
+    np.testing.assert_array_equal(got, np.concatenate([vl.ravel(), tl.ravel()]))
