@@ -73,6 +73,17 @@ public:
         }
         return ok(s2b_load_weights_dir(ctx_, model_dir.c_str(), 0, 32));
     }
+    // Loads only layers [layer_lo, layer_hi) (plus the input / output
+    // projections): enough for forward_latent over that range, as the
+    // reference's chunked path uses one chunk at a time.
+    bool init(const std::string& model_dir, int precision, int layer_lo, int layer_hi) {
+        if (ctx_) { s2b_ctx_destroy(ctx_); ctx_ = nullptr; }
+        if (s2b_ctx_create(device_, precision, &ctx_) != S2B_OK) {
+            ctx_ = nullptr;
+            return fail(s2b_last_error(nullptr));
+        }
+        return ok(s2b_load_weights_dir(ctx_, model_dir.c_str(), layer_lo, layer_hi));
+    }
 
     bool forward(const std::vector<float>& vid_patch, int Lv, const std::vector<float>& txt, int TXT,
                  float timestep, std::vector<float>& out_sr) {
