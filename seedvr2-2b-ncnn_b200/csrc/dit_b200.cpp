@@ -569,7 +569,7 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
         // one tcgen05 GEMM epilogue writes the packed Q/K/V directly (no qkv buffer)
         GemmEpi e; e.mode = EPI_QKV_PACK;
         PackEpi& k = e.pk;
-        k.tokpos = G.tokpos.as<const int4>(); k.cums = G.view.cums; k.cs = G.cs.as<const float2>();
+        k.tokpos = G.tokpos.as<const int4>(); k.cums = G.view.cums; k.cs = G.cs.as<const float2>(); k.npos = G.npos;
         k.nq0 = normw(i, 0, 0); k.nk0 = normw(i, 0, 1); k.nq1 = normw(i, 1, 0); k.nk1 = normw(i, 1, 1);
         k.eps = NORM_EPS; k.Lv = Lv; k.TXT = TXT; k.nwin = G.view.nwin; k.sumS = G.view.sumS;
         k.Qp = B.Qp; k.Kp = B.Kp; k.Vp = B.Vp;
@@ -605,12 +605,11 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
                &launches_);
     pend(s);
     pbeg(KK_OTHER, 0, (double)G.view.nwin * TXT * DIM * 4 + (double)TXT * DIM * ab, s);
-    if (B.txt_sum) {
-        // window-sharded: sum this rank's windows, all-reduce across ranks,
-        // then divide by the global window count
-        awa_coalesce_div(B.TOUTW, G.view.nwin, TXT, B.txt_sum, DIM, ACT_F32, 0.f, s);
-        if (int rc = B.txt_reduce(B.reduce_ctx, s)) return rc;
-        awa_coalesce_div(B.txt_sum, 1, TXT, att + (size_t)Lv * DIM * ab, DIM, act_, (float)B.nwin_global[i % 2], s);
+    if (B.txt_partial) {
+        // window-sharded: sum this rank's windows, then combine the ranks'
+        // partials and divide by the global window count
+        awa_coalesce_div(B.TOUTW, G.view.nwin, TXT, B.txt_partial(B.shard_ctx, i), DIM, ACT_F32, 0.f, s);
+        if (int rc = B.txt_finish(B.shard_ctx, i, att + (size_t)Lv * DIM * ab, s)) return rc;
         launches_ += 2;
     } else {
         awa_coalesce(B.TOUTW, G.view.nwin, TXT, att + (size_t)Lv * DIM * ab, DIM, act_, s);

@@ -5,6 +5,7 @@
 #include "s2b_common.h"
 #include "awa_geometry.h"
 #include "kernels.h"
+#include "shard_plan.h"
 #include <cuda_runtime.h>
 #include <string>
 #include <vector>
@@ -74,12 +75,12 @@ struct LayerBufs {
     void *Qp = nullptr, *Kp = nullptr, *Vp = nullptr;
     float* TOUTW = nullptr;
     GeomDev* geom[2] = {nullptr, nullptr};
-    // sharded only: this rank's txt partial sums, their cross-rank reduction
-    // and the global window counts the sum is divided by
-    float* txt_sum = nullptr;
-    int (*txt_reduce)(void* ctx, cudaStream_t s) = nullptr;
-    void* reduce_ctx = nullptr;
-    int nwin_global[2] = {0, 0};
+    // sharded only: where this rank's txt partial sum of layer i goes, and the
+    // step that combines all ranks' partials into the mean over all windows
+    // (written to att_txt)
+    float* (*txt_partial)(void* ctx, int layer) = nullptr;
+    int (*txt_finish)(void* ctx, int layer, void* att_txt, cudaStream_t s) = nullptr;
+    void* shard_ctx = nullptr;
 };
 
 // 256-wide sinusoidal timestep features (src/dit_vk.cpp:295-302).
@@ -171,6 +172,7 @@ private:
     int shard_enqueue(cudaStream_t s);
     int shard_exchange(int p, cudaStream_t s);
     int shard_capture();
+    int shard_setup_peers(const ShardPlan& plan, int n0, int n1, int TXT);
     cudaStream_t capture_stream() const { return stream_; }
     const float* ada(int layer, int flow, int k) const {
         return ada_.as<float>() + ((size_t)(layer * 12 + flow * 6 + k)) * DIM;

@@ -49,6 +49,7 @@ const NcclLib* nccl_lib(std::string* err) {
         sym(lib.Recv, "ncclRecv");
         sym(lib.GroupStart, "ncclGroupStart");
         sym(lib.GroupEnd, "ncclGroupEnd");
+        sym(lib.AllGather, "ncclAllGather");
         sym(lib.GetErrorString, "ncclGetErrorString");
         if (!ok) {
             load_err = "the NCCL library lacks an entry point this build needs";
@@ -70,10 +71,17 @@ int DitB200::ShardState::nccl_check(ncclResult_t r, const char* what, std::strin
     return ERR_NCCL;
 }
 
+void DitB200::ShardState::close_peers() {
+    for (void* ptr : opened) cudaIpcCloseMemHandle(ptr);
+    opened.clear();
+    p2p = false;
+}
+
 DitB200::ShardState::~ShardState() {
     if (dev >= 0) cudaSetDevice(dev);
     // a graph holding NCCL calls goes before its communicator
     if (gexec) cudaGraphExecDestroy(gexec);
+    close_peers();
     if (comm && nl) nl->CommDestroy(comm);
 }
 
@@ -216,17 +224,126 @@ int DitB200::shard_prepare(int Lv, int TXT) {
         if ((rc = up(S.self_src[p], ssrc[p]))) return rc;
         if ((rc = up(S.self_dst[p], sdst[p]))) return rc;
     }
+    if ((rc = shard_setup_peers(plan, n0, n1, TXT))) return rc;
     S.plan = std::move(plan);
     S.Lv = Lv; S.TXT = TXT;
     S.plan_gen = geom_gen_;
     return OK;
 }
 
-static int shard_txt_reduce(void* ctx, cudaStream_t s) {
+// Maps every rank's txt partials, flags and residual buffers into this rank
+// (CUDA IPC handles swapped with one NCCL all-gather) and builds the
+// peer-store exchange lists.  All ranks agree on the outcome: if any rank
+// cannot map its peers, every rank keeps the NCCL exchanges.
+int DitB200::shard_setup_peers(const ShardPlan& plan, int n0, int n1, int TXT) {
+    ShardState& S = *shard_;
+    S.close_peers();
+    const char* env = std::getenv("S2B_SHARD_P2P");
+    const bool want = S.world <= 8 && !(env && env[0] == '0');
+    int rc;
+    if ((rc = cuda_check(S.TXTP.ensure((size_t)2 * TXT * DIM * 4), "cudaMalloc(shard TXTP)"))) return rc;
+    if ((rc = cuda_check(S.FLAGS.ensure((size_t)2 * 2 * 8 * 4), "cudaMalloc(shard flags)"))) return rc;
+    if ((rc = cuda_check(S.EPOCH.ensure(16), "cudaMalloc(shard epoch)"))) return rc;
+    cudaMemset(S.FLAGS.p, 0, S.FLAGS.bytes);
+    cudaMemset(S.EPOCH.p, 0, S.EPOCH.bytes);
+    // this rank's 4 handles (TXTP, FLAGS, X[0], X[1]) + whether it wants peer mode
+    struct Rec { cudaIpcMemHandle_t h[4]; int want; int pad[15]; };
+    static_assert(sizeof(Rec) % 16 == 0, "record size");
+    Rec mine;
+    std::memset(&mine, 0, sizeof mine);
+    mine.want = want ? 1 : 0;
+    void* bases[4] = {S.TXTP.p, S.FLAGS.p, S.X[0].p, S.X[1].p};
+    for (int k = 0; k < 4 && mine.want; k++)
+        if (cudaIpcGetMemHandle(&mine.h[k], bases[k]) != cudaSuccess) mine.want = 0;
+    cudaGetLastError();
+    DevBuf dev_recs;
+    if ((rc = cuda_check(dev_recs.ensure(sizeof(Rec) * (S.world + 1)), "cudaMalloc(shard handles)"))) return rc;
+    cudaMemcpy(dev_recs.as<char>() + sizeof(Rec) * S.world, &mine, sizeof mine, cudaMemcpyHostToDevice);
+    if ((rc = S.nccl_check(S.nl->AllGather(dev_recs.as<char>() + sizeof(Rec) * S.world, dev_recs.p, sizeof(Rec),
+                                           ncclUint8, S.comm, stream_), "ncclAllGather(handles)", err)))
+        return rc;
+    std::vector<Rec> recs(S.world);
+    if ((rc = cuda_check(cudaMemcpyAsync(recs.data(), dev_recs.p, sizeof(Rec) * S.world, cudaMemcpyDeviceToHost, stream_),
+                         "copy handles")))
+        return rc;
+    cudaStreamSynchronize(stream_);
+    bool all = true;
+    for (const Rec& r : recs) all = all && r.want;
+    int ok = all ? 1 : 0;
+    ShardPeers P;
+    P.world = S.world; P.rank = S.rank;
+    for (int q = 0; q < S.world && ok; q++) {
+        void* ptr[4];
+        for (int k = 0; k < 4; k++) {
+            if (q == S.rank) { ptr[k] = bases[k]; continue; }
+            if (cudaIpcOpenMemHandle(&ptr[k], recs[q].h[k], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                ok = 0;
+                break;
+            }
+            S.opened.push_back(ptr[k]);
+        }
+        if (!ok) break;
+        P.txtp[q] = (float*)ptr[0]; P.flags[q] = (uint32_t*)ptr[1];
+        P.x[0][q] = (float*)ptr[2]; P.x[1][q] = (float*)ptr[3];
+    }
+    // every rank must have mapped every peer
+    DevBuf dev_ok;
+    if ((rc = cuda_check(dev_ok.ensure(4 * (S.world + 1)), "cudaMalloc(shard ok)"))) return rc;
+    cudaMemcpy(dev_ok.as<int>() + S.world, &ok, 4, cudaMemcpyHostToDevice);
+    if ((rc = S.nccl_check(S.nl->AllGather(dev_ok.as<int>() + S.world, dev_ok.p, 1, ncclInt32, S.comm, stream_),
+                           "ncclAllGather(peer status)", err)))
+        return rc;
+    std::vector<int> oks(S.world);
+    cudaMemcpyAsync(oks.data(), dev_ok.p, 4 * S.world, cudaMemcpyDeviceToHost, stream_);
+    if ((rc = cuda_check(cudaStreamSynchronize(stream_), "peer status"))) return rc;
+    for (int v : oks) ok = ok && v;
+    if (!ok) { S.close_peers(); return OK; }
+    S.peers = P;
+    // peer-store exchange lists: every local row (vid rows of this rank's
+    // windows, then the replicated txt rows) to its owner's row in the next layout
+    const int nl[2] = {n0, n1};
+    for (int p = 0; p < 2; p++) {
+        std::vector<int> src, rnk, dst;
+        for (int j = 0; j < nl[p]; j++) {
+            const int tok = plan.tokens[p][j];
+            src.push_back(j);
+            rnk.push_back(plan.owner[1 - p][tok]);
+            dst.push_back(plan.lrow[1 - p][tok]);
+        }
+        for (int t = 0; t < TXT; t++) { src.push_back(nl[p] + t); rnk.push_back(S.rank); dst.push_back(nl[1 - p] + t); }
+        S.n_xr[p] = (int)src.size();
+        DevBuf* bufs[3] = {&S.xr_src[p], &S.xr_rank[p], &S.xr_dst[p]};
+        const std::vector<int>* vals[3] = {&src, &rnk, &dst};
+        for (int k = 0; k < 3; k++) {
+            if ((rc = cuda_check(bufs[k]->ensure(vals[k]->size() * 4), "cudaMalloc(exchange list)"))) return rc;
+            cudaMemcpy(bufs[k]->p, vals[k]->data(), vals[k]->size() * 4, cudaMemcpyHostToDevice);
+        }
+    }
+    S.p2p = true;
+    return cuda_check(cudaGetLastError(), "peer setup");
+}
+
+// Where layer i's txt partial sum goes: a slot of the peer-visible buffer, or
+// the NCCL all-reduce buffer.
+static float* shard_txt_partial(void* ctx, int layer) {
     auto* S = static_cast<DitB200::ShardState*>(ctx);
+    return S->p2p ? S->TXTP.as<float>() + (size_t)(layer & 1) * S->TXT * DIM : S->TXTSUM.as<float>();
+}
+
+// All ranks' partials -> the mean over all windows in att_txt.
+static int shard_txt_finish(void* ctx, int layer, void* att_txt, cudaStream_t s) {
+    auto* S = static_cast<DitB200::ShardState*>(ctx);
+    const float div = (float)S->nwin_global[layer & 1];
+    if (S->p2p) {
+        shard_txt_reduce(S->peers, S->EPOCH.as<uint32_t>(), layer, S->TXT, div, att_txt, DIM, S->act, s);
+        return OK;
+    }
     const ncclResult_t r = S->nl->AllReduce(S->TXTSUM.p, S->TXTSUM.p, (size_t)S->TXT * DIM, ncclFloat32, ncclSum,
                                             S->comm, s);
-    return r == ncclSuccess ? OK : ERR_NCCL;
+    if (r != ncclSuccess) return ERR_NCCL;
+    awa_coalesce_div(S->TXTSUM.as<float>(), 1, S->TXT, att_txt, DIM, S->act, div, s);
+    return OK;
 }
 
 int DitB200::shard_exchange(int p, cudaStream_t s) {
@@ -263,6 +380,8 @@ int DitB200::shard_enqueue(cudaStream_t s) {
     ShardState& S = *shard_;
     const int TXT = S.TXT, n0 = S.plan.n_local(0);
     launches_ = 0;
+    S.act = act_;
+    if (S.p2p) { shard_epoch_inc(S.EPOCH.as<uint32_t>(), s); launches_++; }
     // vid_in (this rank's patches of the layer-0 layout) and txt_in, src/dit_vk.cpp:494-497
     copy_rows_f32(S.VIDIN.as<float>(), PATCH_IN, S.tok0.as<int>(), S.VIDLOC.as<float>(), PATCH_IN, nullptr, n0,
                   PATCH_IN, s);
@@ -281,14 +400,20 @@ int DitB200::shard_enqueue(cudaStream_t s) {
         B.X = S.X[p].as<float>(); B.Xn = S.Xn.p; B.QKV = S.QKV.p; B.ATT = S.ATT.p; B.Hs = S.Hs.p;
         B.Qp = S.Qp.p; B.Kp = S.Kp.p; B.Vp = S.Vp.p; B.TOUTW = S.TOUTW.as<float>();
         B.geom[0] = &S.geom[0]; B.geom[1] = &S.geom[1];
-        B.txt_sum = S.TXTSUM.as<float>(); B.txt_reduce = shard_txt_reduce; B.reduce_ctx = &S;
-        B.nwin_global[0] = S.nwin_global[0]; B.nwin_global[1] = S.nwin_global[1];
+        B.txt_partial = shard_txt_partial; B.txt_finish = shard_txt_finish; B.shard_ctx = &S;
         if (int rc = enqueue_layer_on(i, S.plan.n_local(p), TXT, s, B)) {
             if (rc == ERR_NCCL) err = "ncclAllReduce of the txt attention sums failed";
             return rc;
         }
-        if (i + 1 < NUM_LAYERS)
-            if (int rc = shard_exchange(p, s)) return rc;
+        if (i + 1 < NUM_LAYERS) {
+            if (S.p2p) {
+                shard_exchange_rows(S.peers, p, S.xr_src[p].as<int>(), S.xr_rank[p].as<int>(), S.xr_dst[p].as<int>(),
+                                    S.n_xr[p], S.EPOCH.as<uint32_t>(), i, s);
+                launches_ += 2;
+            } else if (int rc = shard_exchange(p, s)) {
+                return rc;
+            }
+        }
     }
     // final norm + vid_out_proj on this rank's rows (src/dit_vk.cpp:657-675),
     // then every rank assembles the whole [Lv, 64] output
@@ -327,7 +452,11 @@ int DitB200::shard_forward(const float* vid_patch, int Lv, const float* txt, int
     cudaMemcpyAsync(sr_out, S.SRFULL.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToHost, stream_);
     last_launches_ = prof_on_ ? launches_ : S.graph_launches;
     if (int rc = cuda_check(cudaGetLastError(), "kernel launch")) return rc;
-    return cuda_check(cudaStreamSynchronize(stream_), "shard_forward");
+    if (int rc = cuda_check(cudaStreamSynchronize(stream_), "shard_forward")) return rc;
+    int expired = 0;
+    if (S.p2p && shard_error_reset(&expired) == 0 && expired)
+        return fail(ERR_TIMEOUT, "a peer-memory exchange wait expired (a rank fell behind or stopped)");
+    return OK;
 }
 
 int DitB200::shard_forward_dev(const float* d_vid, int Lv, const float* d_txt, int TXT, float t, float* d_sr,

@@ -20,6 +20,7 @@ struct NcclLib {
     ncclResult_t (*Recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*GroupStart)() = nullptr;
     ncclResult_t (*GroupEnd)() = nullptr;
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
 };
 // Loads the library once per process; null (and *err set) when it is missing.
@@ -49,6 +50,17 @@ struct DitB200::ShardState {
     std::vector<int> send_ns_off[2], recv_ns_off[2];
     int n_self[2] = {0, 0};
     DevBuf XSEND, XRECV;
+
+    // Exchanges over NVLink peer memory (k_shard.cu) instead of NCCL calls,
+    // when every pair of ranks can map each other's memory.
+    bool p2p = false;
+    ActT act = ACT_BF16;            // activation type of the context
+    DevBuf TXTP, FLAGS, EPOCH;      // [2][TXT*2560] partials, flags, forward counter
+    ShardPeers peers;
+    std::vector<void*> opened;      // IPC mappings of the other ranks' buffers
+    DevBuf xr_src[2], xr_rank[2], xr_dst[2];   // peer-store exchange lists per parity
+    int n_xr[2] = {0, 0};
+    void close_peers();
 
     // the captured shard forward (kernels + NCCL calls) of the current plan
     cudaGraphExec_t gexec = nullptr;

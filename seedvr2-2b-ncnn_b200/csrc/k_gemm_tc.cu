@@ -120,14 +120,14 @@ __device__ __forceinline__ void prefetch_resid(const TcParams& p, int row, int n
 // rotate in adjacent pairs (src/dit_vk.cpp:62-71), pair i with the angle of
 // position pos[i / 21] and frequency i % 21 (cos/sin from the [pos][21]
 // table); dims 126..127 pass through.
-__device__ __forceinline__ void rope64(float* x, int d0, const float2* __restrict__ cs, int p0, int p1, int p2) {
+__device__ __forceinline__ void rope64(float* x, int d0, const float2* cs, int p0, int p1, int p2) {
     #pragma unroll
     for (int j = 0; j < 64; j += 2) {
         const int kd = d0 + j;
         if (kd < 126) {
             const int i = kd >> 1, ax = i / 21, f = i % 21;
             const int pos = ax == 0 ? p0 : (ax == 1 ? p1 : p2);
-            const float2 t = __ldg(cs + pos * 21 + f);
+            const float2 t = cs[pos * 21 + f];          // shared or global (generic load)
             const float a = x[j], b = x[j + 1];
             x[j] = __fadd_rn(__fmul_rn(a, t.x), __fmul_rn(-b, t.y));
             x[j + 1] = __fadd_rn(__fmul_rn(b, t.x), __fmul_rn(a, t.y));
@@ -141,7 +141,8 @@ __device__ __forceinline__ void rope64(float* x, int d0, const float2* __restric
 // and RoPE, v heads pass through; each row lands in its window-packed slot(s)
 // (a txt row in every window, with the same angles in each).
 template <int BN>
-__device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t taddr, int row, int n0) {
+__device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t taddr, int row, int n0,
+                                                  const float2* __restrict__ cs) {
     const PackEpi& k = p.e.pk;
     bool row_ok = row < p.M;
     const int gr = k.row_base + row;
@@ -192,7 +193,7 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
                     x[d] = x[d] * inv * w4.x; x[d + 1] = x[d + 1] * inv * w4.y;
                     x[d + 2] = x[d + 2] * inv * w4.z; x[d + 3] = x[d + 3] * inv * w4.w;
                 }
-                rope64(x, c * 64, k.cs, p0, p1, p2);
+                rope64(x, c * 64, cs, p0, p1, p2);
             }
             store32(dst0 + c * 64, x);
             store32(dst0 + c * 64 + 32, x + 32);
@@ -213,9 +214,10 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
 // tile's 256 columns starting at n0.  The tcgen05.ld are warp-collective and
 // executed by every lane; only the stores depend on the row.
 template <int MODE, int BN = 256>
-__device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, int row, int n0) {
+__device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, int row, int n0,
+                                             const float2* cs = nullptr) {
     const GemmEpi& e = p.e;
-    if constexpr (MODE == EPI_QKV_PACK) { epilogue_qkv_pack<BN>(p, taddr, row, n0); return; }
+    if constexpr (MODE == EPI_QKV_PACK) { epilogue_qkv_pack<BN>(p, taddr, row, n0, cs); return; }
     const bool row_ok = row < p.M;
     if constexpr (MODE == EPI_SWIGLU) {
         // column block [h 128 | g 128] -> 128 outputs at n0 / 2
@@ -383,6 +385,20 @@ __device__ __forceinline__ void resid_finish(ResidPipe& rp) {
     sm100::bulk_wait_all();
 }
 
+// EPI_QKV_PACK: the epilogue warps (128 threads) copy the (cos, sin) table
+// into the shared-memory area the residual boxes use in the gate/residual
+// mode, when it fits; per-row table reads then gather from shared memory
+// instead of issuing 32 distinct L1 lines per warp load.  Returns the table
+// the epilogue reads.
+__device__ __forceinline__ const float2* stage_rope_table(const PackEpi& k, uint8_t* sR) {
+    const int n = k.npos * 21;
+    if (n <= 0 || n * (int)sizeof(float2) > RES_BYTES) return k.cs;
+    float2* t = reinterpret_cast<float2*>(sR);
+    for (int i = (int)threadIdx.x - 64; i < n; i += 128) t[i] = __ldg(k.cs + i);
+    asm volatile("bar.sync 1, 128;" ::: "memory");     // the 4 epilogue warps (threads 64..191)
+    return t;
+}
+
 // ------------------------------------------------------------ single CTA
 template <int MODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -471,6 +487,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
         const int q = warp & 3;                 // TMEM lane quadrant this warp may access
         ResidPipe rp{sR + q * 2 * RBOX_BYTES, ctl->rfull[q], 0u, 0u};
         const bool rt = MODE == EPI_GATE_RESID && p.resid_tma;
+        const float2* cs = nullptr;
+        if constexpr (MODE == EPI_QKV_PACK) cs = stage_rope_table(p.e.pk, sR);
         if (rt && lane == 0 && (int)blockIdx.x < num_tiles)
             resid_load(&tR, rp, ((int)blockIdx.x / p.num_m) * BN1, ((int)blockIdx.x % p.num_m) * BM1 + q * 32);
         int it = 0;
@@ -491,7 +509,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
                     break;
             } else {
                 if (nt < num_tiles) prefetch_resid<MODE>(p, (nt % p.num_m) * BM1 + q * 32 + lane, (nt / p.num_m) * BN1);
-                epilogue_row<MODE>(p, taddr, mb * BM1 + q * 32 + lane, nb * BN1);
+                epilogue_row<MODE>(p, taddr, mb * BM1 + q * 32 + lane, nb * BN1, cs);
             }
             sm100::tc_fence_before();
             __syncwarp();
@@ -636,6 +654,8 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
         ResidPipe rp{sR + q * 2 * RBOX_BYTES, ctl->rfull[q], 0u, 0u};
         // TMA residual boxes only when every group has them (checked on the host)
         const bool rt = MODE == EPI_GATE_RESID && p0.resid_tma;
+        const float2* cs = nullptr;
+        if constexpr (MODE == EPI_QKV_PACK) cs = stage_rope_table(p0.e.pk, sR);   // both groups share the geometry
         if (rt && lane == 0 && pair < num_tiles) {
             const TileRef t = tile_ref(p0, p1, tiles0, pair);
             resid_load(&maps.r[t.grp], rp, t.nb * BN, t.mb * BM2 + rbase);
@@ -658,7 +678,7 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
                     break;
             } else {
                 if (more) prefetch_resid<MODE>(u.grp ? p1 : p0, u.mb * BM2 + rbase + lane, u.nb * BN);
-                epilogue_row<MODE, BN>(p, taddr, t.mb * BM2 + rbase + lane, t.nb * BN);
+                epilogue_row<MODE, BN>(p, taddr, t.mb * BM2 + rbase + lane, t.nb * BN, cs);
             }
             sm100::tc_fence_before();
             __syncwarp();

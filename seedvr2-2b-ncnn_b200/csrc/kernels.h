@@ -29,6 +29,7 @@ struct PackEpi {
     const int4* tokpos = nullptr;   // [Lv] (vid packed index gi, window, pos0 | pos1 << 16, pos2)
     const int* cums = nullptr;      // [nwin+1] packed row offsets of windows
     const float2* cs = nullptr;     // [npos][21] (cos, sin)
+    int npos = 0;
     const float *nq0 = nullptr, *nk0 = nullptr;     // vid flow qk-norm weights [128]
     const float *nq1 = nullptr, *nk1 = nullptr;     // txt flow
     float eps = 1e-5f;
@@ -130,6 +131,27 @@ void awa_coalesce_div(const float* toutw, int nwin, int TXT, void* att_txt, int 
 // (a null index array means the identity).
 void copy_rows_f32(const float* src, int ld_src, const int* src_idx, float* dst, int ld_dst, const int* dst_idx,
                    int n, int width, cudaStream_t s);
+
+// ---------------------------------------------------------------- sharded exchanges over peer memory (k_shard.cu)
+// Every rank's buffers, mapped into this rank (own entries are local).
+struct ShardPeers {
+    float* txtp[8] = {};          // [2 slots][TXT * 2560] txt partial sums
+    uint32_t* flags[8] = {};      // [2 kinds][2 slots][world] ready flags
+    float* x[2][8] = {};          // residual of each layout parity, [rows][2560]
+    int world = 1, rank = 0;
+};
+// Forward counter (flag values grow across forwards).
+void shard_epoch_inc(uint32_t* epoch, cudaStream_t s);
+// Publish this rank's partial of `layer`, wait for all ranks', write their
+// rank-ordered sum / divisor to the TXT rows at out (stride ld).
+void shard_txt_reduce(const ShardPeers& P, const uint32_t* epoch, int layer, int TXT, float divisor, void* out, int ld,
+                      ActT t, cudaStream_t s);
+// Rows src[k] of X[p] -> rows dst[k] of rank rank_of[k]'s X[1-p]; then flags
+// and a wait until every rank's rows of this exchange have arrived.
+void shard_exchange_rows(const ShardPeers& P, int p, const int* src, const int* rank_of, const int* dst, int n,
+                         const uint32_t* epoch, int layer, cudaStream_t s);
+// Reads and clears the flag a timed-out wait sets.  Returns a cudaError_t value.
+int shard_error_reset(int* had_error);
 
 // ---------------------------------------------------------------- grid / engine formats (k_engine.cu)
 // (T, H, W, 33) -> (T*H/2*W/2, 132) and (T*H/2*W/2, 64) -> (T, H, W, 16), src/dit_vk.cpp:717-750.

@@ -64,6 +64,8 @@ bool make_shard_plan(const WinGeom& ns, const WinTables& tns, const WinGeom& sh,
             }
         }
     }
+    out.owner[0] = owner[0]; out.owner[1] = owner[1];
+    out.lrow[0] = lrow[0]; out.lrow[1] = lrow[1];
     for (int p = 0; p < 2; p++) {
         const int q1 = 1 - p;
         std::vector<std::vector<int>> snd(world), rcv(world);

@@ -29,6 +29,9 @@ struct ShardPlan {
     // (sender, receiver) pair rows go in ascending grid-token order, which
     // both sides derive independently.  q == rank is the local move.
     std::vector<int> send_idx[2], send_off[2], recv_idx[2], recv_off[2];
+    // every rank's view: owner[p][tok] = rank holding grid token tok in parity
+    // p's layout, lrow[p][tok] = its local row there
+    std::vector<int> owner[2], lrow[2];
     int n_local(int p) const { return (int)tokens[p].size(); }
 };
 

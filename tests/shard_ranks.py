@@ -74,7 +74,9 @@ def gloo_exchange(rank: int, world: int, port: int, grid, out_dir: str):
         dist.destroy_process_group()
 
 
-def nccl_forward(rank: int, world: int, uid: bytes, prec: int, grid, out_dir: str):
+def nccl_forward(rank: int, world: int, uid: bytes, prec: int, grid, out_dir: str, p2p: bool = True):
+    # p2p: the per-layer exchanges through peer-memory kernels (default), else NCCL calls
+    os.environ["S2B_SHARD_P2P"] = "1" if p2p else "0"
     import s2b
     T, H, W = grid
     Lv, TXT = T * H * W, 58

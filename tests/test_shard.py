@@ -106,13 +106,14 @@ def _gpu_count() -> int:
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("p2p", [True, False], ids=["peer", "nccl"])
 @pytest.mark.parametrize("prec", [s2b.PREC_BF16, s2b.PREC_FP32])
-def test_nccl_shard_forward_matches_single_gpu(tmp_path, prec):
+def test_nccl_shard_forward_matches_single_gpu(tmp_path, prec, p2p):
     if _gpu_count() < 2:
         pytest.skip("needs 2 GPUs")
     import shard_ranks
     uid = s2b.nccl_unique_id()
-    _run_ranks(shard_ranks.nccl_forward, 2, (uid, prec, GRID_1080P, str(tmp_path)), 900)
+    _run_ranks(shard_ranks.nccl_forward, 2, (uid, prec, GRID_1080P, str(tmp_path), p2p), 900)
     o0, o1 = np.load(tmp_path / "rank0.npz"), np.load(tmp_path / "rank1.npz")
     # every rank returns the whole output, identical across ranks and calls
     np.testing.assert_array_equal(o0["sr"], o1["sr"])
