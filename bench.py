@@ -39,6 +39,9 @@ sys.path.insert(0, os.path.join(ROOT, "seedvr2-2b-ncnn_b200"))
 sys.path.insert(0, ROOT)
 
 GRID = (1, 68, 80)        # tokens of a 1080p output (latent 136 x 160)
+# cfg2 720p (latent 90 x 106), cfg3 1080p, cfg5 2160p (latent 270 x 318)
+GRIDS = {"720p": (1, 45, 53), "1080p": (1, 68, 80), "2160p": (1, 135, 159)}
+CFG = {"720p": "cfg2", "1080p": "cfg3", "2160p": "cfg5"}
 TXT = 58
 TIMESTEP = 1000.0
 WEIGHT_SEED = 1234
@@ -295,12 +298,15 @@ def run_ours(args):
                 "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": False,
                 "scaling": "strong" if image else "weak", "vs_baseline": None, "dtype": args.precision,
                 "data": "synthetic",
-                "config": {"workload": ("cfg3: 1080p 32-layer NaDiT DiT forward of one frame, windows sharded "
-                                        "over the GPUs (txt all-reduce + residual exchange per layer, NCCL)")
-                           if image else ("cfg3/cfg4: 1080p 32-layer NaDiT DiT forward per frame, frames "
-                                          "round-robin over GPUs (frame k: seed 42+k)"),
+                "config": {"workload": (f"{CFG[args.res]}: {args.res} 32-layer NaDiT DiT forward of one frame, "
+                                        "windows sharded over the GPUs (txt mean + residual exchange per layer "
+                                        "over NVLink peer memory)")
+                           if image else (f"{CFG[args.res]}/cfg4: {args.res} 32-layer NaDiT DiT forward per frame, "
+                                          "frames round-robin over GPUs (frame k: seed 42+k)"),
                            "mode": args.mode,
-                           "precision": args.precision, "grid": list(GRID), "txt": TXT, "windows": [16, 25],
+                           "res": args.res, "precision": args.precision, "grid": list(GRID), "txt": TXT,
+                           "windows": [s2b.make_win(T, H, W, (4, 3, 3), TXT, False).nwin,
+                                       s2b.make_win(T, H, W, (4, 3, 3), TXT, True).nwin],
                            "frames_per_step_per_gpu": 1,
                            "l2": "no flush: every forward streams 6.7 GB of bf16 weights (> 126 MB L2)"},
                 "e2e": {"value": e2e_value, "unit": "ms/frame", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -392,12 +398,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
+    ap.add_argument("--res", choices=sorted(GRIDS), default="1080p",
+                    help="output resolution of the workload (the metric is quoted at 1080p)")
     ap.add_argument("--mode", choices=["frames", "image"], default="frames",
                     help="frames: independent frames dealt round-robin (weak scaling); image: one frame's "
                          "windows sharded over the GPUs (strong scaling)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the reference CPU baseline leg")
     args = ap.parse_args()
     args.warmup_ref = 0
+    global GRID
+    GRID = GRIDS[args.res]
     if args.kernel_case:
         return run_kernel_case(args.kernel_case)
     if args.warmup < 3:

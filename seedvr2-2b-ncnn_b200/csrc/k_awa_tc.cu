@@ -29,6 +29,7 @@ namespace s2b {
 bool make_tmap_bf16(CUtensorMap* m, const void* base, int rows, int cols, int ld, int box_rows, int box_cols);
 int awa_tc_kernel_version();
 int awa_tc_poly_exp();
+int awa_tc_alu_pack();
 
 namespace {
 
@@ -105,25 +106,38 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
-// Two non-negative finite floats rounded to nearest-even bf16 and packed
-// (a in the low half) with integer ALU operations, leaving the conversion
+// Two floats rounded to nearest-even bf16 and packed (a in the low half):
+// with the conversion instruction, or (ALU) by integer rounding of the two
+// non-negative finite values, which leaves the conversion/transcendental
 // unit to the exponentials.
-__device__ __forceinline__ uint32_t pack_bf16x2_rn(float a, float b) {
-    uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
-    ua += 0x7FFFu + ((ua >> 16) & 1u);
-    ub += 0x7FFFu + ((ub >> 16) & 1u);
-    return __byte_perm(ua, ub, 0x7632);
+template <bool ALU>
+__device__ __forceinline__ uint32_t pack_bf16x2_t(float a, float b) {
+    if constexpr (ALU) {
+        uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+        ua += 0x7FFFu + ((ua >> 16) & 1u);
+        ub += 0x7FFFu + ((ub >> 16) & 1u);
+        return __byte_perm(ua, ub, 0x7632);
+    } else {
+        __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
 }
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float a, float b) { return pack_bf16x2_t<false>(a, b); }
 
 // Max of n (<= 64) leading values of v, -inf for the rest, through 8
 // independent accumulators (a chain of 8 instead of 64 dependent fmaxf).
-__device__ __forceinline__ float max64(const float* v, int nvalid) {
+template <bool MASK>
+__device__ __forceinline__ float max64_t(const float* v, int nvalid) {
     float a[8];
     #pragma unroll
     for (int i = 0; i < 8; i++) a[i] = -INFINITY;
     #pragma unroll
-    for (int u = 0; u < 64; u++) a[u & 7] = fmaxf(a[u & 7], (u < nvalid) ? v[u] : -INFINITY);
+    for (int u = 0; u < 64; u++) a[u & 7] = fmaxf(a[u & 7], (!MASK || u < nvalid) ? v[u] : -INFINITY);
     return fmaxf(fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3])), fmaxf(fmaxf(a[4], a[5]), fmaxf(a[6], a[7])));
+}
+// nvalid >= 64: no masking instructions at all.
+__device__ __forceinline__ float max64(const float* v, int nvalid) {
+    return nvalid >= 64 ? max64_t<false>(v, 64) : max64_t<true>(v, nvalid);
 }
 __device__ __forceinline__ float sum8(const float* a) {
     return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
@@ -750,6 +764,7 @@ __device__ __forceinline__ uint64_t desc_v64(const void* tile, uint32_t k_group_
     return d;
 }
 
+template <bool POLY, bool ALU>
 __global__ void __launch_bounds__(T4_THREADS, 2)
 k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
                const __grid_constant__ CUtensorMap tV, const AttnParams p) {
@@ -918,10 +933,13 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
             float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
             #pragma unroll
             for (int u = 0; u < 32; u++) {
-                float a = ex2_approx(fmaf(v[2 * u], sl, nm)), b = ex2_approx(fmaf(v[2 * u + 1], sl, nm));
+                const float xa = fmaf(v[2 * u], sl, nm), xb = fmaf(v[2 * u + 1], sl, nm);
+                float a, b;
+                if (POLY && (u & 3) == 3) { a = ex2_poly(xa); b = ex2_poly(xb); }
+                else { a = ex2_approx(xa); b = ex2_approx(xb); }
                 if (!full) { a = (2 * u < kvalid) ? a : 0.f; b = (2 * u + 1 < kvalid) ? b : 0.f; }
                 ls[u & 7] += a + b;
-                pk[u] = pack_bf16x2_rn(a, b);
+                pk[u] = pack_bf16x2_t<ALU>(a, b);
             }
             l += sum8(ls);
             tmem_st32u(tmem + lane_off + st * 64, pk);
@@ -994,7 +1012,11 @@ int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, const AwaDev& 
         if (!make_tmap_bf16(&tk4, Kp, rows, D, D, KT4, 64) || !make_tmap_bf16(&tv4, Vp, rows, D, D, KT4, 64))
             return -1;
         dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
-        k_awa_attn_tc4<<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
+        const int poly = awa_tc_poly_exp(), alu = awa_tc_alu_pack();
+        if (poly && alu) k_awa_attn_tc4<true, true><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
+        else if (poly) k_awa_attn_tc4<true, false><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
+        else if (alu) k_awa_attn_tc4<false, true><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
+        else k_awa_attn_tc4<false, false><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
     } else if (awa_tc_kernel_version() == 1) {
         dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
         if (awa_tc_poly_exp())
@@ -1023,8 +1045,10 @@ int awa_tc_init_device() {
         return (int)e;
     if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES))
         return (int)e;
-    if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc4, cudaFuncAttributeMaxDynamicSharedMemorySize, T4_SMEM))
-        return (int)e;
+    const void* v4[4] = {(const void*)k_awa_attn_tc4<false, false>, (const void*)k_awa_attn_tc4<false, true>,
+                         (const void*)k_awa_attn_tc4<true, false>, (const void*)k_awa_attn_tc4<true, true>};
+    for (const void* k : v4)
+        if (cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, T4_SMEM)) return (int)e;
     if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc2<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, T2_SMEM))
         return (int)e;
     return (int)cudaFuncSetAttribute(k_awa_attn_tc2<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, T2_SMEM);
@@ -1033,6 +1057,15 @@ int awa_tc_init_device() {
 // S2B_ATTN_POLY=1: a quarter of the softmax exponentials on the FMA pipe
 // (ex2_poly).  Off by default: measured slower at 1080p (the FMA pipe work
 // costs more than the conversion unit it frees).
+// S2B_ATTN_PACK=alu: bf16 packing of P by integer rounding instead of the
+// conversion instruction (64-key kernel).  Per 1080p forward, alternating in
+// one process: conversion 2.6-3.0 ms, integer 3.0-3.1 ms; with a quarter of
+// the exponentials as polynomials (S2B_ATTN_POLY=1) 2.9-3.1 / 3.1-3.2 ms.
+int awa_tc_alu_pack() {
+    const char* e = std::getenv("S2B_ATTN_PACK");
+    return (e && e[0] == 'a') ? 1 : 0;
+}
+
 int awa_tc_poly_exp() {
     const char* e = std::getenv("S2B_ATTN_POLY");
     return (e && e[0] == '1') ? 1 : 0;
