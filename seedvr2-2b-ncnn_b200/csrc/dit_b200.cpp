@@ -288,7 +288,29 @@ int DitB200::load_weights(const char* dir_c, bool synth, uint64_t seed, int lo, 
     // shared layers: the txt flow uses the same Linear objects
     layer_lo_ = lo; layer_hi_ = hi;
     weights_ = true;
+    if (act_ == ACT_F32) return prepare_tf32x3();
     return OK;
+}
+
+// fp32 contexts: the [hi | lo] tf32 halves of every Linear the tensor-core
+// fp32 GEMM serves (input width a multiple of 32), unless S2B_FP32_TC=0.
+int DitB200::prepare_tf32x3() {
+    const char* env = std::getenv("S2B_FP32_TC");
+    tf32x3_ = !(env && env[0] == '0');
+    if (!tf32x3_) return OK;
+    auto split = [&](Linear& L) -> int {
+        if (!L.w.bytes || L.t != ACT_F32 || L.in % 32) return OK;
+        if (int rc = cuda_check(L.w2.ensure((size_t)L.out * 2 * L.in * 4), "cudaMalloc(tf32 weights)")) return rc;
+        split_tf32(L.w.as<float>(), L.ld, L.out, L.in, L.w2.as<float>(), 2 * L.in, stream_);
+        return OK;
+    };
+    if (int rc = split(txt_in_)) return rc;
+    if (int rc = split(vid_out_)) return rc;
+    for (auto& row : blk_)
+        for (auto& B : row)
+            for (Linear* L : {&B.qkv, &B.out, &B.mlp_hg, &B.mlp_out})
+                if (int rc = split(*L)) return rc;
+    return cuda_check(cudaStreamSynchronize(stream_), "tf32 weight split");
 }
 
 // ------------------------------------------------------------------ geometry
@@ -420,6 +442,7 @@ int DitB200::ensure_acts(int Lv, int TXT) {
     // [h | g] fp32 staging of the SIMT SwiGLU path (the tcgen05 path fuses it)
     const bool need_hg = act_ == ACT_F32 || !gemm_tc_supported((int)M, 2 * MLP_DIM, DIM, DIM, DIM);
     if (need_hg && (rc = cuda_check(HG_.ensure(M * 2 * MLP_DIM * 4), "cudaMalloc(HG)"))) return rc;
+    if (act_ == ACT_F32 && tf32x3_ && (rc = cuda_check(A2_.ensure(M * 2 * MLP_DIM * 4), "cudaMalloc(A2)"))) return rc;
     if ((rc = cuda_check(Hs_.ensure(M * MLP_DIM * ab), "cudaMalloc(Hs)"))) return rc;
     if ((rc = cuda_check(VPIN_.ensure((size_t)Lv * PATCH_IN_PAD * ab), "cudaMalloc(VPIN)"))) return rc;
     if ((rc = cuda_check(TIN_.ensure((size_t)TXT * TXT_IN * ab), "cudaMalloc(TIN)"))) return rc;
@@ -433,6 +456,17 @@ int DitB200::ensure_acts(int Lv, int TXT) {
 // ------------------------------------------------------------------ enqueue
 void DitB200::gemm(const void* A, int lda, const Linear& L, int M, const GemmEpi& e, cudaStream_t s) {
     if (M <= 0) return;
+    if (act_ == ACT_F32 && L.w2.bytes && e.mode != EPI_QKV_PACK && A2_.bytes >= (size_t)M * 2 * L.in * 4 &&
+        gemm_tf32x3_supported(M, L.out, L.in, 2 * L.in, 2 * L.in)) {
+        // fp32 path on the tensor cores: split the activations, then hi*hi + hi*lo + lo*hi
+        pbeg(KK_GEMM_SIMT, 2.0 * M * L.out * L.in,
+             (double)M * L.in * 12 + (double)L.out * L.in * 8 + (double)M * L.out * (e.mode == EPI_GATE_RESID ? 8 : 4), s);
+        split_tf32((const float*)A, lda, M, L.in, A2_.as<float>(), 2 * L.in, s);
+        const int rc = gemm_tf32x3(A2_.p, 2 * L.in, L.w2.p, 2 * L.in, M, L.out, L.in, e, s, &launches_);
+        launches_++;
+        pend(s);
+        if (rc == 0) return;
+    }
     const double flops = 2.0 * M * L.out * L.in;
     const double bytes = (double)M * L.in * act_bytes(act_) + (double)L.out * L.in * act_bytes(L.t) +
                          (double)M * L.out * (e.mode == EPI_GATE_RESID ? 8 : e.mode == EPI_SWIGLU ? act_bytes(e.out_t) / 2.0 : act_bytes(e.out_t));
@@ -895,6 +929,11 @@ int DitB200::linear(const float* x, int M, int K, const float* W, int N, const f
     L.t = act_; L.out = N; L.in = K; L.ld = ld;
     L.w = std::move(dwa);
     L.b = std::move(db);
+    if (act_ == ACT_F32 && tf32x3_ && K % 32 == 0) {
+        if ((rc = cuda_check(L.w2.ensure((size_t)N * 2 * K * 4), "cudaMalloc"))) return rc;
+        split_tf32(L.w.as<float>(), ld, N, K, L.w2.as<float>(), 2 * K, stream_);
+        if ((rc = cuda_check(A2_.ensure((size_t)M * 2 * K * 4), "cudaMalloc"))) return rc;
+    }
     GemmEpi e; e.mode = EPI_STORE; e.bias = L.bias(); e.out = dy.p; e.ldo = N; e.out_t = ACT_F32;
     gemm(dxa.p, ld, L, M, e, stream_);
     cudaMemcpyAsync(y, dy.p, (size_t)M * N * 4, cudaMemcpyDeviceToHost, stream_);

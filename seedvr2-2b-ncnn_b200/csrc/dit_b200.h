@@ -56,6 +56,7 @@ struct GeomDev {
 
 struct Linear {
     DevBuf w;          // [out][ld] in `t`
+    DevBuf w2;         // fp32 contexts: [out][2*in] = [tf32 hi | lo] halves for the tensor-core fp32 GEMM
     DevBuf b;          // [out] fp32 or empty
     ActT t = ACT_F32;
     int out = 0, in = 0, ld = 0;
@@ -203,6 +204,9 @@ private:
     // activations
     int cap_Lv_ = 0, cap_TXT_ = 0;
     DevBuf X_, Xn_, QKV_, ATT_, Qp_, Kp_, Vp_, TOUTW_, HG_, Hs_, VPIN_, TIN_, SR_, VIDIN_F_, TXTIN_F_;
+    DevBuf A2_;         // fp32 contexts: [M][2K] split activations of the tensor-core fp32 GEMM
+    bool tf32x3_ = false;
+    int prepare_tf32x3();
     size_t qkv_pack_rows_ = 0;
 
     // captured full forward

@@ -216,6 +216,7 @@ int DitB200::shard_prepare(int Lv, int TXT) {
     if ((act_ == ACT_F32 || !gemm_tc_supported((int)Mmax, 2 * MLP_DIM, DIM, DIM, DIM)) &&
         (rc = alloc(HG_, Mmax * 2 * MLP_DIM * 4, "cudaMalloc(HG)")))
         return rc;
+    if (act_ == ACT_F32 && tf32x3_ && (rc = alloc(A2_, Mmax * 2 * MLP_DIM * 4, "cudaMalloc(A2)"))) return rc;
     if ((rc = up(S.tok0, plan.tokens[0]))) return rc;
     if ((rc = up(S.tok1, plan.tokens[(NUM_LAYERS - 1) % 2]))) return rc;
     for (int p = 0; p < 2; p++) {

@@ -178,7 +178,27 @@ __global__ void k_to_f32(const TI* __restrict__ src, size_t n, float* __restrict
     if (i < n) dst[i] = Cvt<TI>::to_f(src[i]);
 }
 
+// hi = x rounded to the nearest tf32 (10 explicit mantissa bits, ties to
+// even), lo = x - hi (exact in fp32).
+__global__ void k_split_tf32(const float* __restrict__ src, int ld_src, int rows, int cols, float* __restrict__ dst,
+                             int ld_dst) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)rows * cols) return;
+    const int r = (int)(i / cols), c = (int)(i % cols);
+    const float x = src[(size_t)r * ld_src + c];
+    uint32_t b = __float_as_uint(x);
+    if ((b & 0x7F800000u) != 0x7F800000u) b = (b + 0xFFFu + ((b >> 13) & 1u)) & 0xFFFFE000u;
+    const float hi = __uint_as_float(b);
+    dst[(size_t)r * ld_dst + c] = hi;
+    dst[(size_t)r * ld_dst + cols + c] = __fsub_rn(x, hi);
+}
+
 }  // namespace
+
+void split_tf32(const float* src, int ld_src, int rows, int cols, float* dst, int ld_dst, cudaStream_t s) {
+    const size_t n = (size_t)rows * cols;
+    if (n) k_split_tf32<<<(int)((n + 255) / 256), 256, 0, s>>>(src, ld_src, rows, cols, dst, ld_dst);
+}
 
 void rmsnorm_mod(const float* X, int ldx, int rows, int split, const float* sc0, const float* sh0,
                  const float* sc1, const float* sh1, const float* affine, float eps, void* Y, int ldy,

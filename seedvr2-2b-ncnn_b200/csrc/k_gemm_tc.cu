@@ -53,20 +53,35 @@ constexpr uint32_t IDESC1 = sm100::idesc_bf16_f32(BM1, BN1);
 // would leave much of the last wave idle); each CTA stages 128 A rows and
 // BN / 2 B rows per k-block.
 constexpr int BM2 = 256;
-template <int BN>
+// KIND_BF16: bf16 operands, 64-element k-blocks.  KIND_TF32X3: the fp32
+// path's "3xTF32" split product -- A and B arrive as [hi | lo] halves of fp32
+// (hi = x rounded to tf32, lo = x - hi), and every k-step issues
+// hi*hi + hi*lo + lo*hi as tcgen05.mma kind::tf32 (fp32 accumulate), which
+// keeps the products to about fp32 accuracy; k-blocks of 32 fp32 elements
+// (one 128-byte swizzle row), each stage holding the four tiles.
+constexpr int KIND_BF16 = 0, KIND_TF32X3 = 1;
+constexpr uint32_t idesc_tf32_f32(int M, int N) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+template <int BN, int KIND = KIND_BF16>
 struct PairCfg {
-    static constexpr int STAGES = BN == 256 ? 6 : 8;
-    static constexpr int A_BYTES = 128 * BK * 2;
-    static constexpr int B_BYTES = (BN / 2) * BK * 2;
+    static constexpr int KB = KIND == KIND_BF16 ? BK : 32;                 // k elements per stage
+    static constexpr int NPART = KIND == KIND_BF16 ? 1 : 2;                // operand parts (hi, lo)
+    static constexpr int A_TILE = 128 * 128;                               // bytes of one 128-row, 128-B tile
+    static constexpr int B_TILE = (BN / 2) * 128;
+    static constexpr int A_BYTES = NPART * A_TILE;
+    static constexpr int B_BYTES = NPART * B_TILE;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = KIND == KIND_TF32X3 ? 3 : (BN == 256 ? 6 : 8);
     static constexpr int SMEM = STAGES * STAGE_BYTES + RES_BYTES + 1024 + 512;
-    static constexpr uint32_t IDESC = sm100::idesc_bf16_f32(BM2, BN);
+    static constexpr uint32_t IDESC = KIND == KIND_BF16 ? sm100::idesc_bf16_f32(BM2, BN) : idesc_tf32_f32(BM2, BN);
 };
 
 __device__ int g_tc_err;
 
 struct TcParams {
     int M, N, num_m, num_n, num_kb;
+    int kdim;            // K (the column offset of the lo half in the tf32x3 kind)
     int resid_tma;       // EPI_GATE_RESID through TMA-staged residual boxes
     GemmEpi e;
 };
@@ -546,11 +561,11 @@ __device__ __forceinline__ TileRef tile_ref(const TcParams& p0, const TcParams& 
     return t;
 }
 
-template <int MODE, int BN>
+template <int MODE, int BN, int KIND = KIND_BF16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ TcParams p0,
                const __grid_constant__ TcParams p1, int ngroups) {
-    using C = PairCfg<BN>;
+    using C = PairCfg<BN, KIND>;
     constexpr int STAGES2 = C::STAGES, A2_BYTES = C::A_BYTES, B2_BYTES = C::B_BYTES, STAGE2_BYTES = C::STAGE_BYTES;
     constexpr int ACC = BN;                                 // TMEM columns per accumulator
     extern __shared__ uint8_t smem_raw[];
@@ -601,8 +616,15 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
                     // both CTAs' bytes complete on the even CTA's full barrier
                     if (rank == 0) sm100::mbar_arrive_expect_tx(&ctl->full[stage], 2 * STAGE2_BYTES);
                     const uint32_t fb = sm100::map_to_rank(&ctl->full[stage], 0);
-                    sm100::tma_load_2d_pair(sA + stage * A2_BYTES, ta, fb, kb * BK, t.mb * BM2 + (int)rank * 128);
-                    sm100::tma_load_2d_pair(sB + stage * B2_BYTES, tb, fb, kb * BK, t.nb * BN + (int)rank * (BN / 2));
+                    #pragma unroll
+                    for (int part = 0; part < C::NPART; part++) {
+                        // part 1 (lo) sits K elements to the right of part 0 (hi)
+                        const int x = part * p0.kdim + kb * C::KB;
+                        sm100::tma_load_2d_pair(sA + stage * A2_BYTES + part * C::A_TILE, ta, fb, x,
+                                                t.mb * BM2 + (int)rank * 128);
+                        sm100::tma_load_2d_pair(sB + stage * B2_BYTES + part * C::B_TILE, tb, fb, x,
+                                                t.nb * BN + (int)rank * (BN / 2));
+                    }
                     issued++;
                     if (++stage == STAGES2) { stage = 0; phase ^= 1; }
                 }
@@ -633,10 +655,23 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
                     sm100::tc_fence_after();
                     const uint8_t* a = sA + stage * A2_BYTES;
                     const uint8_t* b = sB + stage * B2_BYTES;
-                    #pragma unroll
-                    for (int kk = 0; kk < BK / 16; kk++)
-                        sm100::mma_bf16_pair(d, sm100::desc_kmajor_sw128(a, kk * 32),
-                                             sm100::desc_kmajor_sw128(b, kk * 32), C::IDESC, (kb | kk) != 0);
+                    if constexpr (KIND == KIND_BF16) {
+                        #pragma unroll
+                        for (int kk = 0; kk < BK / 16; kk++)
+                            sm100::mma_bf16_pair(d, sm100::desc_kmajor_sw128(a, kk * 32),
+                                                 sm100::desc_kmajor_sw128(b, kk * 32), C::IDESC, (kb | kk) != 0);
+                    } else {
+                        const uint8_t* al = a + C::A_TILE;
+                        const uint8_t* bl = b + C::B_TILE;
+                        #pragma unroll
+                        for (int kk = 0; kk < C::KB / 8; kk++) {      // 8 tf32 = 32 bytes per k-step
+                            const uint64_t ah = sm100::desc_kmajor_sw128(a, kk * 32);
+                            const uint64_t bh = sm100::desc_kmajor_sw128(b, kk * 32);
+                            sm100::mma_tf32_pair(d, ah, bh, C::IDESC, (kb | kk) != 0);
+                            sm100::mma_tf32_pair(d, ah, sm100::desc_kmajor_sw128(bl, kk * 32), C::IDESC, 1);
+                            sm100::mma_tf32_pair(d, sm100::desc_kmajor_sw128(al, kk * 32), bh, C::IDESC, 1);
+                        }
+                    }
                     // release this stage in both CTAs
                     sm100::mma_commit_pair(sm100::map_to_rank(&ctl->empty[stage], 0));
                     sm100::mma_commit_pair(sm100::map_to_rank(&ctl->empty[stage], 1));
@@ -768,6 +803,7 @@ static bool pair_group(const void* A, int lda, const void* W, int ldw, int M, in
                        TcParams& p, CUtensorMap& ta, CUtensorMap& tb, CUtensorMap& tr) {
     p.M = M; p.N = N;
     p.num_kb = (K + BK - 1) / BK;
+    p.kdim = K;
     p.e = e;
     // gate/residual epilogue through TMA boxes when the residual is 16-B aligned
     p.resid_tma = e.mode == EPI_GATE_RESID && e.resid && ((uintptr_t)e.resid & 15) == 0 && e.ldr % 4 == 0 &&
@@ -828,6 +864,7 @@ int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K,
         TcParams p;
         p.M = M; p.N = N;
         p.num_kb = (K + BK - 1) / BK;
+        p.kdim = K;
         p.e = e;
         CUtensorMap ta, tb, tr;
         p.resid_tma = e.mode == EPI_GATE_RESID && e.resid && ((uintptr_t)e.resid & 15) == 0 && e.ldr % 4 == 0 &&
@@ -845,6 +882,58 @@ int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K,
             case EPI_SWIGLU: k_gemm_tc<EPI_SWIGLU><<<grid, NUM_THREADS, SMEM1_BYTES, s>>>(ta, tb, tr, p); break;
             case EPI_QKV_PACK: k_gemm_tc<EPI_QKV_PACK><<<grid, NUM_THREADS, SMEM1_BYTES, s>>>(ta, tb, tr, p); break;
         }
+    }
+    if (launches) (*launches)++;
+    return 0;
+}
+
+// fp32 [rows][cols] (row stride ld elements) for the tf32x3 kind: boxes of
+// box_rows x 32 elements (one 128-byte swizzle row), zero fill.
+static bool make_tmap_f32(CUtensorMap* m, const void* base, int rows, int cols, int ld, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+    const cuuint32_t box[2] = {32, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool gemm_tf32x3_supported(int M, int N, int K, int lda2, int ldw2) {
+    return M > 0 && N > 0 && K > 0 && K % 32 == 0 && N % 32 == 0 && lda2 % 4 == 0 && ldw2 % 4 == 0 &&
+           lda2 >= 2 * K && ldw2 >= 2 * K && encode_fn() != nullptr;
+}
+
+int gemm_tf32x3(const void* A2, int lda2, const void* W2, int ldw2, int M, int N, int K, const GemmEpi& e,
+                cudaStream_t s, int* launches) {
+    if (!gemm_tf32x3_supported(M, N, K, lda2, ldw2)) return -1;
+    if (((uintptr_t)A2 & 15) || ((uintptr_t)W2 & 15)) return -1;
+    if (e.mode == EPI_SWIGLU && N % 256) return -1;
+    if (e.mode == EPI_QKV_PACK) return -1;            // the fused pack writes bf16 operands
+    using C = PairCfg<256, KIND_TF32X3>;
+    PairMaps maps;
+    TcParams p;
+    p.M = M; p.N = N;
+    p.num_kb = K / C::KB;
+    p.kdim = K;
+    p.e = e;
+    p.resid_tma = e.mode == EPI_GATE_RESID && e.resid && ((uintptr_t)e.resid & 15) == 0 && e.ldr % 4 == 0 &&
+                  make_tmap_resid(&maps.r[0], e.resid, M, N, e.ldr);
+    if (!p.resid_tma) std::memset(&maps.r[0], 0, sizeof maps.r[0]);
+    if (!make_tmap_f32(&maps.a[0], A2, M, 2 * K, lda2, 128) || !make_tmap_f32(&maps.b[0], W2, N, 2 * K, ldw2, 128))
+        return -1;
+    p.num_m = (M + BM2 - 1) / BM2;
+    p.num_n = (N + 255) / 256;
+    const int tiles = p.num_m * p.num_n;
+    int pairs = num_sms() / 2;
+    if (tiles < pairs) pairs = tiles;
+    switch (e.mode) {
+        case EPI_STORE: k_gemm_tc_pair<EPI_STORE, 256, KIND_TF32X3><<<2 * pairs, NUM_THREADS, C::SMEM, s>>>(maps, p, p, 1); break;
+        case EPI_GATE_RESID: k_gemm_tc_pair<EPI_GATE_RESID, 256, KIND_TF32X3><<<2 * pairs, NUM_THREADS, C::SMEM, s>>>(maps, p, p, 1); break;
+        case EPI_SWIGLU: k_gemm_tc_pair<EPI_SWIGLU, 256, KIND_TF32X3><<<2 * pairs, NUM_THREADS, C::SMEM, s>>>(maps, p, p, 1); break;
+        default: return -1;
     }
     if (launches) (*launches)++;
     return 0;
@@ -889,6 +978,12 @@ int kernels_init_device() {
                             (const void*)k_gemm_tc_pair<EPI_SWIGLU, 256>, (const void*)k_gemm_tc_pair<EPI_QKV_PACK, 256>};
     const void* pairn[3] = {(const void*)k_gemm_tc_pair<EPI_STORE, 128>, (const void*)k_gemm_tc_pair<EPI_GATE_RESID, 128>,
                             (const void*)k_gemm_tc_pair<EPI_QKV_PACK, 128>};
+    const void* tf32k[3] = {(const void*)k_gemm_tc_pair<EPI_STORE, 256, KIND_TF32X3>,
+                            (const void*)k_gemm_tc_pair<EPI_GATE_RESID, 256, KIND_TF32X3>,
+                            (const void*)k_gemm_tc_pair<EPI_SWIGLU, 256, KIND_TF32X3>};
+    for (const void* k : tf32k)
+        if (cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg<256, KIND_TF32X3>::SMEM))
+            return (int)e;
     for (int i = 0; i < 4; i++) {
         cudaError_t e = cudaFuncSetAttribute(single[i], cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM1_BYTES);
         if (e == cudaSuccess) e = cudaFuncSetAttribute(pairk[i], cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg<256>::SMEM);

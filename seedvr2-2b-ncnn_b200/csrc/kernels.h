@@ -73,6 +73,14 @@ int gemm_tc(const void* A, int lda, const void* W, int ldw, int M, int N, int K,
 int gemm_tc_grouped(const void* A0, int lda0, const void* W0, int ldw0, int M0, const GemmEpi& e0, const void* A1,
                     int lda1, const void* W1, int ldw1, int M1, const GemmEpi& e1, int N, int K, cudaStream_t s,
                     int* launches);
+// fp32 GEMM on the tensor cores ("3xTF32"): A2 [M][2K] and W2 [N][2K] hold
+// [hi | lo] halves (split_tf32); C = A_hi W_hi^T + A_hi W_lo^T + A_lo W_hi^T
+// with fp32 accumulation.  K % 32 == 0; lda2 / ldw2 multiples of 4.
+bool gemm_tf32x3_supported(int M, int N, int K, int lda2, int ldw2);
+int gemm_tf32x3(const void* A2, int lda2, const void* W2, int ldw2, int M, int N, int K, const GemmEpi& e,
+                cudaStream_t s, int* launches);
+// dst[r][0..cols) = tf32(src[r][c]) (round to nearest), dst[r][cols..2cols) = src - that.
+void split_tf32(const float* src, int ld_src, int rows, int cols, float* dst, int ld_dst, cudaStream_t s);
 // Reads and clears the current device's tcgen05-kernel error flag (set when a
 // bounded wait expired).  Returns a cudaError_t value.
 int gemm_tc_error_reset(int* had_error);

@@ -197,3 +197,29 @@ def test_cpp_dropin_engine_matches_python(m5_small, inputs, tmp_path):
     finally:
         c.close()
     np.testing.assert_array_equal(got, np.concatenate([vl.ravel(), tl.ravel()]))
+
+
+@pytest.mark.parametrize("prec", [s2b.PREC_FP32, s2b.PREC_BF16], ids=["fp32", "bf16"])
+def test_temporal_windows_vs_port(port, m5_small, prec):
+    """T > 1 (temporal windows and RoPE time offsets, src/awa_window.cpp:26-27,
+    103-105): a 3 x 12 x 14 token grid through layers [0, 2) against the port."""
+    T3, H3, W3 = 3, 12, 14
+    L3 = T3 * H3 * W3
+    vp = s2b.patchify_grid(s2b.synth_vid_grid(T3, 2 * H3, 2 * W3, 5))
+    txt = s2b.synth_txt(TXT, 5)
+    gns = (T3, H3, W3, TXT) + port.make_win(T3, H3, W3, (4, 3, 3), TXT, False)
+    gsh = (T3, H3, W3, TXT) + port.make_win(T3, H3, W3, (4, 3, 3), TXT, True)
+    port.load(m5_small, 0, 2)
+    _, _, sr_r = port.forward_latent(gns, gsh, vp, txt, TS, 0, 2, True, True)
+    c = s2b.DitB200(0, prec)
+    try:
+        c.init(m5_small, 0, 2)
+        c.set_windows(s2b.make_win(T3, H3, W3, (4, 3, 3), TXT, False), s2b.make_win(T3, H3, W3, (4, 3, 3), TXT, True))
+        _, _, sr = c.forward_latent(vp, L3, txt, TXT, TS, 0, 2, True, True)
+    finally:
+        c.close()
+    cos, rel = cases.compare(sr, sr_r)
+    if prec == s2b.PREC_FP32:
+        assert cos >= 0.99999 and rel <= 1e-4, (cos, rel)
+    else:
+        assert cos >= 0.9999, (cos, rel)
