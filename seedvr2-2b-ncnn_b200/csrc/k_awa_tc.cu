@@ -14,8 +14,8 @@
 //                             the spent K tile.
 //   k_awa_attn_tc2            persistent, two query tiles per CTA sharing
 //                             every K/V tile (ping-pong softmax warpgroups).
-// Softmax: one query row per thread, ex2.approx, bf16 packing on the integer
-// ALU, lazy O rescale (only when a row's max grows by more than 2^8, so
+// Softmax: one query row per thread, ex2.approx, bf16 packing with the
+// conversion instruction (integer-ALU packing selectable), lazy O rescale (only when a row's max grows by more than 2^8, so
 // P <= 2^8).  Every mbarrier wait is bounded (error flag g_attn_err on
 // expiry); warp-collective TMEM instructions run under warp-uniform control.
 #include "kernels.h"
