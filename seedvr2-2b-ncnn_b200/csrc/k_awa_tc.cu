@@ -29,7 +29,6 @@ namespace s2b {
 bool make_tmap_bf16(CUtensorMap* m, const void* base, int rows, int cols, int ld, int box_rows, int box_cols);
 int awa_tc_kernel_version();
 int awa_tc_poly_exp();
-int awa_tc_alu_pack();
 
 namespace {
 
@@ -728,22 +727,29 @@ k_awa_attn_tc2(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
 // 64-key tiles through two-stage K and V rings.  TMEM per CTA (256 columns):
 // S in two 64-column slots (S_{j+1} is computed while the softmax reads
 // S_j), O in 128 columns.  The softmax writes P_j back into its S slot as
-// packed bf16 pairs, and P_j is the TMEM A operand of O += P_j V_j, so a K
-// stage is free as soon as its scores are computed and the next loads are
-// issued one key tile ahead.  Roles:
+// packed bf16 pairs, and P_j is the TMEM A operand of O += P_j V_j.  Roles:
 //   warps 0-3  softmax + epilogue (thread = query row)
 //   warp 4     TMEM allocation; lane 0 issues the MMAs:
 //                S_0; per j: S_{j+1} (once K_{j+1} is in and PV_{j-1} has
 //                read the slot), then PV_j (once P_j is ready)
-//   warp 5     lane 0 issues the TMA loads (Q; K_j, V_j as stages free up)
+//   warp 5     lane 0 issues the TMA loads: Q, then K one tile ahead of V
+//              (K_0, K_1, V_0, K_2, V_1, ...), since K_{j+1} gates S_{j+1}
+//              while V_j is needed only after the softmax of step j
 // The softmax rescales O only when a row's max grows by more than 2^8, and
-// then waits for the PV in flight first.
+// then waits for the PV in flight first.  A warp whose 32 rows all lie past
+// the window's end (the tail query tile) keeps the barrier protocol but does
+// no arithmetic: its O rows are never stored.  The epilogue stages each
+// warp's 32 normalised O rows in shared memory (the spent Q/K/V tiles) and
+// writes them back one row per warp instruction (256 B bf16 / 512 B fp32),
+// instead of 32 rows per instruction.
 constexpr int KT4 = 64;
 constexpr int KV4_BYTES = KT4 * D * 2;             // 16 KB: two 64-column halves of 8 KB
 constexpr int KV4_HALF = KV4_BYTES / 2;
 constexpr int T4_THREADS = 192;
 constexpr int T4_SMEM = TILE_BYTES + 4 * KV4_BYTES + 1024 + 256;
 constexpr uint32_t IDESC_QK4 = sm100::idesc_bf16_f32(QT, KT4);
+constexpr int STG_LD = D + 4;                      // staging row stride in floats (528 B: 4-way, not 32-way, banks)
+static_assert(4 * 32 * STG_LD * 4 <= TILE_BYTES + 4 * KV4_BYTES, "epilogue staging must fit in the Q/K/V tiles");
 
 struct Attn4Ctl {
     uint64_t q_full, k_full[2], k_empty[2], v_full[2], v_empty[2];
@@ -764,7 +770,71 @@ __device__ __forceinline__ uint64_t desc_v64(const void* tile, uint32_t k_group_
     return d;
 }
 
-template <bool POLY, bool ALU>
+// Packed fp32 pairs (Blackwell f32x2 arithmetic: one instruction per pair).
+__device__ __forceinline__ uint64_t f2pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// 2^x for a pair on the FMA pipe (the ex2_poly steps in f32x2 form): clamp
+// at -125 so the exponent field stays normal, x = j + f by adding 1.5 * 2^23
+// (round to nearest), the cubic on f, then j added to the exponent field
+// (the rounded sum's low bits are j, and its remaining bits vanish in the
+// shift by 23).
+__device__ __forceinline__ void ex2_poly2(uint64_t x2, float& ra, float& rb) {
+    float xa, xb;
+    f2unpack(x2, xa, xb);
+    const uint64_t xc = f2pack(fmaxf(xa, -125.f), fmaxf(xb, -125.f));
+    const uint64_t magic = f2pack(12582912.f, 12582912.f);
+    const uint64_t t = fadd2(xc, magic);
+    const uint64_t fr = fsub2(xc, fsub2(t, magic));
+    uint64_t p = ffma2(fr, f2pack(0.05508868396282196f, 0.05508868396282196f),
+                       f2pack(0.24260404706001282f, 0.24260404706001282f));
+    p = ffma2(fr, p, f2pack(0.6932762265205383f, 0.6932762265205383f));
+    p = ffma2(fr, p, f2pack(0.9999289512634277f, 0.9999289512634277f));
+    float pa, pb, ta, tb;
+    f2unpack(p, pa, pb);
+    f2unpack(t, ta, tb);
+    ra = __int_as_float(__float_as_int(pa) + (__float_as_int(ta) << 23));
+    rb = __int_as_float(__float_as_int(pb) + (__float_as_int(tb) << 23));
+}
+
+// Max of the 64 values (three-input max, 8 independent chains).
+__device__ __forceinline__ float max64_full(const float* v) {
+    float a[8];
+    #pragma unroll
+    for (int i = 0; i < 8; i++) a[i] = fmaxf(v[2 * i], v[2 * i + 1]);
+    #pragma unroll
+    for (int u = 16; u < 64; u += 2) a[(u >> 1) & 7] = fmax3(a[(u >> 1) & 7], v[u], v[u + 1]);
+    return fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+}
+
+// NP of every 4 exponential pairs on the FMA pipe (ex2_poly2), the rest on MUFU.
+template <int NP>
 __global__ void __launch_bounds__(T4_THREADS, 2)
 k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
                const __grid_constant__ CUtensorMap tV, const AttnParams p) {
@@ -784,7 +854,15 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
     volatile int* abort_flag = &ctl->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    if (threadIdx.x == 0) {
+    // the producer initialises the barriers and starts the Q / K_0 loads
+    // before the CTA-wide barrier, so their latency overlaps the TMEM
+    // allocation; the softmax threads fetch their rows' grid tokens now,
+    // long before the epilogue needs them
+    const int tid_prod = 5 * 32;
+    if (threadIdx.x == tid_prod) {
+        sm100::tma_prefetch_desc(&tQ);
+        sm100::tma_prefetch_desc(&tK);
+        sm100::tma_prefetch_desc(&tV);
         sm100::mbar_init(&ctl->q_full, 1);
         for (int i = 0; i < 2; i++) {
             sm100::mbar_init(&ctl->k_full[i], 1);
@@ -799,7 +877,26 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
         sm100::mbar_init(&ctl->drain, 1);
         ctl->abort = 0;
         sm100::fence_barrier_init();
+        sm100::mbar_arrive_expect_tx(&ctl->q_full, TILE_BYTES);
+        sm100::tma_load_2d(sQ, &tQ, &ctl->q_full, 0, row_base + q0);
+        sm100::tma_load_2d(sQ + HALF_BYTES, &tQ, &ctl->q_full, 64, row_base + q0);
+        sm100::mbar_arrive_expect_tx(&ctl->k_full[0], KV4_BYTES);
+        sm100::tma_load_2d(sK, &tK, &ctl->k_full[0], 0, row_base);
+        sm100::tma_load_2d(sK + KV4_HALF, &tK, &ctl->k_full[0], 64, row_base);
+        // the two-stage rings run only one tile ahead: bring every later K/V
+        // tile of this (window, head) into L2 now, so each ring load is an
+        // L2 hit rather than a DRAM round trip
+        for (int j = 1; j < nkt; j++) {
+            sm100::tma_prefetch_l2_2d(&tK, 0, row_base + j * KT4);
+            sm100::tma_prefetch_l2_2d(&tK, 64, row_base + j * KT4);
+        }
+        for (int j = 0; j < nkt; j++) {
+            sm100::tma_prefetch_l2_2d(&tV, 0, row_base + j * KT4);
+            sm100::tma_prefetch_l2_2d(&tV, 64, row_base + j * KT4);
+        }
     }
+    const int my_q = q0 + (threadIdx.x & 127);
+    const int my_tok = (warp < 4 && my_q < f) ? p.g.vidx[p.g.cumf[wi] + my_q] : 0;
     if (warp == 4) {
         sm100::tmem_alloc(&ctl->tmem_slot, TMEM_COLS);
         sm100::tmem_relinquish();
@@ -814,23 +911,29 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
         if (lane == 0) {
             // ---- TMA producer
             bool ok = true;
-            int kq = 0, vq = 0;                // K / V tiles issued
-            sm100::mbar_arrive_expect_tx(&ctl->q_full, TILE_BYTES);
-            sm100::tma_load_2d(sQ, &tQ, &ctl->q_full, 0, row_base + q0);
-            sm100::tma_load_2d(sQ + HALF_BYTES, &tQ, &ctl->q_full, 64, row_base + q0);
-            for (int j = 0; j < nkt && ok; j++) {
+            int kq = 1, vq = 0;                // K / V tiles issued (Q and K_0 above)
+            // stage j & 1 held tile j - 2: its S (K) or PV (V) must be done
+            auto load_k = [&](int j) -> bool {
                 const int st = j & 1, r = row_base + j * KT4;
-                const uint32_t eph = (uint32_t)((j >> 1) - 1) & 1;
-                if (j >= 2 && !(ok = wait_bar(&ctl->k_empty[st], eph, abort_flag))) break;
+                if (j >= 2 && !wait_bar(&ctl->k_empty[st], (uint32_t)((j >> 1) - 1) & 1, abort_flag)) return false;
                 sm100::mbar_arrive_expect_tx(&ctl->k_full[st], KV4_BYTES);
                 sm100::tma_load_2d(sK + st * KV4_BYTES, &tK, &ctl->k_full[st], 0, r);
                 sm100::tma_load_2d(sK + st * KV4_BYTES + KV4_HALF, &tK, &ctl->k_full[st], 64, r);
                 kq++;
-                if (j >= 2 && !(ok = wait_bar(&ctl->v_empty[st], eph, abort_flag))) break;
+                return true;
+            };
+            auto load_v = [&](int j) -> bool {
+                const int st = j & 1, r = row_base + j * KT4;
+                if (j >= 2 && !wait_bar(&ctl->v_empty[st], (uint32_t)((j >> 1) - 1) & 1, abort_flag)) return false;
                 sm100::mbar_arrive_expect_tx(&ctl->v_full[st], KV4_BYTES);
                 sm100::tma_load_2d(sV + st * KV4_BYTES, &tV, &ctl->v_full[st], 0, r);
                 sm100::tma_load_2d(sV + st * KV4_BYTES + KV4_HALF, &tV, &ctl->v_full[st], 64, r);
                 vq++;
+                return true;
+            };
+            for (int j = 0; j < nkt && ok; j++) {
+                if (j + 1 < nkt && !(ok = load_k(j + 1))) break;
+                ok = load_v(j);
             }
             if (!ok) {
                 // drain this thread's own TMA loads (bounded) before shared memory is released
@@ -888,9 +991,9 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
         }
     } else {
         // ---- softmax + epilogue: thread = query row q0 + r; TMEM lane quadrant = warp
-        const int r = warp * 32 + lane;
         const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
         const float sl = p.scale_log2;
+        const bool live = q0 + warp * 32 < S;  // warp-uniform: any of this warp's rows is a query
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         // tcgen05.ld / st are warp-collective: control flow stays warp-uniform
@@ -898,52 +1001,65 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
             const int st = j & 1;
             ok = __all_sync(0xffffffffu, wait_bar(&ctl->s_full[st], (uint32_t)(j >> 1) & 1, abort_flag));
             if (!ok) break;
-            sm100::tc_fence_after();
-            const int kvalid = S - j * KT4;
-            const bool full = kvalid >= KT4;           // CTA-uniform
-            float v[64];
-            sm100::tmem_ld64(tmem + lane_off + st * 64, v);
-            const float mx = max64(v, full ? 64 : kvalid) * sl;
-            if (j == 0) {
-                m = mx;
-            } else {
-                const bool grow = mx > m + T_RESCALE;
-                if (__any_sync(0xffffffffu, grow)) {
-                    // the previous PV accumulates into O: wait for it first
-                    ok = __all_sync(0xffffffffu, wait_bar(&ctl->pv_done, (uint32_t)(j - 1) & 1, abort_flag));
-                    if (!ok) break;
-                    sm100::tc_fence_after();
-                    const float mn = grow ? mx : m;
-                    const float corr = exp2f(m - mn);
-                    #pragma unroll 1
-                    for (int c = 0; c < 4; c++) {
-                        float o[32];
-                        sm100::tmem_ld32(tO + lane_off + c * 32, o);
-                        #pragma unroll
-                        for (int u = 0; u < 32; u++) o[u] *= corr;
-                        tmem_st32(tO + lane_off + c * 32, o);
+            if (live) {
+                sm100::tc_fence_after();
+                const int kvalid = S - j * KT4;
+                const bool full = kvalid >= KT4;           // CTA-uniform
+                float v[64];
+                sm100::tmem_ld64(tmem + lane_off + st * 64, v);
+                const float mx = (full ? max64_full(v) : max64_t<true>(v, kvalid)) * sl;
+                if (j == 0) {
+                    m = mx;
+                } else {
+                    const bool grow = mx > m + T_RESCALE;
+                    if (__any_sync(0xffffffffu, grow)) {
+                        // the previous PV accumulates into O: wait for it first
+                        ok = __all_sync(0xffffffffu, wait_bar(&ctl->pv_done, (uint32_t)(j - 1) & 1, abort_flag));
+                        if (!ok) break;
+                        sm100::tc_fence_after();
+                        const float mn = grow ? mx : m;
+                        const float corr = exp2f(m - mn);
+                        #pragma unroll 1
+                        for (int c = 0; c < 4; c++) {
+                            float o[32];
+                            sm100::tmem_ld32(tO + lane_off + c * 32, o);
+                            #pragma unroll
+                            for (int u = 0; u < 32; u++) o[u] *= corr;
+                            tmem_st32(tO + lane_off + c * 32, o);
+                        }
+                        l *= corr;
+                        m = mn;
                     }
-                    l *= corr;
-                    m = mn;
                 }
+                // P_j as packed bf16 pairs over the slot's columns [0, 32)
+                const uint64_t sl2 = f2pack(sl, sl), nm2 = f2pack(-m, -m);
+                uint32_t pk[32];
+                uint64_t ls[4];
+                #pragma unroll
+                for (int i = 0; i < 4; i++) ls[i] = f2pack(0.f, 0.f);
+                #pragma unroll
+                for (int u = 0; u < 32; u++) {
+                    const uint64_t x2 = ffma2(f2pack(v[2 * u], v[2 * u + 1]), sl2, nm2);
+                    float a, b;
+                    if ((u & 3) < NP) {
+                        ex2_poly2(x2, a, b);
+                    } else {
+                        float xa, xb;
+                        f2unpack(x2, xa, xb);
+                        a = ex2_approx(xa);
+                        b = ex2_approx(xb);
+                    }
+                    if (!full) { a = (2 * u < kvalid) ? a : 0.f; b = (2 * u + 1 < kvalid) ? b : 0.f; }
+                    ls[u & 3] = fadd2(ls[u & 3], f2pack(a, b));
+                    pk[u] = pack_bf16x2_rn(a, b);
+                }
+                float s8[8];
+                #pragma unroll
+                for (int i = 0; i < 4; i++) f2unpack(ls[i], s8[2 * i], s8[2 * i + 1]);
+                l += sum8(s8);
+                tmem_st32u(tmem + lane_off + st * 64, pk);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             }
-            // P_j as packed bf16 pairs over the slot's columns [0, 32)
-            const float nm = -m;
-            uint32_t pk[32];
-            float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            #pragma unroll
-            for (int u = 0; u < 32; u++) {
-                const float xa = fmaf(v[2 * u], sl, nm), xb = fmaf(v[2 * u + 1], sl, nm);
-                float a, b;
-                if (POLY && (u & 3) == 3) { a = ex2_poly(xa); b = ex2_poly(xb); }
-                else { a = ex2_approx(xa); b = ex2_approx(xb); }
-                if (!full) { a = (2 * u < kvalid) ? a : 0.f; b = (2 * u + 1 < kvalid) ? b : 0.f; }
-                ls[u & 7] += a + b;
-                pk[u] = pack_bf16x2_t<ALU>(a, b);
-            }
-            l += sum8(ls);
-            tmem_st32u(tmem + lane_off + st * 64, pk);
-            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             sm100::tc_fence_before();
             __syncwarp();
             if (lane == 0) sm100::mbar_arrive(&ctl->p_ready[st]);
@@ -951,32 +1067,38 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
         // O is final once every PV is done (a barrier of its own: pv_done may
         // still be two phases behind here, which its parity cannot tell apart)
         if (ok) ok = __all_sync(0xffffffffu, wait_bar(&ctl->o_full, 0, abort_flag));
-        if (ok) {
+        if (ok && live) {
             sm100::tc_fence_after();
-            const int q = q0 + r;
+            // every MMA and TMA load of the CTA is complete: the Q/K/V tiles
+            // are free to stage this warp's 32 rows
             const float inv = 1.f / l;
-            const bool is_vid = q < f, is_txt = (q >= f) && (q < S);
-            float* tdst = p.toutw + ((size_t)wi * p.g.TXT + (is_txt ? q - f : 0)) * 2560 + h * D;
-            const size_t tok = is_vid ? (size_t)p.g.vidx[p.g.cumf[wi] + q] : 0;
+            float* stage = reinterpret_cast<float*>(smem) + (size_t)warp * 32 * STG_LD;
+            float* mine = stage + lane * STG_LD;
             #pragma unroll 1
             for (int c = 0; c < 2; c++) {
                 float o[64];
                 sm100::tmem_ld64(tO + lane_off + c * 64, o);
                 #pragma unroll
-                for (int u = 0; u < 64; u++) o[u] *= inv;
-                if (is_vid) {
-                    if (p.att_bf16) {
-                        bf16* dst = (bf16*)p.att + tok * p.ld_att + h * D + c * 64;
-                        #pragma unroll
-                        for (int u = 0; u < 64; u += 4) store4(dst + u, o + u);
-                    } else {
-                        float* dst = (float*)p.att + tok * p.ld_att + h * D + c * 64;
-                        #pragma unroll
-                        for (int u = 0; u < 64; u += 4) store4(dst + u, o + u);
-                    }
-                } else if (is_txt) {
-                    #pragma unroll
-                    for (int u = 0; u < 64; u += 4) store4(tdst + c * 64 + u, o + u);
+                for (int u = 0; u < 64; u += 4)
+                    *reinterpret_cast<float4*>(mine + c * 64 + u) =
+                        make_float4(o[u] * inv, o[u + 1] * inv, o[u + 2] * inv, o[u + 3] * inv);
+            }
+            const int qw = q0 + warp * 32;
+            const int nrows = min(32, S - qw);
+            __syncwarp();
+            #pragma unroll 4
+            for (int rr = 0; rr < nrows; rr++) {
+                const int q = qw + rr;
+                const int tok = __shfl_sync(0xffffffffu, my_tok, rr);
+                const float4 x = *reinterpret_cast<const float4*>(stage + rr * STG_LD + lane * 4);
+                const float xv[4] = {x.x, x.y, x.z, x.w};
+                if (q < f) {
+                    if (p.att_bf16)
+                        store4((bf16*)p.att + (size_t)tok * p.ld_att + h * D + lane * 4, xv);
+                    else
+                        store4((float*)p.att + (size_t)tok * p.ld_att + h * D + lane * 4, xv);
+                } else {
+                    store4(p.toutw + ((size_t)wi * p.g.TXT + (q - f)) * 2560 + h * D + lane * 4, xv);
                 }
             }
         }
@@ -1012,11 +1134,10 @@ int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, const AwaDev& 
         if (!make_tmap_bf16(&tk4, Kp, rows, D, D, KT4, 64) || !make_tmap_bf16(&tv4, Vp, rows, D, D, KT4, 64))
             return -1;
         dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
-        const int poly = awa_tc_poly_exp(), alu = awa_tc_alu_pack();
-        if (poly && alu) k_awa_attn_tc4<true, true><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
-        else if (poly) k_awa_attn_tc4<true, false><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
-        else if (alu) k_awa_attn_tc4<false, true><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
-        else k_awa_attn_tc4<false, false><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
+        const int np = awa_tc_poly_exp();
+        if (np == 2) k_awa_attn_tc4<2><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
+        else if (np == 1) k_awa_attn_tc4<1><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
+        else k_awa_attn_tc4<0><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
     } else if (awa_tc_kernel_version() == 1) {
         dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
         if (awa_tc_poly_exp())
@@ -1045,8 +1166,8 @@ int awa_tc_init_device() {
         return (int)e;
     if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES))
         return (int)e;
-    const void* v4[4] = {(const void*)k_awa_attn_tc4<false, false>, (const void*)k_awa_attn_tc4<false, true>,
-                         (const void*)k_awa_attn_tc4<true, false>, (const void*)k_awa_attn_tc4<true, true>};
+    const void* v4[3] = {(const void*)k_awa_attn_tc4<0>, (const void*)k_awa_attn_tc4<1>,
+                         (const void*)k_awa_attn_tc4<2>};
     for (const void* k : v4)
         if (cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, T4_SMEM)) return (int)e;
     if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc2<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, T2_SMEM))
@@ -1054,21 +1175,11 @@ int awa_tc_init_device() {
     return (int)cudaFuncSetAttribute(k_awa_attn_tc2<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, T2_SMEM);
 }
 
-// S2B_ATTN_POLY=1: a quarter of the softmax exponentials on the FMA pipe
-// (ex2_poly).  Off by default: measured slower at 1080p (the FMA pipe work
-// costs more than the conversion unit it frees).
-// S2B_ATTN_PACK=alu: bf16 packing of P by integer rounding instead of the
-// conversion instruction (64-key kernel).  Per 1080p forward, alternating in
-// one process: conversion 2.6-3.0 ms, integer 3.0-3.1 ms; with a quarter of
-// the exponentials as polynomials (S2B_ATTN_POLY=1) 2.9-3.1 / 3.1-3.2 ms.
-int awa_tc_alu_pack() {
-    const char* e = std::getenv("S2B_ATTN_PACK");
-    return (e && e[0] == 'a') ? 1 : 0;
-}
-
+// S2B_ATTN_POLY=n (0, 1, 2): n of every 4 softmax exponential pairs on the
+// FMA pipe (ex2_poly2 in the 64-key kernel; ex2_poly in the others).
 int awa_tc_poly_exp() {
     const char* e = std::getenv("S2B_ATTN_POLY");
-    return (e && e[0] == '1') ? 1 : 0;
+    return (e && e[0] == '2') ? 2 : (e && e[0] == '1') ? 1 : 0;
 }
 
 // 3 = 64-key tiles, double-buffered K/V, P in TMEM (default);

@@ -354,6 +354,12 @@ __device__ __forceinline__ bool epilogue_resid_tma(const TcParams& p, const CUte
     const int row = r0 + lane;
     const float* gate = (row < e.gate_split) ? e.gate0 : e.gate1;
     const int nch = min(bn / 32, (p.N - n0) / 32);
+    // the box ring runs one chunk ahead; pull the next tile's boxes into L2
+    // now, a whole mainloop before they are loaded (groups share N)
+    if (lane == 0 && next_n0 >= 0) {
+        const int nn = min(bn / 32, (p.N - next_n0) / 32);
+        for (int c = 0; c < nn; c++) sm100::tma_prefetch_l2_2d(tR_next, next_n0 + 32 * c, next_r0);
+    }
     for (int c = 0; c < nch; c++) {
         const int col = n0 + 32 * c;
         float v[32];
@@ -694,6 +700,8 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
         if (rt && lane == 0 && pair < num_tiles) {
             const TileRef t = tile_ref(p0, p1, tiles0, pair);
             resid_load(&maps.r[t.grp], rp, t.nb * BN, t.mb * BM2 + rbase);
+            const int nn = min(BN / 32, (p0.N - t.nb * BN) / 32);
+            for (int c = 1; c < nn; c++) sm100::tma_prefetch_l2_2d(&maps.r[t.grp], t.nb * BN + 32 * c, t.mb * BM2 + rbase);
         }
         int it = 0;
         for (int tile = pair; tile < num_tiles; tile += npairs, it++) {
