@@ -373,6 +373,43 @@ def run_kernel_case(case: str):
         for _ in range(2):
             c.forward_latent(vid, Lv, txt, TXT, TIMESTEP, 0, 32, True, True)
         print("launches per forward", c.last_launches())
+    elif case == "gemm_cublas":
+        # the forward's Linear shapes (and a square reference): this library's
+        # tcgen05 GEMM (s2b_linear_bf16_dev, bf16 out) beside cuBLAS
+        # (torch.matmul, bf16) on the same device buffers, CUDA events, best of 3
+        import torch
+        dev = torch.device("cuda", 0)
+        st = torch.cuda.current_stream(dev)
+        shapes = [("qkv", 5498, 7680, 2560), ("out", 5498, 2560, 2560), ("mlp_in", 5498, 13824, 2560),
+                  ("mlp_out", 5498, 2560, 6912), ("square", 8192, 8192, 8192)]
+        g = torch.Generator(device=dev).manual_seed(7)
+        for name, M, N, K in shapes:
+            x = (torch.randn(M, K, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+            w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            ours = lambda: c.linear_bf16_dev(x.data_ptr(), M, K, w.data_ptr(), N, None, y.data_ptr(), st.cuda_stream)
+            ref = lambda: torch.matmul(x, w.t())
+            res = {}
+            for tag, fn in (("ours", ours), ("cublas", ref)):
+                best = None
+                for _ in range(3):
+                    for _ in range(3):
+                        fn()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                    for _ in range(20):
+                        fn()
+                    e1.record(st)
+                    torch.cuda.synchronize(dev)
+                    ms = e0.elapsed_time(e1) / 20
+                    best = ms if best is None else min(best, ms)
+                res[tag] = best
+            ours()
+            d = (y.float() - ref().float()).abs().max().item()
+            tf = lambda ms: 2.0 * M * N * K / (ms * 1e-3) / 1e12
+            print(f"{name:8s} M={M:5d} N={N:5d} K={K:5d}  ours {res['ours'] * 1e3:7.1f} us {tf(res['ours']):6.0f} TFLOP/s"
+                  f"   cuBLAS {res['cublas'] * 1e3:7.1f} us {tf(res['cublas']):6.0f} TFLOP/s   ratio "
+                  f"{res['cublas'] / res['ours']:.3f}   max|d| {d:.3g}")
     elif case == "attn_1080p":
         T, H, W = GRID
         Lv = T * H * W
@@ -391,7 +428,8 @@ def run_kernel_case(case: str):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--kernel-case", choices=sorted(list(KERNEL_CASES) + ["attn_1080p", "layer_1080p", "forward_1080p"]),
+    ap.add_argument("--kernel-case", choices=sorted(list(KERNEL_CASES) + ["attn_1080p", "layer_1080p", "forward_1080p",
+                                                                           "gemm_cublas"]),
                     help="run one small single-kernel workload (for ncu captures) instead of the bench")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)

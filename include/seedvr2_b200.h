@@ -218,6 +218,15 @@ int s2b_forward_profile(s2b_ctx* ctx, const float* vid_patch, int Lv, const floa
  * contexts run the fp32 kernel.  x (M,K), W (N,K), bias (N) or NULL, y (M,N),
  * fp32 host buffers. */
 int s2b_linear(s2b_ctx* ctx, const float* x, int M, int K, const float* W, int N, const float* bias, float* y);
+/* The same Linear on device buffers, the form the engine's GEMMs take inside
+ * the forward (DitVk::lin, src/dit_vk.cpp:270-293, with x and W already
+ * resident): x (M,K) and W (N,K) bf16 row-major, bias (N) fp32 or NULL,
+ * y (M,N) bf16, fp32 accumulation on the tcgen05 tensor cores, enqueued on
+ * `stream` (a cudaStream_t; NULL = legacy default stream) without
+ * synchronising.  K % 64 == 0, N % 32 == 0, 16-byte aligned buffers; else
+ * S2B_ERR_ARG.  Works in contexts of either precision. */
+int s2b_linear_bf16_dev(s2b_ctx* ctx, const void* d_x, int M, int K, const void* d_w, int N, const float* d_bias,
+                        void* d_y, void* stream);
 
 /* ---- synthetic data (no checkpoint ships with this build) ------------- */
 /* Writes the m5 directory layout for layers [layer_lo, layer_hi) with

@@ -277,6 +277,12 @@ int s2b_linear(s2b_ctx* ctx, const float* x, int M, int K, const float* W, int N
     return ctx->dit.linear(x, M, K, W, N, bias, y);
 }
 
+int s2b_linear_bf16_dev(s2b_ctx* ctx, const void* d_x, int M, int K, const void* d_w, int N, const float* d_bias,
+                        void* d_y, void* stream) {
+    if (!ctx) return S2B_ERR_ARG;
+    return ctx->dit.linear_bf16_dev(d_x, M, K, d_w, N, d_bias, d_y, (cudaStream_t)stream);
+}
+
 int s2b_synth_write_m5(const char* dir, uint64_t seed, int lo, int hi) {
     if (!dir) return S2B_ERR_ARG;
     std::string err;

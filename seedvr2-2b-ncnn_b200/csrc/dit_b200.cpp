@@ -943,6 +943,20 @@ int DitB200::linear(const float* x, int M, int K, const float* W, int N, const f
     return OK;
 }
 
+int DitB200::linear_bf16_dev(const void* x, int M, int K, const void* W, int N, const float* bias, void* y,
+                             cudaStream_t s) {
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    if (!x || !W || !y || M <= 0 || K <= 0 || N <= 0) return fail(ERR_ARG, "bad linear arguments");
+    if (K % 64 || N % 32 || ((uintptr_t)x & 15) || ((uintptr_t)W & 15) || ((uintptr_t)y & 15) || ((uintptr_t)bias & 15))
+        return fail(ERR_ARG, "the device bf16 Linear needs K % 64 == 0, N % 32 == 0 and 16-byte aligned buffers");
+    if (!gemm_tc_supported(M, N, K, K, K)) return fail(ERR_UNSUPPORTED, "shape not supported by the tcgen05 GEMM");
+    cudaSetDevice(dev_);
+    GemmEpi e;
+    e.mode = EPI_STORE; e.bias = bias; e.out = y; e.ldo = N; e.out_t = ACT_BF16;
+    if (gemm_tc(x, K, W, K, M, N, K, e, s, &launches_)) return fail(ERR_UNSUPPORTED, "tcgen05 GEMM launch rejected");
+    return cuda_check(cudaGetLastError(), "linear_bf16_dev");
+}
+
 int DitB200::ada_compose(const float* emb_host, float* out_host) {
     if (!weights_) return fail(ERR_STATE, "weights not loaded");
     cudaSetDevice(dev_);

@@ -120,6 +120,8 @@ public:
                         double* flops, double* bytes, int* count, bool sharded = false);
     // One Linear on the context's GEMM engine (host buffers).
     int linear(const float* x, int M, int K, const float* W, int N, const float* bias, float* y);
+    // y = x W^T (+ bias) on device bf16 buffers, bf16 out, on stream s (any precision context)
+    int linear_bf16_dev(const void* x, int M, int K, const void* W, int N, const float* bias, void* y, cudaStream_t s);
     int ada_compose(const float* emb_host, float* out_host);
     // AwaVk::forward (host) / AwaLayer::forward (device, stored geometry)
     int awa_forward(const float* vqkv, const float* tqkv, const WinGeom& win, const float* nqv, const float* nkv,

@@ -96,6 +96,7 @@ def lib() -> ctypes.CDLL:
         "s2b_linear": [vp, _F32P, ip, ip, _F32P, ip, _F32P, _F32P],
         "s2b_forward_profile": [vp, _F32P, ip, _F32P, ip, ctypes.c_float, ctypes.POINTER(ctypes.c_double),
                                 ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), _I32P],
+        "s2b_linear_bf16_dev": [vp, vp, ip, ip, vp, ip, vp, vp, vp],
         "s2b_synth_write_m5": [ctypes.c_char_p, u64, ip, ip],
         "s2b_synth_vid_grid": [_F32P, ip, ip, ip, u64],
         "s2b_synth_txt": [_F32P, ip, u64],
@@ -386,6 +387,10 @@ class DitB200:
 
     def forward_dev(self, d_vid: int, Lv: int, d_txt: int, TXT: int, timestep: float, d_sr: int, stream: int):
         self._c(lib().s2b_forward_dev(self._ctx, d_vid, Lv, d_txt, TXT, timestep, d_sr, stream))
+
+    def linear_bf16_dev(self, d_x: int, M: int, K: int, d_w: int, N: int, d_bias, d_y: int, stream: int):
+        """y = x W^T (+ bias) on device bf16 buffers (pointers as ints), enqueued on `stream`."""
+        self._c(lib().s2b_linear_bf16_dev(self._ctx, d_x, M, K, d_w, N, d_bias, d_y, stream))
 
     def forward_grid(self, vid_grid, txt, TXT, timestep=1000.0):
         T, H, W, _ = vid_grid.shape

@@ -52,3 +52,30 @@ def test_linear_vs_torch_fp32(ctx, M, N, K):
         ref = (xt @ wt.T + torch.from_numpy(b).cuda()).cpu().numpy()
     rel = np.abs(y - ref).max() / np.abs(ref).max()
     assert rel <= (1e-3 if ctx.precision == s2b.PREC_BF16 else 1e-5), rel
+
+
+@pytest.mark.parametrize("M,N,K", [(5498, 2560, 2560), (300, 13824, 2560), (58, 256, 128), (129, 288, 64)])
+def test_linear_bf16_dev_vs_torch_fp32(M, N, K):
+    """s2b_linear_bf16_dev on device bf16 buffers, on the caller's stream:
+    against torch fp32 on the same bf16 operands, bf16 output rounding
+    (max|d|/max|ref| <= 8e-3, two bf16 ulps at the top of the range)."""
+    import torch
+    c = s2b.DitB200(0, s2b.PREC_BF16)
+    try:
+        dev = torch.device("cuda", 0)
+        x = torch.from_numpy(s2b.synth_normal((M, K), 4, f"dx{M}{K}")).to(dev).bfloat16()
+        w = torch.from_numpy(s2b.synth_normal((N, K), 5, f"dw{N}{K}", 0.0, 0.02)).to(dev).bfloat16()
+        b = torch.from_numpy(s2b.synth_normal((N,), 6, f"db{N}", 0.0, 0.02)).to(dev)
+        y = torch.full((M, N), float("nan"), device=dev, dtype=torch.bfloat16)
+        st = torch.cuda.current_stream(dev)
+        c.linear_bf16_dev(x.data_ptr(), M, K, w.data_ptr(), N, b.data_ptr(), y.data_ptr(), st.cuda_stream)
+        torch.cuda.synchronize(dev)
+        torch.backends.cuda.matmul.allow_tf32 = False
+        ref = x.float() @ w.float().T + b
+        rel = ((y.float() - ref).abs().max() / ref.abs().max()).item()
+        assert rel <= 8e-3, rel
+        # shapes the kernel cannot take are refused with an argument error
+        with pytest.raises(s2b.S2BError):
+            c.linear_bf16_dev(x.data_ptr(), M, K - 1, w.data_ptr(), N, None, y.data_ptr(), st.cuda_stream)
+    finally:
+        c.close()
