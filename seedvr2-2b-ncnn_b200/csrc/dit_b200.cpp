@@ -51,6 +51,9 @@ int DitB200::create(int device, int precision) {
     if (prop.major != 10) return fail(ERR_UNSUPPORTED, std::string("sm_100a kernels need a B200-class GPU, found ") + prop.name);
     prec_ = precision;
     act_ = (precision == PREC_BF16) ? ACT_BF16 : ACT_F32;
+    // fp32 attention on the tensor cores (split3 operands) unless S2B_FP32_ATTN=simt
+    const char* aenv = std::getenv("S2B_FP32_ATTN");
+    attn_split3_ = act_ == ACT_F32 && !(aenv && aenv[0] == 's');
     if (int rc = cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate")) return rc;
     if (kernels_init_device() != 0) return fail(ERR_CUDA, "kernel attribute setup failed");
     return OK;
@@ -435,9 +438,10 @@ int DitB200::ensure_acts(int Lv, int TXT) {
     if ((rc = cuda_check(Xn_.ensure(M * DIM * ab), "cudaMalloc(Xn)"))) return rc;
     if ((rc = cuda_check(QKV_.ensure(M * QKV * ab), "cudaMalloc(QKV)"))) return rc;
     if ((rc = cuda_check(ATT_.ensure(M * DIM * ab), "cudaMalloc(ATT)"))) return rc;
-    if ((rc = cuda_check(Qp_.ensure(std::max<size_t>(sumS, 1) * DIM * ab), "cudaMalloc(Qp)"))) return rc;
-    if ((rc = cuda_check(Kp_.ensure(std::max<size_t>(sumS, 1) * DIM * ab), "cudaMalloc(Kp)"))) return rc;
-    if ((rc = cuda_check(Vp_.ensure(std::max<size_t>(sumS, 1) * DIM * ab), "cudaMalloc(Vp)"))) return rc;
+    const size_t pb = attn_elem_bytes();
+    if ((rc = cuda_check(Qp_.ensure(std::max<size_t>(sumS, 1) * DIM * pb), "cudaMalloc(Qp)"))) return rc;
+    if ((rc = cuda_check(Kp_.ensure(std::max<size_t>(sumS, 1) * DIM * pb), "cudaMalloc(Kp)"))) return rc;
+    if ((rc = cuda_check(Vp_.ensure(std::max<size_t>(sumS, 1) * DIM * pb), "cudaMalloc(Vp)"))) return rc;
     if ((rc = cuda_check(TOUTW_.ensure(std::max<size_t>(nwinTXT, 1) * DIM * 4), "cudaMalloc(TOUTW)"))) return rc;
     // [h | g] fp32 staging of the SIMT SwiGLU path (the tcgen05 path fuses it)
     const bool need_hg = act_ == ACT_F32 || !gemm_tc_supported((int)M, 2 * MLP_DIM, DIM, DIM, DIM);
@@ -622,9 +626,13 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
         } else {
             e.out = qkv; gemm(xn, DIM, BV.qkv, M, e, s);
         }
-        pbeg(KK_PACK, 0, (double)G.view.sumS * QKV * ab * 2, s);
-        awa_pack(qkv, qkv + (size_t)Lv * QKV * ab, act_, QKV, G.view, normw(i, 0, 0), normw(i, 0, 1),
-                 normw(i, 1, 0), normw(i, 1, 1), NORM_EPS, B.Qp, B.Kp, B.Vp, act_, s);
+        pbeg(KK_PACK, 0, (double)G.view.sumS * QKV * (ab + attn_elem_bytes()), s);
+        if (attn_split3_)
+            awa_pack_split3(qkv, qkv + (size_t)Lv * QKV * ab, act_, QKV, G.view, normw(i, 0, 0), normw(i, 0, 1),
+                            normw(i, 1, 0), normw(i, 1, 1), NORM_EPS, B.Qp, B.Kp, B.Vp, s);
+        else
+            awa_pack(qkv, qkv + (size_t)Lv * QKV * ab, act_, QKV, G.view, normw(i, 0, 0), normw(i, 0, 1),
+                     normw(i, 1, 0), normw(i, 1, 1), NORM_EPS, B.Qp, B.Kp, B.Vp, act_, s);
         launches_++;
         pend(s);
     }
@@ -634,9 +642,15 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
         const double S = G.tab.cums[w + 1] - G.tab.cums[w];
         attn_flops += 4.0 * S * S * HEAD_D * HEADS;
     }
-    pbeg(KK_ATTN, attn_flops, (double)G.view.sumS * QKV * ab + (double)Lv * DIM * ab + (double)G.view.nwin * TXT * DIM * 4, s);
-    awa_attend(B.Qp, B.Kp, B.Vp, act_, G.view, 1.0f / sqrtf((float)HEAD_D), att, DIM, act_, B.TOUTW, s,
-               &launches_);
+    pbeg(KK_ATTN, attn_flops, (double)G.view.sumS * QKV * attn_elem_bytes() + (double)Lv * DIM * ab + (double)G.view.nwin * TXT * DIM * 4, s);
+    if (attn_split3_) {
+        if (awa_attend_split3(B.Qp, B.Kp, B.Vp, G.view, 1.0f / sqrtf((float)HEAD_D), att, DIM, act_, B.TOUTW, s))
+            return fail(ERR_CUDA, "fp32 tensor-core attention: tensor maps could not be encoded");
+        launches_++;
+    } else {
+        awa_attend(B.Qp, B.Kp, B.Vp, act_, G.view, 1.0f / sqrtf((float)HEAD_D), att, DIM, act_, B.TOUTW, s,
+                   &launches_);
+    }
     pend(s);
     pbeg(KK_OTHER, 0, (double)G.view.nwin * TXT * DIM * 4 + (double)TXT * DIM * ab, s);
     if (B.txt_partial) {
@@ -980,18 +994,25 @@ int DitB200::awa_run(GeomDev& G, const float* vqkv, const float* tqkv, const flo
     if (!G.ready) return fail(ERR_STATE, "AWA geometry not set");
     if (Lv != G.view.Lv || TXT != G.view.TXT || TXT <= 0) return fail(ERR_ARG, "Lv/TXT do not match the geometry");
     if (G.view.nwin <= 0) return fail(ERR_ARG, "no windows");
-    const size_t ab = act_bytes(act_), sumS = (size_t)G.view.sumS;
+    const size_t pb = attn_elem_bytes(), sumS = (size_t)G.view.sumS;
     DevBuf q, k, v, tw;
     int rc;
-    if ((rc = cuda_check(q.ensure(sumS * DIM * ab), "cudaMalloc"))) return rc;
-    if ((rc = cuda_check(k.ensure(sumS * DIM * ab), "cudaMalloc"))) return rc;
-    if ((rc = cuda_check(v.ensure(sumS * DIM * ab), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(q.ensure(sumS * DIM * pb), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(k.ensure(sumS * DIM * pb), "cudaMalloc"))) return rc;
+    if ((rc = cuda_check(v.ensure(sumS * DIM * pb), "cudaMalloc"))) return rc;
     if ((rc = cuda_check(tw.ensure((size_t)G.view.nwin * TXT * DIM * 4), "cudaMalloc"))) return rc;
     // tokens outside every window read 0 (reference awa_init.comp)
     if (!G.tab.covers_all) cudaMemsetAsync(vid_out, 0, (size_t)Lv * DIM * 4, user);
-    awa_pack(vqkv, tqkv, ACT_F32, QKV, G.view, nqv, nkv, nqt, nkt, eps, q.p, k.p, v.p, act_, user);
-    awa_attend(q.p, k.p, v.p, act_, G.view, 1.0f / sqrtf((float)HEAD_D), vid_out, DIM, ACT_F32, tw.as<float>(), user,
-               nullptr);
+    if (attn_split3_) {
+        awa_pack_split3(vqkv, tqkv, ACT_F32, QKV, G.view, nqv, nkv, nqt, nkt, eps, q.p, k.p, v.p, user);
+        if (awa_attend_split3(q.p, k.p, v.p, G.view, 1.0f / sqrtf((float)HEAD_D), vid_out, DIM, ACT_F32,
+                              tw.as<float>(), user))
+            return fail(ERR_CUDA, "fp32 tensor-core attention: tensor maps could not be encoded");
+    } else {
+        awa_pack(vqkv, tqkv, ACT_F32, QKV, G.view, nqv, nkv, nqt, nkt, eps, q.p, k.p, v.p, act_, user);
+        awa_attend(q.p, k.p, v.p, act_, G.view, 1.0f / sqrtf((float)HEAD_D), vid_out, DIM, ACT_F32, tw.as<float>(),
+                   user, nullptr);
+    }
     awa_coalesce(tw.as<float>(), G.view.nwin, TXT, txt_out, DIM, ACT_F32, user);
     if ((rc = cuda_check(cudaGetLastError(), "awa launch"))) return rc;
     // the scratch buffers above must outlive the enqueued kernels

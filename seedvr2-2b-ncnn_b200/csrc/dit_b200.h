@@ -209,6 +209,11 @@ private:
     DevBuf A2_;         // fp32 contexts: [M][2K] split activations of the tensor-core fp32 GEMM
     bool tf32x3_ = false;
     int prepare_tf32x3();
+    // fp32 contexts: attention on the tensor cores from split3 operands
+    // (awa_pack_split3 / awa_attend_split3) unless S2B_FP32_ATTN=simt
+    bool attn_split3_ = false;
+    // bytes per element of the packed Q/K/V buffers (three bf16 parts under split3)
+    size_t attn_elem_bytes() const { return attn_split3_ ? 6 : act_bytes(act_); }
     size_t qkv_pack_rows_ = 0;
 
     // captured full forward

@@ -198,9 +198,9 @@ int DitB200::shard_prepare(int Lv, int TXT) {
     if ((rc = alloc(S.QKV, Mmax * QKV * ab, "cudaMalloc(shard QKV)"))) return rc;
     if ((rc = alloc(S.ATT, Mmax * DIM * ab, "cudaMalloc(shard ATT)"))) return rc;
     if ((rc = alloc(S.Hs, Mmax * MLP_DIM * ab, "cudaMalloc(shard Hs)"))) return rc;
-    if ((rc = alloc(S.Qp, sumS * DIM * ab, "cudaMalloc(shard Qp)"))) return rc;
-    if ((rc = alloc(S.Kp, sumS * DIM * ab, "cudaMalloc(shard Kp)"))) return rc;
-    if ((rc = alloc(S.Vp, sumS * DIM * ab, "cudaMalloc(shard Vp)"))) return rc;
+    if ((rc = alloc(S.Qp, sumS * DIM * attn_elem_bytes(), "cudaMalloc(shard Qp)"))) return rc;
+    if ((rc = alloc(S.Kp, sumS * DIM * attn_elem_bytes(), "cudaMalloc(shard Kp)"))) return rc;
+    if ((rc = alloc(S.Vp, sumS * DIM * attn_elem_bytes(), "cudaMalloc(shard Vp)"))) return rc;
     if ((rc = alloc(S.TOUTW, nwT * DIM * 4, "cudaMalloc(shard TOUTW)"))) return rc;
     if ((rc = alloc(S.TXTSUM, (size_t)TXT * DIM * 4, "cudaMalloc(shard TXTSUM)"))) return rc;
     if ((rc = alloc(S.VIDIN, (size_t)Lv * PATCH_IN * 4, "cudaMalloc(shard VIDIN)"))) return rc;

@@ -21,7 +21,36 @@
 namespace s2b {
 namespace {
 
-template <typename TI, typename TP>
+// fp32 x as three bf16 parts with x == hi + mid + lo to fp32 precision:
+// hi = rn(x), mid = rn(x - hi), lo = rn(x - hi - mid).  Both differences are
+// exact in fp32 (each drops the leading 8 significant bits), so the parts
+// carry x's 24-bit significand.
+__device__ __forceinline__ void split3_bf16(float x, bf16& hi, bf16& mid, bf16& lo) {
+    hi = __float2bfloat16_rn(x);
+    const float r = __fsub_rn(x, __bfloat162float(hi));
+    mid = __float2bfloat16_rn(r);
+    lo = __float2bfloat16_rn(__fsub_rn(r, __bfloat162float(mid)));
+}
+
+// Four consecutive values as their three bf16 parts, part k at p + k * part.
+__device__ __forceinline__ void store4_split3(bf16* p, size_t part, const float v[4]) {
+    uint32_t w[3][2];
+    #pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+        bf16 a[3], b[3];
+        split3_bf16(v[j], a[0], a[1], a[2]);
+        split3_bf16(v[j + 1], b[0], b[1], b[2]);
+        #pragma unroll
+        for (int k = 0; k < 3; k++)
+            w[k][j >> 1] = (uint32_t)__bfloat16_as_ushort(a[k]) | ((uint32_t)__bfloat16_as_ushort(b[k]) << 16);
+    }
+    #pragma unroll
+    for (int k = 0; k < 3; k++) *reinterpret_cast<uint2*>(p + k * part) = make_uint2(w[k][0], w[k][1]);
+}
+
+// SPLIT3: TP is bf16 and each of Qp/Kp/Vp holds three parts of
+// [HEADS][sumS][128] (hi, mid, lo), 20 * sumS * 128 elements apart.
+template <typename TI, typename TP, bool SPLIT3 = false>
 __global__ void __launch_bounds__(640)
 k_awa_pack(const TI* __restrict__ vqkv, const TI* __restrict__ tqkv, int ldq, AwaDev g,
            const float* __restrict__ nqv, const float* __restrict__ nkv, const float* __restrict__ nqt,
@@ -68,11 +97,13 @@ k_awa_pack(const TI* __restrict__ vqkv, const TI* __restrict__ tqkv, int ldq, Aw
                 o[j] = x[j];
             }
         }
-        store4((which == 0 ? Qp : Kp) + dst, o);
+        if constexpr (SPLIT3) store4_split3((which == 0 ? Qp : Kp) + dst, (size_t)20 * g.sumS * 128, o);
+        else store4((which == 0 ? Qp : Kp) + dst, o);
     }
     float v[4];
     load4(row + 2 * 2560 + h * 128 + d0, v);
-    store4(Vp + dst, v);
+    if constexpr (SPLIT3) store4_split3(Vp + dst, (size_t)20 * g.sumS * 128, v);
+    else store4(Vp + dst, v);
 }
 
 // SIMT flash attention: CTA = 64 queries of one (window, head); 4 threads per
@@ -231,6 +262,18 @@ void awa_pack(const void* vqkv, const void* tqkv, ActT in_t, int ldq, const AwaD
     else
         k_awa_pack<bf16, float><<<g.sumS, 640, 0, s>>>((const bf16*)vqkv, (const bf16*)tqkv, ldq, g, nqv, nkv,
                                                        nqt, nkt, eps, (float*)Qp, (float*)Kp, (float*)Vp);
+}
+
+void awa_pack_split3(const void* vqkv, const void* tqkv, ActT in_t, int ldq, const AwaDev& g, const float* nqv,
+                     const float* nkv, const float* nqt, const float* nkt, float eps, void* Q3, void* K3, void* V3,
+                     cudaStream_t s) {
+    if (g.sumS <= 0) return;
+    if (in_t == ACT_F32)
+        k_awa_pack<float, bf16, true><<<g.sumS, 640, 0, s>>>((const float*)vqkv, (const float*)tqkv, ldq, g, nqv, nkv,
+                                                             nqt, nkt, eps, (bf16*)Q3, (bf16*)K3, (bf16*)V3);
+    else
+        k_awa_pack<bf16, bf16, true><<<g.sumS, 640, 0, s>>>((const bf16*)vqkv, (const bf16*)tqkv, ldq, g, nqv, nkv,
+                                                            nqt, nkt, eps, (bf16*)Q3, (bf16*)K3, (bf16*)V3);
 }
 
 int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, const AwaDev& g, float scale, void* att, int ld_att,

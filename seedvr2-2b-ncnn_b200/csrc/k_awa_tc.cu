@@ -1111,6 +1111,303 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
     }
 }
 
+// ---------------------------------------------------------------- fp32 attention on the tensor cores
+// The fp32 path's attention from split3 operands (awa_pack_split3): every
+// fp32 value of Q, K, V and P is hi + mid + lo in bf16, and QK^T and PV are
+// the six part products of order <= 2 -- (1,1), (2,0), (0,2), (1,0), (0,1),
+// (0,0) with 0 = hi, 1 = mid, 2 = lo, smallest first -- accumulated in fp32
+// in TMEM; the dropped terms are below 2^-24 of the product.  Structure of
+// k_awa_attn_tc4, one CTA per SM (192 KB of part tiles, all 512 TMEM
+// columns): Q parts 3 x 32 KB, one K and one V tile (3 x 16 KB each, 64
+// keys), S in one 64-column slot, P as three 32-column parts of packed bf16
+// pairs, O in 128 columns.  The S slot is released (s_free) as soon as the
+// softmax has S_j in registers, so S_{j+1} runs on the tensor pipe during
+// the softmax of step j; the softmax waits for PV_{j-1} only before it
+// overwrites the P parts.  The loads run one tile ahead: K_{j+1} once S_j is
+// done, V_{j+1} once PV_j is done.
+constexpr int X3_TILES = 3 * TILE_BYTES + 6 * KV4_BYTES;   // 192 KB
+constexpr int X3_SMEM = X3_TILES + 1024 + 256;
+constexpr int X3_TMEM = 512;
+constexpr int X3_NTERM = 6;
+__device__ __constant__ int8_t c_x3_terms[X3_NTERM][2] = {{1, 1}, {2, 0}, {0, 2}, {1, 0}, {0, 1}, {0, 0}};
+
+struct AttnX3Ctl {
+    uint64_t q_full, k_full, k_empty, v_full, v_empty;
+    uint64_t s_full, s_free, p_ready, pv_done, o_full, drain;
+    uint32_t tmem_slot;
+    int abort;
+};
+
+// fp32 P as three bf16 parts of a pair (a in the low halves).
+__device__ __forceinline__ void split3_pair(float a, float b, uint32_t& hi, uint32_t& mid, uint32_t& lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(h);
+    const float ra = __fsub_rn(a, hf.x), rb = __fsub_rn(b, hf.y);
+    const __nv_bfloat162 m = __floats2bfloat162_rn(ra, rb);
+    const float2 mf = __bfloat1622float2(m);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(__fsub_rn(ra, mf.x), __fsub_rn(rb, mf.y));
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    mid = *reinterpret_cast<const uint32_t*>(&m);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+__global__ void __launch_bounds__(T4_THREADS, 1)
+k_awa_attn_x3(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
+              const __grid_constant__ CUtensorMap tV, const AttnParams p) {
+    const int wi = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * QT;
+    const int f = p.g.cumf[wi + 1] - p.g.cumf[wi];
+    const int S = f + p.g.TXT;
+    if (q0 >= S) return;                       // uniform across the CTA, before any barrier
+    const int nkt = (S + KT4 - 1) / KT4;
+    const int row_base = h * p.g.sumS + p.g.cums[wi];
+    const int part_rows = 20 * p.g.sumS;       // rows between the parts of one operand
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;                              // 3 parts x 32 KB
+    uint8_t* sK = smem + 3 * TILE_BYTES;             // 3 parts x 16 KB
+    uint8_t* sV = sK + 3 * KV4_BYTES;                // 3 parts x 16 KB
+    AttnX3Ctl* ctl = reinterpret_cast<AttnX3Ctl*>(smem + X3_TILES);
+    volatile int* abort_flag = &ctl->abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    auto load_kv = [&](const CUtensorMap* tm, uint8_t* dst, uint64_t* bar, int j) {
+        sm100::mbar_arrive_expect_tx(bar, 3 * KV4_BYTES);
+        #pragma unroll
+        for (int a = 0; a < 3; a++) {
+            const int r = a * part_rows + row_base + j * KT4;
+            sm100::tma_load_2d(dst + a * KV4_BYTES, tm, bar, 0, r);
+            sm100::tma_load_2d(dst + a * KV4_BYTES + KV4_HALF, tm, bar, 64, r);
+        }
+    };
+    if (threadIdx.x == 5 * 32) {
+        sm100::tma_prefetch_desc(&tQ);
+        sm100::tma_prefetch_desc(&tK);
+        sm100::tma_prefetch_desc(&tV);
+        sm100::mbar_init(&ctl->q_full, 1);
+        sm100::mbar_init(&ctl->k_full, 1);
+        sm100::mbar_init(&ctl->k_empty, 1);
+        sm100::mbar_init(&ctl->v_full, 1);
+        sm100::mbar_init(&ctl->v_empty, 1);
+        sm100::mbar_init(&ctl->s_full, 1);
+        sm100::mbar_init(&ctl->s_free, 4);
+        sm100::mbar_init(&ctl->p_ready, 4);
+        sm100::mbar_init(&ctl->pv_done, 1);
+        sm100::mbar_init(&ctl->o_full, 1);
+        sm100::mbar_init(&ctl->drain, 1);
+        ctl->abort = 0;
+        sm100::fence_barrier_init();
+        sm100::mbar_arrive_expect_tx(&ctl->q_full, 3 * TILE_BYTES);
+        #pragma unroll
+        for (int a = 0; a < 3; a++) {
+            const int r = a * part_rows + row_base + q0;
+            sm100::tma_load_2d(sQ + a * TILE_BYTES, &tQ, &ctl->q_full, 0, r);
+            sm100::tma_load_2d(sQ + a * TILE_BYTES + HALF_BYTES, &tQ, &ctl->q_full, 64, r);
+        }
+        load_kv(&tK, sK, &ctl->k_full, 0);
+        load_kv(&tV, sV, &ctl->v_full, 0);
+    }
+    const int my_q = q0 + (threadIdx.x & 127);
+    const int my_tok = (warp < 4 && my_q < f) ? p.g.vidx[p.g.cumf[wi] + my_q] : 0;
+    if (warp == 4) {
+        sm100::tmem_alloc(&ctl->tmem_slot, X3_TMEM);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = ctl->tmem_slot;
+    const uint32_t tS = tmem, tP = tmem + 64, tO = tmem + 256;   // P parts at tP + 32 * part
+
+    if (warp == 5) {
+        if (lane == 0) {
+            // ---- TMA producer: K_{j+1} once S_j is done, V_{j+1} once PV_j is done
+            bool ok = true;
+            int kq = 1, vq = 1;
+            for (int j = 0; j + 1 < nkt && ok; j++) {
+                if (!(ok = wait_bar(&ctl->k_empty, (uint32_t)j & 1, abort_flag))) break;
+                load_kv(&tK, sK, &ctl->k_full, j + 1);
+                kq++;
+                if (!(ok = wait_bar(&ctl->v_empty, (uint32_t)j & 1, abort_flag))) break;
+                load_kv(&tV, sV, &ctl->v_full, j + 1);
+                vq++;
+            }
+            if (!ok) {
+                // drain this thread's own TMA loads (bounded) before shared memory is released
+                for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->q_full, 0); w++) {}
+                for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->k_full, (uint32_t)(kq - 1) & 1); w++) {}
+                for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->v_full, (uint32_t)(vq - 1) & 1); w++) {}
+            }
+        }
+    } else if (warp == 4) {
+        if (lane == 0) {
+            // ---- MMA issuer
+            auto issue_s = [&]() {
+                #pragma unroll 1
+                for (int t = 0; t < X3_NTERM; t++) {
+                    const uint8_t* qa = sQ + c_x3_terms[t][0] * TILE_BYTES;
+                    const uint8_t* kb = sK + c_x3_terms[t][1] * KV4_BYTES;
+                    #pragma unroll
+                    for (int kk = 0; kk < D / 16; kk++) {
+                        const uint32_t aoff = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
+                        const uint32_t boff = (kk >> 2) * KV4_HALF + (kk & 3) * 32;
+                        sm100::mma_bf16(tS, sm100::desc_kmajor_sw128(qa, aoff), sm100::desc_kmajor_sw128(kb, boff),
+                                        IDESC_QK4, (t | kk) != 0);
+                    }
+                }
+                sm100::mma_commit(&ctl->s_full);
+                sm100::mma_commit(&ctl->k_empty);
+            };
+            bool ok = wait_bar(&ctl->q_full, 0, abort_flag);
+            if (ok && (ok = wait_bar(&ctl->k_full, 0, abort_flag))) {
+                sm100::tc_fence_after();
+                issue_s();
+            }
+            for (int j = 0; j < nkt && ok; j++) {
+                if (j + 1 < nkt) {
+                    // the softmax has S_j in registers and K_{j+1} is in
+                    if (!(ok = wait_bar(&ctl->s_free, (uint32_t)j & 1, abort_flag))) break;
+                    if (!(ok = wait_bar(&ctl->k_full, (uint32_t)(j + 1) & 1, abort_flag))) break;
+                    sm100::tc_fence_after();
+                    issue_s();
+                }
+                if (!(ok = wait_bar(&ctl->p_ready, (uint32_t)j & 1, abort_flag))) break;
+                if (!(ok = wait_bar(&ctl->v_full, (uint32_t)j & 1, abort_flag))) break;
+                sm100::tc_fence_after();
+                #pragma unroll 1
+                for (int t = 0; t < X3_NTERM; t++) {
+                    const uint32_t pa = tP + 32 * c_x3_terms[t][0];
+                    const uint8_t* vb = sV + c_x3_terms[t][1] * KV4_BYTES;
+                    #pragma unroll
+                    for (int kk = 0; kk < KT4 / 16; kk++)
+                        sm100::mma_bf16_tmem_a(tO, pa + kk * 8, desc_v64(vb, kk * 2048), IDESC_PV, (j | t | kk) != 0);
+                }
+                sm100::mma_commit(&ctl->pv_done);
+                sm100::mma_commit(&ctl->v_empty);
+                if (j + 1 == nkt) sm100::mma_commit(&ctl->o_full);
+            }
+            sm100::mma_commit(&ctl->drain);
+            for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->drain, 0); w++) {}
+        }
+    } else {
+        // ---- softmax + epilogue: thread = query row q0 + r; TMEM lane quadrant = warp
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        const float sl = p.scale_log2;
+        const bool live = q0 + warp * 32 < S;  // warp-uniform: any of this warp's rows is a query
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nkt; j++) {
+            ok = __all_sync(0xffffffffu, wait_bar(&ctl->s_full, (uint32_t)j & 1, abort_flag));
+            if (!ok) break;
+            float v[64];
+            if (live) {
+                sm100::tc_fence_after();
+                sm100::tmem_ld64(tS + lane_off, v);
+            }
+            // S_j is in registers: the slot may take S_{j+1}
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(&ctl->s_free);
+            bool pv_waited = (j == 0);                 // warp-uniform
+            uint32_t ph[32], pm[32], pl[32];
+            if (live) {
+                const int kvalid = S - j * KT4;
+                const bool full = kvalid >= KT4;           // CTA-uniform
+                const float mx = (full ? max64_full(v) : max64_t<true>(v, kvalid)) * sl;
+                if (j == 0) {
+                    m = mx;
+                } else {
+                    const bool grow = mx > m + T_RESCALE;
+                    if (__any_sync(0xffffffffu, grow)) {
+                        ok = __all_sync(0xffffffffu, wait_bar(&ctl->pv_done, (uint32_t)(j - 1) & 1, abort_flag));
+                        if (!ok) break;
+                        pv_waited = true;
+                        sm100::tc_fence_after();
+                        const float mn = grow ? mx : m;
+                        const float corr = exp2f(m - mn);
+                        #pragma unroll 1
+                        for (int c = 0; c < 4; c++) {
+                            float o[32];
+                            sm100::tmem_ld32(tO + lane_off + c * 32, o);
+                            #pragma unroll
+                            for (int u = 0; u < 32; u++) o[u] *= corr;
+                            tmem_st32(tO + lane_off + c * 32, o);
+                        }
+                        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                        l *= corr;
+                        m = mn;
+                    }
+                }
+                const float nm = -m;
+                float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                #pragma unroll
+                for (int u = 0; u < 32; u++) {
+                    float a = ex2_approx(fmaf(v[2 * u], sl, nm)), b = ex2_approx(fmaf(v[2 * u + 1], sl, nm));
+                    if (!full) { a = (2 * u < kvalid) ? a : 0.f; b = (2 * u + 1 < kvalid) ? b : 0.f; }
+                    ls[u & 7] += a + b;
+                    split3_pair(a, b, ph[u], pm[u], pl[u]);
+                }
+                l += sum8(ls);
+            }
+            // every warp waits for PV_{j-1} before its p_ready of step j: the
+            // P parts are free, and no arrival of step j lands in step j-1's phase
+            if (!pv_waited) {
+                ok = __all_sync(0xffffffffu, wait_bar(&ctl->pv_done, (uint32_t)(j - 1) & 1, abort_flag));
+                if (!ok) break;
+            }
+            if (live) {
+                tmem_st32u(tP + lane_off, ph);
+                tmem_st32u(tP + lane_off + 32, pm);
+                tmem_st32u(tP + lane_off + 64, pl);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            }
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(&ctl->p_ready);
+        }
+        if (ok) ok = __all_sync(0xffffffffu, wait_bar(&ctl->o_full, 0, abort_flag));
+        if (ok && live) {
+            sm100::tc_fence_after();
+            const float inv = 1.f / l;
+            float* stage = reinterpret_cast<float*>(smem) + (size_t)warp * 32 * STG_LD;
+            float* mine = stage + lane * STG_LD;
+            #pragma unroll 1
+            for (int c = 0; c < 2; c++) {
+                float o[64];
+                sm100::tmem_ld64(tO + lane_off + c * 64, o);
+                #pragma unroll
+                for (int u = 0; u < 64; u += 4)
+                    *reinterpret_cast<float4*>(mine + c * 64 + u) =
+                        make_float4(o[u] * inv, o[u + 1] * inv, o[u + 2] * inv, o[u + 3] * inv);
+            }
+            const int qw = q0 + warp * 32;
+            const int nrows = min(32, S - qw);
+            __syncwarp();
+            #pragma unroll 4
+            for (int rr = 0; rr < nrows; rr++) {
+                const int q = qw + rr;
+                const int tok = __shfl_sync(0xffffffffu, my_tok, rr);
+                const float4 x = *reinterpret_cast<const float4*>(stage + rr * STG_LD + lane * 4);
+                const float xv[4] = {x.x, x.y, x.z, x.w};
+                if (q < f) {
+                    if (p.att_bf16)
+                        store4((bf16*)p.att + (size_t)tok * p.ld_att + h * D + lane * 4, xv);
+                    else
+                        store4((float*)p.att + (size_t)tok * p.ld_att + h * D + lane * 4, xv);
+                } else {
+                    store4(p.toutw + ((size_t)wi * p.g.TXT + (q - f)) * 2560 + h * D + lane * 4, xv);
+                }
+            }
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        sm100::tc_fence_after();
+        sm100::tmem_dealloc(tmem, X3_TMEM);
+    }
+}
+
 }  // namespace
 
 bool awa_tc_available() { return true; }
@@ -1161,7 +1458,28 @@ int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, const AwaDev& 
     return 0;
 }
 
+int awa_attend_split3(const void* Q3, const void* K3, const void* V3, const AwaDev& g, float scale, void* att,
+                      int ld_att, ActT at, float* toutw, cudaStream_t s) {
+    const int rows = 3 * 20 * g.sumS;       // the three parts stacked
+    CUtensorMap tq, tk, tv;
+    if (!make_tmap_bf16(&tq, Q3, rows, D, D, QT, 64) || !make_tmap_bf16(&tk, K3, rows, D, D, KT4, 64) ||
+        !make_tmap_bf16(&tv, V3, rows, D, D, KT4, 64))
+        return -1;
+    AttnParams p;
+    p.g = g;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.att = att;
+    p.ld_att = ld_att;
+    p.att_bf16 = (at == ACT_BF16);
+    p.toutw = toutw;
+    dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
+    k_awa_attn_x3<<<grid, T4_THREADS, X3_SMEM, s>>>(tq, tk, tv, p);
+    return 0;
+}
+
 int awa_tc_init_device() {
+    if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_x3, cudaFuncAttributeMaxDynamicSharedMemorySize, X3_SMEM))
+        return (int)e;
     if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES))
         return (int)e;
     if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES))

@@ -126,6 +126,18 @@ struct AwaDev {
 void awa_pack(const void* vqkv, const void* tqkv, ActT in_t, int ldq, const AwaDev& g, const float* nqv,
               const float* nkv, const float* nqt, const float* nkt, float eps, void* Qp, void* Kp, void* Vp,
               ActT pt, cudaStream_t s);
+// The same packing for the fp32 tensor-core attention: Q3/K3/V3 each hold
+// three bf16 parts [3][HEADS][sumS][128] (hi, mid, lo; hi + mid + lo equals
+// the fp32 value to fp32 precision).
+void awa_pack_split3(const void* vqkv, const void* tqkv, ActT in_t, int ldq, const AwaDev& g, const float* nqv,
+                     const float* nkv, const float* nqt, const float* nkt, float eps, void* Q3, void* K3, void* V3,
+                     cudaStream_t s);
+// fp32 attention on the tcgen05 tensor cores from split3 operands: QK^T and
+// PV as the six bf16 part products of order <= 2 (hi.hi, hi.mid, mid.hi,
+// hi.lo, lo.hi, mid.mid), fp32 accumulation in TMEM.  Returns -1 when the
+// kernel cannot run (no tensor-map encoder); then nothing was launched.
+int awa_attend_split3(const void* Q3, const void* K3, const void* V3, const AwaDev& g, float scale, void* att,
+                      int ld_att, ActT at, float* toutw, cudaStream_t s);
 // Per-window SDPA.  vid rows scattered to att[vidx]; txt rows to toutw[wi][i].
 void awa_attend(const void* Qp, const void* Kp, const void* Vp, ActT pt, const AwaDev& g, float scale,
                 void* att, int ld_att, ActT at, float* toutw, cudaStream_t s, int* launches);

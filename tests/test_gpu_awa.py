@@ -144,3 +144,24 @@ def test_awa_1080p_bf16_vs_fp32(shifted):
     for a, b in zip(out[s2b.PREC_BF16], out[s2b.PREC_FP32]):
         cos, rel = cases.compare(a, b)
         assert cos >= 0.9995 and rel <= 2e-2, (cos, rel)
+
+
+def test_awa_fp32_simt_fallback_vs_port(port):
+    """fp32 contexts run the attention on the tensor cores from split3
+    operands; S2B_FP32_ATTN=simt (read at context creation) keeps the SIMT
+    kernel, held to the same fp32 bar."""
+    Lv, TXT = 24 * 28, 58
+    vqkv, tqkv, nq = cases.awa_cfg_inputs(Lv, TXT)
+    sl, vf, tf = port.make_win(1, 24, 28, (4, 3, 3), TXT, True)
+    vo_r, to_r = port.awa(vqkv, tqkv, 1, 24, 28, TXT, sl, vf, tf, *nq, 1e-6)
+    os.environ["S2B_FP32_ATTN"] = "simt"
+    try:
+        c = s2b.DitB200(0, s2b.PREC_FP32)
+    finally:
+        del os.environ["S2B_FP32_ATTN"]
+    try:
+        vo, to = c.awa_forward(vqkv, tqkv, win_of(1, 24, 28, TXT, sl, vf, tf), *nq, Lv, TXT, 1e-6)
+        check(c, vo, vo_r)
+        check(c, to, to_r)
+    finally:
+        c.close()
