@@ -1,23 +1,21 @@
-// k_awa_tc.cu -- AWA window attention on the 5th-gen tensor cores (bf16).
+// k_awa_tc.cu -- AWA window attention on the 5th-gen tensor cores.
 //
 // All operands come from the window-packed, head-major Q/K/V slabs the QKV
 // GEMM epilogue (or the pack kernel, k_awa.cu) writes, so every tile is a
 // plain 2-D TMA box; vid outputs go back to their grid token, txt outputs to
 // the per-window partials averaged later.  Keys past the window's end are
 // masked (their shared-memory rows hold the neighbouring window's finite data
-// or TMA zero fill).  Three kernels:
-//   k_awa_attn_tc4 (default)  one CTA per (window, head, 128-query tile), two
-//                             CTAs per SM, 64-key K/V tiles double-buffered;
-//                             S in two TMEM slots, P written back into TMEM
-//                             and used as the A operand of O += P V.
-//   k_awa_attn_tc             128-key tiles, P through shared memory over
-//                             the spent K tile.
-//   k_awa_attn_tc2            persistent, two query tiles per CTA sharing
-//                             every K/V tile (ping-pong softmax warpgroups).
-// Softmax: one query row per thread, ex2.approx, bf16 packing with the
-// conversion instruction (integer-ALU packing selectable), lazy O rescale (only when a row's max grows by more than 2^8, so
-// P <= 2^8).  Every mbarrier wait is bounded (error flag g_attn_err on
-// expiry); warp-collective TMEM instructions run under warp-uniform control.
+// or TMA zero fill).  Two kernels:
+//   k_awa_attn_tc4   bf16 operands: one CTA per (window, head, 128-query
+//                    tile), two CTAs per SM, 64-key K/V tiles double-
+//                    buffered; S in two TMEM slots, P written back into TMEM
+//                    and used as the A operand of O += P V.
+//   k_awa_attn_x3    fp32 path: the same tiles from three bf16 parts per
+//                    fp32 value (six part products), one CTA per SM.
+// Softmax: one query row per thread, ex2.approx, lazy O rescale (only when a
+// row's max grows by more than 2^8, so P <= 2^8).  Every mbarrier wait is
+// bounded (error flag g_attn_err on expiry); warp-collective TMEM
+// instructions run under warp-uniform control.
 #include "kernels.h"
 #include "kcommon.cuh"
 #include "sm100.cuh"
@@ -27,28 +25,18 @@
 namespace s2b {
 
 bool make_tmap_bf16(CUtensorMap* m, const void* base, int rows, int cols, int ld, int box_rows, int box_cols);
-int awa_tc_kernel_version();
 int awa_tc_poly_exp();
 
 namespace {
 
-constexpr int QT = 128, KT = 128, D = 128;
+constexpr int QT = 128, D = 128;
 constexpr int TILE_BYTES = QT * D * 2;            // 32 KB: two 64-column swizzled halves
 constexpr int HALF_BYTES = TILE_BYTES / 2;
-constexpr int NUM_THREADS = 160;
-constexpr int TMEM_COLS = 256;                     // S: [0,128), O: [128,256)
-constexpr int SMEM_BYTES = 3 * TILE_BYTES + 1024 + 256;
-constexpr uint32_t IDESC_QK = sm100::idesc_bf16_f32(QT, KT);
+constexpr int TMEM_COLS = 256;                     // 64-key kernel: S slots [0,128), O [128,256)
 constexpr uint32_t IDESC_PV = sm100::idesc_bf16_f32(QT, D) | (1u << 16);   // B (V) MN-major
 constexpr float T_RESCALE = 8.f;
 
 __device__ int g_attn_err;
-
-struct AttnCtl {
-    uint64_t q_full, k_full, v_full, s_full, p_ready, pv_done;
-    uint32_t tmem_slot;
-    int abort;
-};
 
 struct AttnParams {
     AwaDev g;
@@ -67,20 +55,6 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatil
     *abort_flag = 1;
     atomicExch(&g_attn_err, 1);
     return false;
-}
-
-// MN-major operand (V: rows = keys, 64 head dims per 128-B row, two 64-dim
-// halves 16 KB apart): leading byte offset = distance between 64-wide MN
-// blocks, stride byte offset = distance between 8-key groups.
-__device__ __forceinline__ uint64_t desc_mnmajor_sw128(const void* tile, uint32_t k_group_bytes) {
-    const uint32_t addr = sm100::smem_u32(tile) + k_group_bytes;
-    uint64_t d = 0;
-    d |= (uint64_t)((addr >> 4) & 0x3FFFu);
-    d |= (uint64_t)(HALF_BYTES >> 4) << 16;
-    d |= (uint64_t)(1024u >> 4) << 32;
-    d |= (uint64_t)1u << 46;
-    d |= (uint64_t)2u << 61;
-    return d;
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float v[32]) {
@@ -105,23 +79,11 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
-// Two floats rounded to nearest-even bf16 and packed (a in the low half):
-// with the conversion instruction, or (ALU) by integer rounding of the two
-// non-negative finite values, which leaves the conversion/transcendental
-// unit to the exponentials.
-template <bool ALU>
-__device__ __forceinline__ uint32_t pack_bf16x2_t(float a, float b) {
-    if constexpr (ALU) {
-        uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
-        ua += 0x7FFFu + ((ua >> 16) & 1u);
-        ub += 0x7FFFu + ((ub >> 16) & 1u);
-        return __byte_perm(ua, ub, 0x7632);
-    } else {
-        __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
-        return *reinterpret_cast<uint32_t*>(&v);
-    }
+// Two floats rounded to nearest-even bf16 and packed (a in the low half).
+__device__ __forceinline__ uint32_t pack_bf16x2_rn(float a, float b) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
 }
-__device__ __forceinline__ uint32_t pack_bf16x2_rn(float a, float b) { return pack_bf16x2_t<false>(a, b); }
 
 // Max of n (<= 64) leading values of v, -inf for the rest, through 8
 // independent accumulators (a chain of 8 instead of 64 dependent fmaxf).
@@ -134,299 +96,11 @@ __device__ __forceinline__ float max64_t(const float* v, int nvalid) {
     for (int u = 0; u < 64; u++) a[u & 7] = fmaxf(a[u & 7], (!MASK || u < nvalid) ? v[u] : -INFINITY);
     return fmaxf(fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3])), fmaxf(fmaxf(a[4], a[5]), fmaxf(a[6], a[7])));
 }
-// nvalid >= 64: no masking instructions at all.
-__device__ __forceinline__ float max64(const float* v, int nvalid) {
-    return nvalid >= 64 ? max64_t<false>(v, 64) : max64_t<true>(v, nvalid);
-}
 __device__ __forceinline__ float sum8(const float* a) {
     return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
 }
 
-// 2^x on the FMA/ALU pipes, for x <= ~8 (softmax exponents): Cody-Waite
-// split x = j + f with j = round(x) (adding 1.5 * 2^23 rounds to an integer
-// in the low mantissa bits) and |f| <= 1/2, 2^f by a cubic fitted here by
-// relative least squares on Chebyshev nodes of [-1/2, 1/2] (max relative
-// error 7.7e-5, below bf16's 2^-9 rounding of P), and 2^j added to the
-// exponent field.  x is clamped at -120 so the exponent stays normal.
-__device__ __forceinline__ float ex2_poly(float x) {
-    x = fmaxf(x, -120.f);
-    const float t = __fadd_rn(x, 12582912.f);
-    const int j = __float_as_int(t) - 0x4B400000;
-    const float f = __fsub_rn(x, __fsub_rn(t, 12582912.f));
-    float p = fmaf(f, 0.05508868396282196f, 0.24260404706001282f);
-    p = fmaf(f, p, 0.6932762265205383f);
-    p = fmaf(f, p, 0.9999289512634277f);
-    return __int_as_float(__float_as_int(p) + (j << 23));
-}
-
-template <bool POLY>
-__global__ void __launch_bounds__(NUM_THREADS, 2)
-k_awa_attn_tc(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
-              const __grid_constant__ CUtensorMap tV, const AttnParams p) {
-    const int wi = blockIdx.z, h = blockIdx.y, q0 = blockIdx.x * QT;
-    const int f = p.g.cumf[wi + 1] - p.g.cumf[wi];
-    const int S = f + p.g.TXT;
-    if (q0 >= S) return;                       // uniform across the CTA, before any barrier
-    const int nkt = (S + KT - 1) / KT;
-    const int row_base = h * p.g.sumS + p.g.cums[wi];
-
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;
-    uint8_t* sK = smem + TILE_BYTES;          // K_j, then P_j
-    uint8_t* sV = smem + 2 * TILE_BYTES;
-    AttnCtl* ctl = reinterpret_cast<AttnCtl*>(smem + 3 * TILE_BYTES);
-    volatile int* abort_flag = &ctl->abort;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    if (threadIdx.x == 0) {
-        sm100::mbar_init(&ctl->q_full, 1);
-        sm100::mbar_init(&ctl->k_full, 1);
-        sm100::mbar_init(&ctl->v_full, 1);
-        sm100::mbar_init(&ctl->s_full, 1);
-        sm100::mbar_init(&ctl->p_ready, 4);
-        sm100::mbar_init(&ctl->pv_done, 1);
-        ctl->abort = 0;
-        sm100::fence_barrier_init();
-    }
-    if (warp == 4) {
-        sm100::tmem_alloc(&ctl->tmem_slot, TMEM_COLS);
-        sm100::tmem_relinquish();
-    }
-    sm100::tc_fence_before();
-    __syncthreads();
-    sm100::tc_fence_after();
-    const uint32_t tmem = ctl->tmem_slot;
-    const uint32_t tS = tmem, tO = tmem + 128;
-
-    if (warp == 4) {
-        if (lane == 0) {
-            bool ok = true;
-            sm100::mbar_arrive_expect_tx(&ctl->q_full, TILE_BYTES);
-            sm100::tma_load_2d(sQ, &tQ, &ctl->q_full, 0, row_base + q0);
-            sm100::tma_load_2d(sQ + HALF_BYTES, &tQ, &ctl->q_full, 64, row_base + q0);
-            sm100::mbar_arrive_expect_tx(&ctl->k_full, TILE_BYTES);
-            sm100::tma_load_2d(sK, &tK, &ctl->k_full, 0, row_base);
-            sm100::tma_load_2d(sK + HALF_BYTES, &tK, &ctl->k_full, 64, row_base);
-            sm100::mbar_arrive_expect_tx(&ctl->v_full, TILE_BYTES);
-            sm100::tma_load_2d(sV, &tV, &ctl->v_full, 0, row_base);
-            sm100::tma_load_2d(sV + HALF_BYTES, &tV, &ctl->v_full, 64, row_base);
-            int kv_issued = 1;        // K/V tile loads issued so far
-            ok = wait_bar(&ctl->q_full, 0, abort_flag);
-            for (int j = 0; j < nkt && ok; j++) {
-                const uint32_t ph = j & 1;
-                if (!(ok = wait_bar(&ctl->k_full, ph, abort_flag))) break;
-                sm100::tc_fence_after();
-                #pragma unroll
-                for (int kk = 0; kk < D / 16; kk++) {
-                    const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-                    sm100::mma_bf16(tS, sm100::desc_kmajor_sw128(sQ, off), sm100::desc_kmajor_sw128(sK, off),
-                                    IDESC_QK, kk != 0);
-                }
-                sm100::mma_commit(&ctl->s_full);
-                if (!(ok = wait_bar(&ctl->v_full, ph, abort_flag))) break;
-                if (!(ok = wait_bar(&ctl->p_ready, ph, abort_flag))) break;
-                sm100::tc_fence_after();
-                #pragma unroll
-                for (int kk = 0; kk < KT / 16; kk++) {
-                    const uint32_t aoff = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-                    sm100::mma_bf16(tO, sm100::desc_kmajor_sw128(sK, aoff), desc_mnmajor_sw128(sV, kk * 2048),
-                                    IDESC_PV, (j | kk) != 0);
-                }
-                sm100::mma_commit(&ctl->pv_done);
-                if (j + 1 < nkt) {
-                    // P_j (in the K buffer) and V_j are read by the PV MMAs: wait, then refill
-                    if (!(ok = wait_bar(&ctl->pv_done, ph, abort_flag))) break;
-                    const int r = row_base + (j + 1) * KT;
-                    sm100::mbar_arrive_expect_tx(&ctl->k_full, TILE_BYTES);
-                    sm100::tma_load_2d(sK, &tK, &ctl->k_full, 0, r);
-                    sm100::tma_load_2d(sK + HALF_BYTES, &tK, &ctl->k_full, 64, r);
-                    sm100::mbar_arrive_expect_tx(&ctl->v_full, TILE_BYTES);
-                    sm100::tma_load_2d(sV, &tV, &ctl->v_full, 0, r);
-                    sm100::tma_load_2d(sV + HALF_BYTES, &tV, &ctl->v_full, 64, r);
-                    kv_issued++;
-                }
-            }
-            if (!ok) {
-                // drain this thread's own TMA loads (bounded) before shared memory is released
-                const uint32_t ph = (uint32_t)(kv_issued - 1) & 1;
-                for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->q_full, 0); w++) {}
-                for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->k_full, ph); w++) {}
-                for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->v_full, ph); w++) {}
-            }
-        }
-    } else {
-        // softmax / epilogue: thread = query row q0 + r; TMEM lane quadrant = warp
-        const int r = warp * 32 + lane;
-        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-        float m = -INFINITY, l = 0.f;
-        bool ok = true;
-        // Every tcgen05.ld / tcgen05.st below is warp-collective (.sync.aligned):
-        // all 32 lanes execute each one, with warp-uniform control flow; the
-        // per-row differences only select values and stores.
-        for (int j = 0; j < nkt; j++) {
-            ok = __all_sync(0xffffffffu, wait_bar(&ctl->s_full, j & 1, abort_flag));
-            if (!ok) break;
-            sm100::tc_fence_after();
-            const int kvalid = S - j * KT;           // keys [0, kvalid) of this tile are real
-            const bool full = kvalid >= KT;          // CTA-uniform
-            // pass 1: row max of the scores (scale > 0, so scaling commutes)
-            float mr = -INFINITY;
-            #pragma unroll
-            for (int c = 0; c < 2; c++) {
-                float v[64];
-                sm100::tmem_ld64(tS + lane_off + c * 64, v);
-                mr = fmaxf(mr, max64(v, full ? 64 : kvalid - c * 64));
-            }
-            const float mx = mr * p.scale_log2;
-            // A row keeps the max its exponentials use until a tile's max
-            // exceeds it by more than T_RESCALE (log2 units); only then O and
-            // l are rescaled (the previous PV is complete: its commit preceded
-            // this S tile's), so P <= 2^T_RESCALE.
-            if (j == 0) {
-                m = mx;
-            } else {
-                const bool grow = mx > m + T_RESCALE;
-                if (__any_sync(0xffffffffu, grow)) {
-                    const float mn = grow ? mx : m;
-                    const float corr = exp2f(m - mn);
-                    #pragma unroll 1
-                    for (int c = 0; c < 4; c++) {
-                        float o[32];
-                        sm100::tmem_ld32(tO + lane_off + c * 32, o);
-                        #pragma unroll
-                        for (int t = 0; t < 32; t++) o[t] *= corr;
-                        tmem_st32(tO + lane_off + c * 32, o);
-                    }
-                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                    l *= corr;
-                    m = mn;
-                }
-            }
-            // pass 2: P row -> shared memory, K-major 128-B swizzled [128 rows x 128 keys]
-            const float sl = p.scale_log2, nm = -m;
-            float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            #pragma unroll
-            for (int half = 0; half < 2; half++) {
-                float v[64];
-                sm100::tmem_ld64(tS + lane_off + half * 64, v);
-                #pragma unroll
-                for (int chunk = 0; chunk < 8; chunk++) {
-                    float pv[8];
-                    #pragma unroll
-                    for (int t = 0; t < 8; t++) {
-                        const int k = half * 64 + chunk * 8 + t;
-                        const float x = fmaf(v[chunk * 8 + t], sl, nm);
-                        pv[t] = (!full && k >= kvalid) ? 0.f
-                              : (POLY && (t & 3) == 3) ? ex2_poly(x) : ex2_approx(x);
-                        ls[t] += pv[t];
-                    }
-                    uint4 u;
-                    u.x = pack_bf16x2_rn(pv[0], pv[1]); u.y = pack_bf16x2_rn(pv[2], pv[3]);
-                    u.z = pack_bf16x2_rn(pv[4], pv[5]); u.w = pack_bf16x2_rn(pv[6], pv[7]);
-                    uint8_t* dst = sK + half * HALF_BYTES + r * 128 + ((chunk ^ (r & 7)) << 4);
-                    *reinterpret_cast<uint4*>(dst) = u;
-                }
-            }
-            l += sum8(ls);
-            sm100::fence_proxy_async_smem();      // generic-proxy smem writes -> tensor-core reads
-            sm100::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) sm100::mbar_arrive(&ctl->p_ready);
-        }
-        if (ok) ok = __all_sync(0xffffffffu, wait_bar(&ctl->pv_done, (nkt - 1) & 1, abort_flag));
-        if (ok) {
-            sm100::tc_fence_after();
-            const int q = q0 + r;
-            const float inv = 1.f / l;
-            const bool is_vid = q < f, is_txt = (q >= f) && (q < S);
-            float* tdst = p.toutw + ((size_t)wi * p.g.TXT + (is_txt ? q - f : 0)) * 2560 + h * D;
-            const size_t tok = is_vid ? (size_t)p.g.vidx[p.g.cumf[wi] + q] : 0;
-            #pragma unroll 1
-            for (int c = 0; c < 4; c++) {
-                float o[32];
-                sm100::tmem_ld32(tO + lane_off + c * 32, o);
-                #pragma unroll
-                for (int t = 0; t < 32; t++) o[t] *= inv;
-                if (is_vid) {
-                    if (p.att_bf16) {
-                        bf16* dst = (bf16*)p.att + tok * p.ld_att + h * D + c * 32;
-                        #pragma unroll
-                        for (int t = 0; t < 32; t += 4) store4(dst + t, o + t);
-                    } else {
-                        float* dst = (float*)p.att + tok * p.ld_att + h * D + c * 32;
-                        #pragma unroll
-                        for (int t = 0; t < 32; t += 4) store4(dst + t, o + t);
-                    }
-                } else if (is_txt) {
-                    #pragma unroll
-                    for (int t = 0; t < 32; t += 4) store4(tdst + c * 32 + t, o + t);
-                }
-            }
-        }
-    }
-    sm100::tc_fence_before();
-    __syncthreads();
-    if (warp == 4) {
-        sm100::tc_fence_after();
-        sm100::tmem_dealloc(tmem, TMEM_COLS);
-    }
-}
-
-
-// ---------------------------------------------------------------- two-tile persistent kernel
-// One CTA per SM walks a list of work items (window, head, pair of 128-query
-// tiles), so the loads of the next item overlap the current item's work and
-// TMEM / barriers are set up once.  Per item the two query tiles share every
-// K/V tile.  TMEM holds S_0, S_1 (128 columns each) and O_0, O_1 (128 each):
-// all 512 columns.  P_t is written back over S_t's first 64 columns as packed
-// bf16 pairs and is the TMEM A operand of O_t += P_t V.  K and V stream
-// through two-stage TMA rings that continue across items.  Roles:
-//   warps 0-3 / 4-7  softmax + epilogue of tile 0 / tile 1 (thread = query row)
-//   warp 8 lane 0    TMA producer (Q of the next item once the current one's
-//                    scores are done; K/V ring)
-//   warp 9 lane 0    MMA issuer; per key tile j: PV_0(j), S_0(j+1), PV_1(j),
-//                    S_1(j+1), so one tile's scores run while the other
-//                    tile's softmax does.  S_t(step) is issued only after
-//                    PV_t(step-1) has completed (it reads P_t from S_t's
-//                    columns); the first PV of an item waits until the
-//                    epilogue has read the previous item's O_t.
-// Barrier phases: for query tile t, "step" counts its (item, key tile) pairs
-// across the CTA's items; s_full / p_ready / pv_done complete once per step,
-// o_empty once per item, q_full / q_empty once per item, the K/V rings once
-// per key tile.  Every role derives the same counts from the same item walk.
-// Running max: a row keeps the max its exponentials use until a tile's max
-// exceeds it by more than T_RESCALE (log2 units); only then O and l are
-// rescaled, so P <= 2^8 and most tiles skip the O read-modify-write in TMEM.
-constexpr int T2_THREADS = 320;
-constexpr int T2_SMEM = 6 * TILE_BYTES + 1024 + 512;
-
-struct Attn2Ctl {
-    uint64_t q_full, q_empty, k_full[2], v_full[2], k_empty[2], v_empty[2];
-    uint64_t s_full[2], p_ready[2], pv_done[2], o_empty[2], drain;
-    uint32_t tmem_slot;
-    int abort;
-};
-
-struct Item {
-    int wi, h, q0, nt, nkt, S, f, row_base;
-};
-
-// item -> (window, head, pair); false when the pair lies past the window.
-__device__ __forceinline__ bool decode_item(const AttnParams& p, int item, int maxpairs, Item& it) {
-    const int pr = item % maxpairs, rest = item / maxpairs;
-    it.h = rest % 20;
-    it.wi = rest / 20;
-    it.f = p.g.cumf[it.wi + 1] - p.g.cumf[it.wi];
-    it.S = it.f + p.g.TXT;
-    it.q0 = pr * 2 * QT;
-    if (it.q0 >= it.S) return false;
-    it.nt = (it.q0 + QT < it.S) ? 2 : 1;
-    it.nkt = (it.S + KT - 1) / KT;
-    it.row_base = it.h * p.g.sumS + p.g.cums[it.wi];
-    return true;
-}
-
+// 32 lanes x 32 consecutive columns of packed values (tcgen05.st; pair with wait::st).
 __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t r[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -438,289 +112,6 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t r[32])
           "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
 }
-
-template <bool POLY>
-__global__ void __launch_bounds__(T2_THREADS, 1)
-k_awa_attn_tc2(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
-               const __grid_constant__ CUtensorMap tV, const AttnParams p, int maxpairs) {
-    const int num_items = p.g.nwin * 20 * maxpairs;
-
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t* sQ = smem;                        // [2] tiles
-    uint8_t* sK = smem + 2 * TILE_BYTES;       // [2] stages
-    uint8_t* sV = smem + 4 * TILE_BYTES;       // [2] stages
-    Attn2Ctl* ctl = reinterpret_cast<Attn2Ctl*>(smem + 6 * TILE_BYTES);
-    volatile int* abort_flag = &ctl->abort;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    if (threadIdx.x == 0) {
-        sm100::mbar_init(&ctl->q_full, 1);
-        sm100::mbar_init(&ctl->q_empty, 1);
-        for (int i = 0; i < 2; i++) {
-            sm100::mbar_init(&ctl->k_full[i], 1);
-            sm100::mbar_init(&ctl->v_full[i], 1);
-            sm100::mbar_init(&ctl->k_empty[i], 1);
-            sm100::mbar_init(&ctl->v_empty[i], 1);
-            sm100::mbar_init(&ctl->s_full[i], 1);
-            sm100::mbar_init(&ctl->p_ready[i], 4);
-            sm100::mbar_init(&ctl->pv_done[i], 1);
-            sm100::mbar_init(&ctl->o_empty[i], 4);
-        }
-        sm100::mbar_init(&ctl->drain, 1);
-        ctl->abort = 0;
-        sm100::fence_barrier_init();
-    }
-    if (warp == 9) {
-        sm100::tmem_alloc(&ctl->tmem_slot, 512);
-        sm100::tmem_relinquish();
-    }
-    sm100::tc_fence_before();
-    __syncthreads();
-    sm100::tc_fence_after();
-    const uint32_t tmem = ctl->tmem_slot;
-
-    if (warp == 8) {
-        if (lane == 0) {
-            // ---- TMA producer
-            uint32_t nq = 0, gk = 0, gv = 0;   // Q loads, K loads, V loads issued
-            bool ok = true;
-            Item it;
-            for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
-                if (!decode_item(p, item, maxpairs, it)) continue;
-                // the previous item's scores are done with the Q buffers
-                if (nq > 0 && !(ok = wait_bar(&ctl->q_empty, (nq - 1) & 1, abort_flag))) break;
-                sm100::mbar_arrive_expect_tx(&ctl->q_full, it.nt * TILE_BYTES);
-                for (int t = 0; t < it.nt; t++) {
-                    const int y = it.row_base + it.q0 + t * QT;
-                    sm100::tma_load_2d(sQ + t * TILE_BYTES, &tQ, &ctl->q_full, 0, y);
-                    sm100::tma_load_2d(sQ + t * TILE_BYTES + HALF_BYTES, &tQ, &ctl->q_full, 64, y);
-                }
-                nq++;
-                for (int j = 0; j < it.nkt; j++) {
-                    const int r = it.row_base + j * KT;
-                    const int st = gk & 1;
-                    if (gk >= 2 && !(ok = wait_bar(&ctl->k_empty[st], ((gk >> 1) - 1) & 1, abort_flag))) break;
-                    sm100::mbar_arrive_expect_tx(&ctl->k_full[st], TILE_BYTES);
-                    sm100::tma_load_2d(sK + st * TILE_BYTES, &tK, &ctl->k_full[st], 0, r);
-                    sm100::tma_load_2d(sK + st * TILE_BYTES + HALF_BYTES, &tK, &ctl->k_full[st], 64, r);
-                    gk++;
-                    if (gv >= 2 && !(ok = wait_bar(&ctl->v_empty[st], ((gv >> 1) - 1) & 1, abort_flag))) break;
-                    sm100::mbar_arrive_expect_tx(&ctl->v_full[st], TILE_BYTES);
-                    sm100::tma_load_2d(sV + st * TILE_BYTES, &tV, &ctl->v_full[st], 0, r);
-                    sm100::tma_load_2d(sV + st * TILE_BYTES + HALF_BYTES, &tV, &ctl->v_full[st], 64, r);
-                    gv++;
-                }
-            }
-            if (!ok) {
-                // drain this thread's own TMA loads (bounded) before shared memory is released
-                if (nq > 0)
-                    for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->q_full, (nq - 1) & 1); w++) {}
-                for (uint32_t k = (gk > 2 ? gk - 2 : 0); k < gk; k++)
-                    for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->k_full[k & 1], (k >> 1) & 1); w++) {}
-                for (uint32_t k = (gv > 2 ? gv - 2 : 0); k < gv; k++)
-                    for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->v_full[k & 1], (k >> 1) & 1); w++) {}
-            }
-        }
-    } else if (warp == 9) {
-        if (lane == 0) {
-            // ---- MMA issuer
-            uint32_t nq = 0, g = 0;                 // items started, K/V tiles consumed
-            uint32_t step[2] = {0, 0};              // per query tile: steps issued (S)
-            uint32_t items_t[2] = {0, 0};           // per query tile: items finished
-            bool ok = true;
-            auto issue_s = [&](int t, uint32_t kg) {
-                const uint8_t* k = sK + (kg & 1) * TILE_BYTES;
-                const uint8_t* q = sQ + t * TILE_BYTES;
-                #pragma unroll
-                for (int kk = 0; kk < D / 16; kk++) {
-                    const uint32_t off = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
-                    sm100::mma_bf16(tmem + t * 128, sm100::desc_kmajor_sw128(q, off), sm100::desc_kmajor_sw128(k, off),
-                                    IDESC_QK, kk != 0);
-                }
-                sm100::mma_commit(&ctl->s_full[t]);
-            };
-            auto issue_pv = [&](int t, uint32_t vg, bool first) {
-                const uint8_t* v = sV + (vg & 1) * TILE_BYTES;
-                #pragma unroll
-                for (int kk = 0; kk < KT / 16; kk++)
-                    sm100::mma_bf16_tmem_a(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, desc_mnmajor_sw128(v, kk * 2048),
-                                           IDESC_PV, !(first && kk == 0));
-                sm100::mma_commit(&ctl->pv_done[t]);
-            };
-            Item it;
-            for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
-                if (!decode_item(p, item, maxpairs, it)) continue;
-                if (!(ok = wait_bar(&ctl->q_full, nq & 1, abort_flag))) break;
-                nq++;
-                // scores of key tile 0
-                if (!(ok = wait_bar(&ctl->k_full[g & 1], (g >> 1) & 1, abort_flag))) break;
-                sm100::tc_fence_after();
-                for (int t = 0; t < it.nt && ok; t++) {
-                    // S_t's columns still hold the previous step's P_t until its PV is done
-                    if (step[t] > 0 && !(ok = wait_bar(&ctl->pv_done[t], (step[t] - 1) & 1, abort_flag))) break;
-                    sm100::tc_fence_after();
-                    issue_s(t, g);
-                    step[t]++;
-                }
-                if (!ok) break;
-                sm100::mma_commit(&ctl->k_empty[g & 1]);
-                if (it.nkt == 1) sm100::mma_commit(&ctl->q_empty);
-                for (int j = 0; j < it.nkt && ok; j++) {
-                    const uint32_t kg = g + j;
-                    const bool more = j + 1 < it.nkt;
-                    if (!(ok = wait_bar(&ctl->v_full[kg & 1], (kg >> 1) & 1, abort_flag))) break;
-                    if (more && !(ok = wait_bar(&ctl->k_full[(kg + 1) & 1], ((kg + 1) >> 1) & 1, abort_flag))) break;
-                    for (int t = 0; t < it.nt && ok; t++) {
-                        const uint32_t sp = step[t] - 1;        // the step whose P is (about to be) ready
-                        if (!(ok = wait_bar(&ctl->p_ready[t], sp & 1, abort_flag))) break;
-                        // the epilogue of this tile's previous item has read O_t
-                        if (j == 0 && items_t[t] > 0 && !(ok = wait_bar(&ctl->o_empty[t], (items_t[t] - 1) & 1, abort_flag)))
-                            break;
-                        sm100::tc_fence_after();
-                        issue_pv(t, kg, j == 0);
-                        if (more) {
-                            if (!(ok = wait_bar(&ctl->pv_done[t], sp & 1, abort_flag))) break;
-                            sm100::tc_fence_after();
-                            issue_s(t, kg + 1);
-                            step[t]++;
-                        }
-                    }
-                    if (!ok) break;
-                    if (more) {
-                        sm100::mma_commit(&ctl->k_empty[(kg + 1) & 1]);
-                        if (j + 2 == it.nkt) sm100::mma_commit(&ctl->q_empty);
-                    }
-                    sm100::mma_commit(&ctl->v_empty[kg & 1]);
-                }
-                g += it.nkt;
-                for (int t = 0; t < it.nt; t++) items_t[t]++;
-            }
-            // all of this thread's MMAs done before TMEM / shared memory go away
-            sm100::mma_commit(&ctl->drain);
-            for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->drain, 0); w++) {}
-        }
-    } else {
-        // ---- softmax + epilogue: query tile t = warp / 4, row r of the tile
-        const int t = warp >> 2;
-        const int r = (warp & 3) * 32 + lane;
-        const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t tS = tmem + t * 128 + lane_off, tO = tmem + 256 + t * 128 + lane_off;
-        const float sl = p.scale_log2;
-        uint32_t step = 0;
-        bool ok = true;
-        Item it;
-        for (int item = blockIdx.x; item < num_items && ok; item += gridDim.x) {
-            if (!decode_item(p, item, maxpairs, it) || t >= it.nt) continue;
-            float m = -INFINITY, l = 0.f;
-            // tcgen05.ld / st are warp-collective: control flow stays warp-uniform
-            for (int j = 0; j < it.nkt; j++, step++) {
-                ok = __all_sync(0xffffffffu, wait_bar(&ctl->s_full[t], step & 1, abort_flag));
-                if (!ok) break;
-                sm100::tc_fence_after();
-                const int kvalid = it.S - j * KT;
-                const bool full = kvalid >= KT;        // warp-uniform
-                // pass 1: row max of the scores (scale > 0, so scaling commutes)
-                float mr = -INFINITY;
-                #pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    float v[64];
-                    sm100::tmem_ld64(tS + c * 64, v);
-                    mr = fmaxf(mr, max64(v, full ? 64 : kvalid - c * 64));
-                }
-                const float mx = mr * sl;
-                if (j == 0) {
-                    m = mx;
-                } else {
-                    const bool grow = mx > m + T_RESCALE;
-                    if (__any_sync(0xffffffffu, grow)) {
-                        // PV_t of the previous step is complete: this step's S was issued after it
-                        const float mn = grow ? mx : m;
-                        const float corr = exp2f(m - mn);
-                        #pragma unroll 1
-                        for (int c = 0; c < 4; c++) {
-                            float o[32];
-                            sm100::tmem_ld32(tO + c * 32, o);
-                            #pragma unroll
-                            for (int u = 0; u < 32; u++) o[u] *= corr;
-                            tmem_st32(tO + c * 32, o);
-                        }
-                        l *= corr;
-                        m = mn;
-                    }
-                }
-                // pass 2: P_t as packed bf16 pairs over S_t's columns [0, 64);
-                // keys [64h, 64h+64) land in columns [32h, 32h+32), already read
-                const float nm = -m;
-                float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                #pragma unroll
-                for (int hlf = 0; hlf < 2; hlf++) {
-                    float v[64];
-                    sm100::tmem_ld64(tS + hlf * 64, v);
-                    uint32_t pk[32];
-                    #pragma unroll
-                    for (int u = 0; u < 32; u++) {
-                        const int k = hlf * 64 + 2 * u;
-                        const float xa = fmaf(v[2 * u], sl, nm), xb = fmaf(v[2 * u + 1], sl, nm);
-                        float a, b;
-                        if (POLY && (u & 3) == 3) { a = ex2_poly(xa); b = ex2_poly(xb); }
-                        else { a = ex2_approx(xa); b = ex2_approx(xb); }
-                        if (!full) { a = (k < kvalid) ? a : 0.f; b = (k + 1 < kvalid) ? b : 0.f; }
-                        ls[u & 7] += a + b;
-                        pk[u] = pack_bf16x2_rn(a, b);
-                    }
-                    tmem_st32u(tS + hlf * 32, pk);
-                }
-                l += sum8(ls);
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                sm100::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) sm100::mbar_arrive(&ctl->p_ready[t]);
-            }
-            if (!ok) break;
-            ok = __all_sync(0xffffffffu, wait_bar(&ctl->pv_done[t], (step - 1) & 1, abort_flag));
-            if (!ok) break;
-            sm100::tc_fence_after();
-            const int q = it.q0 + t * QT + r;
-            const float inv = 1.f / l;
-            const bool is_vid = q < it.f, is_txt = (q >= it.f) && (q < it.S);
-            float* tdst = p.toutw + ((size_t)it.wi * p.g.TXT + (is_txt ? q - it.f : 0)) * 2560 + it.h * D;
-            const size_t tok = is_vid ? (size_t)p.g.vidx[p.g.cumf[it.wi] + q] : 0;
-            #pragma unroll 1
-            for (int c = 0; c < 2; c++) {
-                float o[64];
-                sm100::tmem_ld64(tO + c * 64, o);
-                #pragma unroll
-                for (int u = 0; u < 64; u++) o[u] *= inv;
-                if (is_vid) {
-                    if (p.att_bf16) {
-                        bf16* dst = (bf16*)p.att + tok * p.ld_att + it.h * D + c * 64;
-                        #pragma unroll
-                        for (int u = 0; u < 64; u += 4) store4(dst + u, o + u);
-                    } else {
-                        float* dst = (float*)p.att + tok * p.ld_att + it.h * D + c * 64;
-                        #pragma unroll
-                        for (int u = 0; u < 64; u += 4) store4(dst + u, o + u);
-                    }
-                } else if (is_txt) {
-                    #pragma unroll
-                    for (int u = 0; u < 64; u += 4) store4(tdst + c * 64 + u, o + u);
-                }
-            }
-            // O_t has been read: the next item's first PV may overwrite it
-            sm100::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) sm100::mbar_arrive(&ctl->o_empty[t]);
-        }
-    }
-    sm100::tc_fence_before();
-    __syncthreads();
-    if (warp == 9) {
-        sm100::tc_fence_after();
-        sm100::tmem_dealloc(tmem, 512);
-    }
-}
-
 
 // ---------------------------------------------------------------- 64-key kernel
 // One CTA = one (window, head, 128-query tile), two CTAs per SM, keys in
@@ -1416,8 +807,8 @@ int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, const AwaDev& 
                   ActT at, float* toutw, cudaStream_t s) {
     const int rows = 20 * g.sumS;
     CUtensorMap tq, tk, tv;
-    if (!make_tmap_bf16(&tq, Qp, rows, D, D, QT, 64) || !make_tmap_bf16(&tk, Kp, rows, D, D, KT, 64) ||
-        !make_tmap_bf16(&tv, Vp, rows, D, D, KT, 64))
+    if (!make_tmap_bf16(&tq, Qp, rows, D, D, QT, 64) || !make_tmap_bf16(&tk, Kp, rows, D, D, KT4, 64) ||
+        !make_tmap_bf16(&tv, Vp, rows, D, D, KT4, 64))
         return -1;
     AttnParams p;
     p.g = g;
@@ -1426,34 +817,12 @@ int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, const AwaDev& 
     p.ld_att = ld_att;
     p.att_bf16 = (at == ACT_BF16);
     p.toutw = toutw;
-    if (awa_tc_kernel_version() == 3) {
-        CUtensorMap tk4, tv4;
-        if (!make_tmap_bf16(&tk4, Kp, rows, D, D, KT4, 64) || !make_tmap_bf16(&tv4, Vp, rows, D, D, KT4, 64))
-            return -1;
+    {
         dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
         const int np = awa_tc_poly_exp();
-        if (np == 2) k_awa_attn_tc4<2><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
-        else if (np == 1) k_awa_attn_tc4<1><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
-        else k_awa_attn_tc4<0><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk4, tv4, p);
-    } else if (awa_tc_kernel_version() == 1) {
-        dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
-        if (awa_tc_poly_exp())
-            k_awa_attn_tc<true><<<grid, NUM_THREADS, SMEM_BYTES, s>>>(tq, tk, tv, p);
-        else
-            k_awa_attn_tc<false><<<grid, NUM_THREADS, SMEM_BYTES, s>>>(tq, tk, tv, p);
-    } else {
-        const int maxpairs = (g.maxS + 2 * QT - 1) / (2 * QT);
-        const int items = g.nwin * 20 * maxpairs;
-        static int sms[64] = {0};
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (dev < 64 && sms[dev] == 0) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-        const int nsm = (dev < 64 && sms[dev] > 0) ? sms[dev] : 148;
-        const int grid = items < nsm ? items : nsm;
-        if (awa_tc_poly_exp())
-            k_awa_attn_tc2<true><<<grid, T2_THREADS, T2_SMEM, s>>>(tq, tk, tv, p, maxpairs);
-        else
-            k_awa_attn_tc2<false><<<grid, T2_THREADS, T2_SMEM, s>>>(tq, tk, tv, p, maxpairs);
+        if (np == 2) k_awa_attn_tc4<2><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk, tv, p);
+        else if (np == 1) k_awa_attn_tc4<1><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk, tv, p);
+        else k_awa_attn_tc4<0><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk, tv, p);
     }
     return 0;
 }
@@ -1480,33 +849,18 @@ int awa_attend_split3(const void* Q3, const void* K3, const void* V3, const AwaD
 int awa_tc_init_device() {
     if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_x3, cudaFuncAttributeMaxDynamicSharedMemorySize, X3_SMEM))
         return (int)e;
-    if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES))
-        return (int)e;
-    if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES))
-        return (int)e;
     const void* v4[3] = {(const void*)k_awa_attn_tc4<0>, (const void*)k_awa_attn_tc4<1>,
                          (const void*)k_awa_attn_tc4<2>};
     for (const void* k : v4)
         if (cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, T4_SMEM)) return (int)e;
-    if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_tc2<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, T2_SMEM))
-        return (int)e;
-    return (int)cudaFuncSetAttribute(k_awa_attn_tc2<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, T2_SMEM);
+    return 0;
 }
 
-// S2B_ATTN_POLY=n (0, 1, 2): n of every 4 softmax exponential pairs on the
-// FMA pipe (ex2_poly2 in the 64-key kernel; ex2_poly in the others).
+// S2B_ATTN_POLY=n (0, 1, 2): n of every 4 softmax exponential pairs of the
+// 64-key kernel on the FMA pipe (ex2_poly2).
 int awa_tc_poly_exp() {
     const char* e = std::getenv("S2B_ATTN_POLY");
     return (e && e[0] == '2') ? 2 : (e && e[0] == '1') ? 1 : 0;
-}
-
-// 3 = 64-key tiles, double-buffered K/V, P in TMEM (default);
-// 1 = 128-key tiles, P in shared memory (S2B_ATTN_KERNEL=1);
-// 2 = the persistent two-tile kernel (S2B_ATTN_KERNEL=2).
-// Per 1080p forward (same process, alternating): 3.0-3.3 ms, 3.0-3.6 ms, 4.7-4.8 ms.
-int awa_tc_kernel_version() {
-    const char* e = std::getenv("S2B_ATTN_KERNEL");
-    return (e && e[0] == '2') ? 2 : (e && e[0] == '1') ? 1 : 3;
 }
 
 int awa_tc_error_reset(int* had_error) {
