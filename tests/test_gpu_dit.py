@@ -143,6 +143,28 @@ def test_full_graph_forward_equals_forward_latent(prec):
     c.close()
 
 
+def test_full_graph_forward_1080p_equals_forward_latent():
+    # the 1080p bf16 forward as one CUDA graph (kernels chained by programmatic
+    # dependencies, each waiting on griddepcontrol before it reads) must be
+    # bit-identical to the same kernels launched one by one, and to itself
+    t, h, w, txt_len = 1, 68, 80, 58
+    c = s2b.DitB200(0, s2b.PREC_BF16)
+    try:
+        c.init_synth(1234, 0, 32)
+        c.set_windows(s2b.make_win(t, h, w, (4, 3, 3), txt_len, False),
+                      s2b.make_win(t, h, w, (4, 3, 3), txt_len, True))
+        vp = s2b.patchify_grid(s2b.synth_vid_grid(t, 2 * h, 2 * w, 42))
+        txt = s2b.synth_txt(txt_len, 42)
+        sr_graph = c.forward(vp, h * w, txt, txt_len, 1000.0)
+        sr_graph2 = c.forward(vp, h * w, txt, txt_len, 1000.0)
+        _, _, sr_lat = c.forward_latent(vp, h * w, txt, txt_len, 1000.0, 0, 32, True, True)
+        assert np.isfinite(sr_graph).all()
+        assert np.array_equal(sr_graph, sr_graph2)
+        assert np.array_equal(sr_graph, sr_lat)
+    finally:
+        c.close()
+
+
 def test_weights_from_memory_equal_weights_from_directory(m5_small, inputs):
     """s2b_load_weights_mem with the directory's files in memory gives the
     same model as s2b_load_weights_dir (bit-identical forward)."""
