@@ -679,13 +679,11 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
                         }
                     }
                     // release this stage in both CTAs
-                    sm100::mma_commit_pair(sm100::map_to_rank(&ctl->empty[stage], 0));
-                    sm100::mma_commit_pair(sm100::map_to_rank(&ctl->empty[stage], 1));
+                    sm100::mma_commit_pair_mc(&ctl->empty[stage], 0x3);
                     if (++stage == STAGES2) { stage = 0; phase ^= 1; }
                 }
                 if (ok) {
-                    sm100::mma_commit_pair(sm100::map_to_rank(&ctl->tfull[acc], 0));
-                    sm100::mma_commit_pair(sm100::map_to_rank(&ctl->tfull[acc], 1));
+                    sm100::mma_commit_pair_mc(&ctl->tfull[acc], 0x3);
                 }
             }
         }

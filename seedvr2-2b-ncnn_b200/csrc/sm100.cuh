@@ -246,6 +246,13 @@ __device__ __forceinline__ void mma_tf32_pair(uint32_t d_tmem, uint64_t adesc, u
         ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
         : "memory");
 }
+// Arrive on the mbarrier at the same shared-memory offset in every CTA of
+// `cta_mask` (bit r = cluster rank r) once this thread's prior cta_group::2
+// MMAs are done: one commit instead of one per CTA.
+__device__ __forceinline__ void mma_commit_pair_mc(const void* bar_local, uint16_t cta_mask) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(smem_u32(bar_local)), "h"(cta_mask) : "memory");
+}
 // Arrive on an mbarrier of either CTA of the pair once this thread's prior
 // cta_group::2 MMAs are done.
 __device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
