@@ -573,6 +573,10 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
                const __grid_constant__ TcParams p1, int ngroups) {
     using C = PairCfg<BN, KIND>;
     constexpr int STAGES2 = C::STAGES, A2_BYTES = C::A_BYTES, B2_BYTES = C::B_BYTES, STAGE2_BYTES = C::STAGE_BYTES;
+    // bf16: two consecutive 64-deep k-blocks share one full / empty barrier
+    // pair, so the MMA thread waits and commits once per 8 MMAs
+    constexpr int GRP = KIND == KIND_BF16 ? 2 : 1, NBAR = STAGES2 / GRP;
+    static_assert(STAGES2 % GRP == 0, "stage groups must tile the ring");
     constexpr int ACC = BN;                                 // TMEM columns per accumulator
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -610,44 +614,50 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
 
     if (warp == 0) {
         if (lane == 0) {
-            uint32_t stage = 0, phase = 0;
-            long issued = 0;
+            uint32_t bs = 0, phase = 0;        // barrier stage (GRP consecutive k-blocks each)
+            long issued = 0;                   // barrier stages filled
             bool ok = true;
             for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
                 const TileRef t = tile_ref(p0, p1, tiles0, tile);
                 const CUtensorMap* ta = &maps.a[t.grp];
                 const CUtensorMap* tb = &maps.b[t.grp];
-                for (int kb = 0; kb < num_kb; kb++) {
-                    if (!wait_or_abort(&ctl->empty[stage], phase ^ 1, abort_flag)) { ok = false; break; }
+                for (int kb0 = 0; kb0 < num_kb; kb0 += GRP) {
+                    const int nsub = min(GRP, num_kb - kb0);
+                    if (!wait_or_abort(&ctl->empty[bs], phase ^ 1, abort_flag)) { ok = false; break; }
                     // both CTAs' bytes complete on the even CTA's full barrier
-                    if (rank == 0) sm100::mbar_arrive_expect_tx(&ctl->full[stage], 2 * STAGE2_BYTES);
-                    const uint32_t fb = sm100::map_to_rank(&ctl->full[stage], 0);
+                    if (rank == 0) sm100::mbar_arrive_expect_tx(&ctl->full[bs], nsub * 2 * STAGE2_BYTES);
+                    const uint32_t fb = sm100::map_to_rank(&ctl->full[bs], 0);
                     #pragma unroll
-                    for (int part = 0; part < C::NPART; part++) {
-                        // part 1 (lo) sits K elements to the right of part 0 (hi)
-                        const int x = part * p0.kdim + kb * C::KB;
-                        sm100::tma_load_2d_pair(sA + stage * A2_BYTES + part * C::A_TILE, ta, fb, x,
-                                                t.mb * BM2 + (int)rank * 128);
-                        sm100::tma_load_2d_pair(sB + stage * B2_BYTES + part * C::B_TILE, tb, fb, x,
-                                                t.nb * BN + (int)rank * (BN / 2));
+                    for (int sub = 0; sub < GRP; sub++) {
+                        if (sub >= nsub) break;
+                        const int slot = (int)bs * GRP + sub;
+                        #pragma unroll
+                        for (int part = 0; part < C::NPART; part++) {
+                            // part 1 (lo) sits K elements to the right of part 0 (hi)
+                            const int x = part * p0.kdim + (kb0 + sub) * C::KB;
+                            sm100::tma_load_2d_pair(sA + slot * A2_BYTES + part * C::A_TILE, ta, fb, x,
+                                                    t.mb * BM2 + (int)rank * 128);
+                            sm100::tma_load_2d_pair(sB + slot * B2_BYTES + part * C::B_TILE, tb, fb, x,
+                                                    t.nb * BN + (int)rank * (BN / 2));
+                        }
                     }
                     issued++;
-                    if (++stage == STAGES2) { stage = 0; phase ^= 1; }
+                    if (++bs == NBAR) { bs = 0; phase ^= 1; }
                 }
             }
             if (!ok && rank == 0) {
                 // drain this CTA pair's loads (bounded) before shared memory goes away
-                const long n = issued < STAGES2 ? issued : STAGES2;
+                const long n = issued < NBAR ? issued : NBAR;
                 for (long i = 1; i <= n; i++) {
                     const long k = issued - i;
-                    const uint32_t s = (uint32_t)(k % STAGES2), ph = (uint32_t)((k / STAGES2) & 1);
-                    for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->full[s], ph); w++) {}
+                    const uint32_t b = (uint32_t)(k % NBAR), ph = (uint32_t)((k / NBAR) & 1);
+                    for (uint32_t w = 0; w < sm100::WAIT_LIMIT && !sm100::mbar_try_wait(&ctl->full[b], ph); w++) {}
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
-            uint32_t stage = 0, phase = 0;
+            uint32_t bs = 0, phase = 0;
             int it = 0;
             bool ok = true;
             for (int tile = pair; tile < num_tiles && ok; tile += npairs, it++) {
@@ -656,31 +666,37 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
                 if (!wait_or_abort(&ctl->tempty[acc], acc_phase ^ 1, abort_flag)) { ok = false; break; }
                 sm100::tc_fence_after();
                 const uint32_t d = tmem_base + acc * ACC;
-                for (int kb = 0; kb < num_kb; kb++) {
-                    if (!wait_or_abort(&ctl->full[stage], phase, abort_flag)) { ok = false; break; }
+                for (int kb0 = 0; kb0 < num_kb; kb0 += GRP) {
+                    const int nsub = min(GRP, num_kb - kb0);
+                    if (!wait_or_abort(&ctl->full[bs], phase, abort_flag)) { ok = false; break; }
                     sm100::tc_fence_after();
-                    const uint8_t* a = sA + stage * A2_BYTES;
-                    const uint8_t* b = sB + stage * B2_BYTES;
-                    if constexpr (KIND == KIND_BF16) {
-                        #pragma unroll
-                        for (int kk = 0; kk < BK / 16; kk++)
-                            sm100::mma_bf16_pair(d, sm100::desc_kmajor_sw128(a, kk * 32),
-                                                 sm100::desc_kmajor_sw128(b, kk * 32), C::IDESC, (kb | kk) != 0);
-                    } else {
-                        const uint8_t* al = a + C::A_TILE;
-                        const uint8_t* bl = b + C::B_TILE;
-                        #pragma unroll
-                        for (int kk = 0; kk < C::KB / 8; kk++) {      // 8 tf32 = 32 bytes per k-step
-                            const uint64_t ah = sm100::desc_kmajor_sw128(a, kk * 32);
-                            const uint64_t bh = sm100::desc_kmajor_sw128(b, kk * 32);
-                            sm100::mma_tf32_pair(d, ah, bh, C::IDESC, (kb | kk) != 0);
-                            sm100::mma_tf32_pair(d, ah, sm100::desc_kmajor_sw128(bl, kk * 32), C::IDESC, 1);
-                            sm100::mma_tf32_pair(d, sm100::desc_kmajor_sw128(al, kk * 32), bh, C::IDESC, 1);
+                    #pragma unroll
+                    for (int sub = 0; sub < GRP; sub++) {
+                        if (sub >= nsub) break;
+                        const int kb = kb0 + sub;
+                        const uint8_t* a = sA + ((int)bs * GRP + sub) * A2_BYTES;
+                        const uint8_t* b = sB + ((int)bs * GRP + sub) * B2_BYTES;
+                        if constexpr (KIND == KIND_BF16) {
+                            #pragma unroll
+                            for (int kk = 0; kk < BK / 16; kk++)
+                                sm100::mma_bf16_pair(d, sm100::desc_kmajor_sw128(a, kk * 32),
+                                                     sm100::desc_kmajor_sw128(b, kk * 32), C::IDESC, (kb | kk) != 0);
+                        } else {
+                            const uint8_t* al = a + C::A_TILE;
+                            const uint8_t* bl = b + C::B_TILE;
+                            #pragma unroll
+                            for (int kk = 0; kk < C::KB / 8; kk++) {      // 8 tf32 = 32 bytes per k-step
+                                const uint64_t ah = sm100::desc_kmajor_sw128(a, kk * 32);
+                                const uint64_t bh = sm100::desc_kmajor_sw128(b, kk * 32);
+                                sm100::mma_tf32_pair(d, ah, bh, C::IDESC, (kb | kk) != 0);
+                                sm100::mma_tf32_pair(d, ah, sm100::desc_kmajor_sw128(bl, kk * 32), C::IDESC, 1);
+                                sm100::mma_tf32_pair(d, sm100::desc_kmajor_sw128(al, kk * 32), bh, C::IDESC, 1);
+                            }
                         }
                     }
-                    // release this stage in both CTAs
-                    sm100::mma_commit_pair_mc(&ctl->empty[stage], 0x3);
-                    if (++stage == STAGES2) { stage = 0; phase ^= 1; }
+                    // release these stages in both CTAs (one multicast commit)
+                    sm100::mma_commit_pair_mc(&ctl->empty[bs], 0x3);
+                    if (++bs == NBAR) { bs = 0; phase ^= 1; }
                 }
                 if (ok) {
                     sm100::mma_commit_pair_mc(&ctl->tfull[acc], 0x3);
