@@ -56,13 +56,17 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled during the timed region:
+    the sampler starts before the warm-up, the timed region begins only once
+    its first sample has arrived, and only samples taken between mark_start()
+    and mark_end() are reported."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu: int):
         self.gpu, self.proc, self.lines = gpu, None, []
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
@@ -75,7 +79,18 @@ class Clocks:
 
     def _read(self):
         for ln in self.proc.stdout:
-            self.lines.append(ln.strip())
+            self.lines.append((time.monotonic(), ln.strip()))
+
+    def wait_first(self, timeout_s: float = 5.0):
+        end = time.monotonic() + timeout_s
+        while self.proc and not self.lines and time.monotonic() < end:
+            time.sleep(0.01)
+
+    def mark_start(self):
+        self.t0 = time.monotonic()
+
+    def mark_end(self):
+        self.t1 = time.monotonic()
 
     def stop(self):
         if self.proc:
@@ -86,7 +101,9 @@ class Clocks:
                 self.proc.kill()
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for t, ln in self.lines:
+            if self.t0 is not None and not (self.t0 <= t <= (self.t1 if self.t1 is not None else t)):
+                continue
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
@@ -215,21 +232,24 @@ def run_ours(args):
         fwd = ctx.shard_forward_dev if image else ctx.forward_dev
         fwd(d_vid[j].data_ptr(), Lv, d_txt.data_ptr(), TXT, TIMESTEP, d_sr[j].data_ptr(), stream.cuda_stream)
 
+    clocks = Clocks(local)
+    clocks.start()
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
     launches_per_fwd = ctx.last_launches()
+    clocks.wait_first()
 
-    clocks = Clocks(local)
-    clocks.start()
     barrier()
     torch.cuda.synchronize(dev)
+    clocks.mark_start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
         step(args.warmup + i)
     e1.record(stream)
     torch.cuda.synchronize(dev)
+    clocks.mark_end()
     barrier()
     ms = e0.elapsed_time(e1)
     clk = clocks.stop()
