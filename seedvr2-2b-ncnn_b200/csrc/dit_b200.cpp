@@ -38,6 +38,14 @@ int DitB200::cuda_check(cudaError_t e, const char* what) {
     return e == cudaErrorMemoryAllocation ? ERR_NOMEM : ERR_CUDA;
 }
 
+// Status of everything enqueued on s: a launch-time error of an async call
+// (reported once, by cudaGetLastError) or an execution error (by the sync).
+int DitB200::sync_check(cudaStream_t s, const char* what) {
+    const cudaError_t launch = cudaGetLastError();
+    const cudaError_t exec = cudaStreamSynchronize(s);
+    return cuda_check(launch != cudaSuccess ? launch : exec, what);
+}
+
 int DitB200::create(int device, int precision) {
     if (precision == PREC_FP16) return fail(ERR_UNSUPPORTED, "fp16 operands are not offered on B200; use fp32 (0) or bf16 (2)");
     if (precision != PREC_FP32 && precision != PREC_BF16) return fail(ERR_ARG, "precision must be 0 (fp32) or 2 (bf16)");
@@ -98,7 +106,7 @@ int DitB200::upload_linear(Linear& L, const void* w_src, bool src_f16, const flo
         if (int rc = cuda_check(L.b.ensure((size_t)out * 4), "cudaMalloc(bias)")) return rc;
         if (int rc = cuda_check(cudaMemcpy(L.b.p, bias, (size_t)out * 4, cudaMemcpyHostToDevice), "upload bias")) return rc;
     }
-    return cuda_check(cudaStreamSynchronize(stream_), "weight ingest");
+    return sync_check(stream_, "weight ingest");
 }
 
 namespace {
@@ -285,8 +293,8 @@ int DitB200::load_weights(const char* dir_c, bool synth, uint64_t seed, int lo, 
     if (int rc = cuda_check(temb_in_.ensure(TEMB_IN * 4), "cudaMalloc")) return rc;
     if (int rc = cuda_check(temb_h1_.ensure(DIM * 4), "cudaMalloc")) return rc;
     if (int rc = cuda_check(temb_h2_.ensure(DIM * 4), "cudaMalloc")) return rc;
-    cudaMemcpy(branch_.p, branch.data(), branch.size() * 4, cudaMemcpyHostToDevice);
-    cudaMemcpy(qknorm_.p, qkn.data(), qkn.size() * 4, cudaMemcpyHostToDevice);
+    if (int rc = cuda_check(cudaMemcpy(branch_.p, branch.data(), branch.size() * 4, cudaMemcpyHostToDevice), "upload vectors")) return rc;
+    if (int rc = cuda_check(cudaMemcpy(qknorm_.p, qkn.data(), qkn.size() * 4, cudaMemcpyHostToDevice), "upload vectors")) return rc;
     if (int rc = cuda_check(cudaMemcpy(von_w_.p, von.data(), DIM * 4, cudaMemcpyHostToDevice), "upload vectors")) return rc;
     // shared layers: the txt flow uses the same Linear objects
     layer_lo_ = lo; layer_hi_ = hi;
@@ -313,7 +321,7 @@ int DitB200::prepare_tf32x3() {
         for (auto& B : row)
             for (Linear* L : {&B.qkv, &B.out, &B.mlp_hg, &B.mlp_out})
                 if (int rc = split(*L)) return rc;
-    return cuda_check(cudaStreamSynchronize(stream_), "tf32 weight split");
+    return sync_check(stream_, "tf32 weight split");
 }
 
 // ------------------------------------------------------------------ geometry
@@ -800,7 +808,7 @@ int DitB200::forward_latent(const float* vid_in, int Lv, const float* txt_in, in
     }
     last_launches_ = launches_;
     if (int rc = cuda_check(cudaGetLastError(), "kernel launch")) return rc;
-    return cuda_check(cudaStreamSynchronize(s), "forward_latent");
+    return sync_check(s, "forward_latent");
 }
 
 int DitB200::capture_full(int Lv, int TXT) {
@@ -904,7 +912,7 @@ int DitB200::forward(const float* vid_patch, int Lv, const float* txt, int TXT, 
     cudaGraphLaunch(gexec_, stream_);
     cudaMemcpyAsync(sr_out, SR_.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToHost, stream_);
     last_launches_ = graph_launches_;
-    return cuda_check(cudaStreamSynchronize(stream_), "forward");
+    return sync_check(stream_, "forward");
 }
 
 int DitB200::time_embedding(float t, float* emb_host) {
@@ -915,7 +923,7 @@ int DitB200::time_embedding(float t, float* emb_host) {
     cudaMemcpyAsync(temb_in_.p, temb, sizeof temb, cudaMemcpyHostToDevice, stream_);
     enqueue_temb(stream_);
     cudaMemcpyAsync(emb_host, emb_.p, EMB_DIM * 4, cudaMemcpyDeviceToHost, stream_);
-    return cuda_check(cudaStreamSynchronize(stream_), "time_embedding");
+    return sync_check(stream_, "time_embedding");
 }
 
 int DitB200::linear(const float* x, int M, int K, const float* W, int N, const float* bias, float* y) {
@@ -977,7 +985,7 @@ int DitB200::ada_compose(const float* emb_host, float* out_host) {
     cudaMemcpyAsync(emb_.p, emb_host, EMB_DIM * 4, cudaMemcpyHostToDevice, stream_);
     s2b::ada_compose(emb_.as<float>(), branch_.as<float>(), NUM_LAYERS * 12 + 2, ada_.as<float>(), stream_);
     cudaMemcpyAsync(out_host, ada_.p, (size_t)(NUM_LAYERS * 12 + 2) * DIM * 4, cudaMemcpyDeviceToHost, stream_);
-    return cuda_check(cudaStreamSynchronize(stream_), "ada_compose");
+    return sync_check(stream_, "ada_compose");
 }
 
 // ------------------------------------------------------------------ AWA operator
@@ -1016,7 +1024,7 @@ int DitB200::awa_run(GeomDev& G, const float* vqkv, const float* tqkv, const flo
     awa_coalesce(tw.as<float>(), G.view.nwin, TXT, txt_out, DIM, ACT_F32, user);
     if ((rc = cuda_check(cudaGetLastError(), "awa launch"))) return rc;
     // the scratch buffers above must outlive the enqueued kernels
-    return cuda_check(cudaStreamSynchronize(user), "awa");
+    return sync_check(user, "awa");
 }
 
 int DitB200::awa_forward_dev(int win_type, const float* vqkv, const float* tqkv, const float* nqv, const float* nkv,
@@ -1085,7 +1093,7 @@ int DitB200::awa_forward(const float* vqkv, const float* tqkv, const WinGeom& wi
     if (rc) return rc;
     cudaMemcpyAsync(vid_out, dvo.p, (size_t)Lv * DIM * 4, cudaMemcpyDeviceToHost, stream_);
     cudaMemcpyAsync(txt_out, dto.p, (size_t)TXT * DIM * 4, cudaMemcpyDeviceToHost, stream_);
-    return cuda_check(cudaStreamSynchronize(stream_), "awa_forward");
+    return sync_check(stream_, "awa_forward");
 }
 
 }  // namespace s2b

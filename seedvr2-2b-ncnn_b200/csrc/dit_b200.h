@@ -151,6 +151,7 @@ public:
 private:
     int fail(int code, const std::string& m) { err = m; return code; }
     int cuda_check(cudaError_t e, const char* what);
+    int sync_check(cudaStream_t s, const char* what);
     int upload_linear(Linear& L, const void* w_src, bool src_f16, const float* bias, int out, int in, ActT t,
                       int ld, int interleave_role);
     int ensure_acts(int Lv, int TXT);
