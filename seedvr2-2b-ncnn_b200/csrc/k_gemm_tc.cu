@@ -10,21 +10,23 @@
 // kernel is shared-memory-bandwidth bound (ncu: L1TEX ~80 % busy, tensor
 // pipe ~35 %).  Roles per CTA:
 //   warp 0      TMA producer: 6-stage ring of [A 128x64 | B 128x64] tiles
-//               (128-byte swizzle); both CTAs' loads complete on the even
-//               CTA's full barrier;
+//               (128-byte swizzle), two consecutive stages per full / empty
+//               barrier (bf16); both CTAs' loads complete on the even CTA's
+//               full barrier;
 //   warp 1      allocates 512 TMEM columns in both CTAs (two 256-column
 //               accumulators); in the even CTA one thread issues
-//               tcgen05.mma.cta_group::2 (M=256, N=256, K=16) and commits
-//               stage releases / accumulator hand-offs to the barriers of
-//               BOTH CTAs (one commit each, no multicast);
+//               tcgen05.mma.cta_group::2 (M=256, N=256, K=16), 8 per barrier
+//               group, and signals stage releases / accumulator hand-offs to
+//               the same barrier in BOTH CTAs with one tcgen05.commit
+//               .multicast::cluster (a barrier arrival, not a data load);
 //   warps 2-5   epilogue on this CTA's 128 accumulator rows: tcgen05.ld 32
 //               lanes x 32 columns, fused bias / adaLN gate + fp32 residual /
 //               SwiGLU, direct stores; then release the accumulator to the
 //               even CTA's MMA thread.
 // Single kernel (M <= 128: the 58-row txt Linears of layers 0..9): one CTA
 // per 128x256 tile, 4-stage ring, same roles within one CTA.
-// All loads are plain TMA tile loads of this GPU's memory (no cluster
-// multicast).  Every mbarrier wait is bounded; on expiry a kernel records
+// All loads are plain TMA tile loads of this GPU's memory (no load with
+// cluster multicast).  Every mbarrier wait is bounded; on expiry a kernel records
 // g_tc_err, drains its own TMA loads (bounded), frees TMEM and returns.
 // Warp-collective TMEM instructions run only under warp-uniform control flow.
 #include "kernels.h"
