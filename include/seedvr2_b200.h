@@ -15,7 +15,17 @@
  *     "_dev" entry points take device pointers and a cudaStream_t (passed as
  *     void*) and only enqueue (the ncnn custom-layer semantics: record on the
  *     caller's command stream);
- *   - inputs are never retained; outputs are caller-owned.
+ *   - inputs are never retained; outputs are caller-owned;
+ *   - S2B_ERR_TIMEOUT: every wait inside the tensor-core kernels and the
+ *     multi-GPU exchanges is bounded; one that expires makes its kernel return
+ *     early (the output of that call is incomplete) and raises a device flag.
+ *     The last kernel of every call folds those flags into the context's
+ *     status word.  Host-buffer calls read it after their final
+ *     synchronisation and return S2B_ERR_TIMEOUT; "_dev" calls cannot report
+ *     at return, so read it with s2b_check_errors after the work finished
+ *     (the next host-buffer call on the context reports it too).  The flags
+ *     are per device: a context may see an expiry of another context's
+ *     kernels on the same device.
  * Layouts are the reference's: fp32, row-major, token index ((t*H)+h)*W+w,
  * qkv rows [q(20x128) | k | v] (src/awa_vk.h:36), patches (ph,pw,c).
  */
@@ -258,10 +268,18 @@ int s2b_group_forward_frames(s2b_group* group, const float* vid_patches, int nfr
                              int TXT, float timestep, float* sr_out);
 
 /* Window-sharded image mode: one rank per GPU; each rank owns a subset of
- * the windows of every layer, txt rows are replicated, and the txt partial
- * sums of the attention are summed across ranks with one NCCL all-reduce
- * per layer.  `nccl_id` is the 128-byte ncclUniqueId created by rank 0 and
- * shared over any host channel. */
+ * the windows of every layer, txt rows are replicated, and per layer the txt
+ * partial sums of the attention and the residual rows that change owner are
+ * exchanged over NVLink peer memory by this library's kernels (NCCL calls
+ * when peers cannot map each other's memory, or S2B_SHARD_P2P=0).
+ * `nccl_id` is the 128-byte ncclUniqueId created by rank 0 and shared over
+ * any host channel.  Every rank calls every shard entry point in the same
+ * order.  Peer waits are bounded by S2B_SHARD_WAIT_MS (default 4000): a rank
+ * that waits longer, or that sees a peer running a later call, returns
+ * S2B_ERR_TIMEOUT; on the NCCL path a host watchdog aborts the communicator
+ * after the same bound (then s2b_shard_init must run again).  After a failed
+ * shard call on ANY rank, every rank calls s2b_shard_resync before the next
+ * forward. */
 int s2b_nccl_unique_id(uint8_t nccl_id[128]);
 int s2b_shard_init(s2b_ctx* ctx, const uint8_t nccl_id[128], int world, int rank);
 int s2b_shard_forward(s2b_ctx* ctx, const float* vid_patch, int Lv, const float* txt, int TXT,
@@ -270,6 +288,11 @@ int s2b_shard_forward(s2b_ctx* ctx, const float* vid_patch, int Lv, const float*
  * every rank passes the whole vid_patch / txt and receives the whole sr. */
 int s2b_shard_forward_dev(s2b_ctx* ctx, const float* d_vid_patch, int Lv, const float* d_txt, int TXT,
                           float timestep, float* d_sr, void* stream);
+/* Collective over the ranks of s2b_shard_init: agree on the number of the
+ * next shard forward (the highest any rank has used), so that the flag values
+ * of the peer exchanges match again after a call failed on some rank.  No
+ * reference counterpart (the reference is single-device). */
+int s2b_shard_resync(s2b_ctx* ctx);
 /* The ownership and exchange plan rank `rank` of `world` uses (host only, no
  * context).  Parity p = 0 is the non-shifted windows (even layers), p = 1 the
  * shifted ones (odd layers).  Outputs (any may be null):
@@ -288,6 +311,28 @@ int s2b_shard_forward_profile(s2b_ctx* ctx, const float* vid_patch, int Lv, cons
                               float timestep, double* ms, double* flops, double* bytes, int* launches);
 int s2b_shard_plan(const s2b_win* ns, const s2b_win* sh, int world, int rank, int* bounds, int* n_local,
                    int* tokens, int* send_off, int* send_idx, int* recv_off, int* recv_idx);
+
+/* Status of the "_dev" calls enqueued so far: waits for the context's own
+ * stream, then returns S2B_ERR_TIMEOUT (and clears the status) if a bounded
+ * wait expired in any of them since the last report, else S2B_OK.  Calls that
+ * run on the caller's stream (s2b_awa_forward_dev, s2b_awa_forward_dev_static,
+ * s2b_linear_bf16_dev) must be complete first (synchronise that stream).  The
+ * reference reports failures of its GPU work through the return value of each
+ * synchronous call (src/awa_vk.cpp:182, src/dit_vk.cpp:27-45); this is the
+ * same report for the stream-ordered form. */
+int s2b_check_errors(s2b_ctx* ctx);
+
+/* Test hooks (no reference counterpart).  s2b_debug_raise_kernel_error raises
+ * the device flags an expired wait raises (mask: 1 GEMM, 2 attention, 4 peer
+ * exchange) from a one-thread kernel; the next call on the device reports
+ * S2B_ERR_TIMEOUT.  s2b_debug_watchdog_selftest runs the NCCL-path watchdog
+ * against simulated work on the host only (scenario 0: finishes after a few
+ * polls; 1: never finishes; 2: the communicator reports an asynchronous error;
+ * 3: the stream fails), with `timeout_ms`; it returns the watchdog's result
+ * (0 done, 1 async error, 2 expired, 3 stream error) and reports the polls
+ * made and whether the communicator would have been aborted. */
+int s2b_debug_raise_kernel_error(s2b_ctx* ctx, int mask);
+int s2b_debug_watchdog_selftest(int scenario, int timeout_ms, int* polls, int* aborted);
 
 #ifdef __cplusplus
 }

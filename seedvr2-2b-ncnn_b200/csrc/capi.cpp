@@ -325,6 +325,39 @@ int s2b_shard_forward_dev(s2b_ctx* ctx, const float* d_vid_patch, int Lv, const 
     return ctx->dit.shard_forward_dev(d_vid_patch, Lv, d_txt, TXT, t, d_sr, (cudaStream_t)stream);
 }
 
+int s2b_shard_resync(s2b_ctx* ctx) {
+    if (!ctx) return S2B_ERR_ARG;
+    return ctx->dit.shard_resync();
+}
+
+int s2b_check_errors(s2b_ctx* ctx) {
+    if (!ctx) return S2B_ERR_ARG;
+    return ctx->dit.check_errors();
+}
+
+int s2b_debug_raise_kernel_error(s2b_ctx* ctx, int mask) {
+    if (!ctx) return S2B_ERR_ARG;
+    return ctx->dit.debug_raise_kernel_error(mask);
+}
+
+int s2b_debug_watchdog_selftest(int scenario, int timeout_ms, int* polls, int* aborted) {
+    if (scenario < 0 || scenario > 3 || timeout_ms <= 0) return -1;
+    int n = 0, ab = 0;
+    const int r = s2b::watch_completion(
+        [&] {
+            n++;
+            if (scenario == 0 && n >= 4) return (int)s2b::WATCH_Q_DONE;
+            if (scenario == 3 && n >= 3) return (int)s2b::WATCH_Q_ERROR;
+            return (int)s2b::WATCH_Q_PENDING;
+        },
+        [&] { return scenario == 2 && n >= 2; },
+        [&] { ab++; },
+        (uint64_t)timeout_ms * 1000000ull, 1000000ull);
+    if (polls) *polls = n;
+    if (aborted) *aborted = ab;
+    return r;
+}
+
 int s2b_shard_plan(const s2b_win* ns, const s2b_win* sh, int world, int rank, int* bounds, int* n_local,
                    int* tokens, int* send_off, int* send_idx, int* recv_off, int* recv_idx) {
     s2b::WinGeom a, b;

@@ -64,7 +64,41 @@ int DitB200::create(int device, int precision) {
     attn_split3_ = act_ == ACT_F32 && !(aenv && aenv[0] == 's');
     if (int rc = cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate")) return rc;
     if (kernels_init_device() != 0) return fail(ERR_CUDA, "kernel attribute setup failed");
-    return OK;
+    if (int rc = cuda_check((cudaError_t)kernel_flags_get(&kflags_), "kernel error flags")) return rc;
+    if (int rc = cuda_check(status_.ensure(16), "cudaMalloc(status)")) return rc;
+    return cuda_check(cudaMemset(status_.p, 0, 16), "status init");
+}
+
+int DitB200::take_status(cudaStream_t s, const char* what) {
+    int st = 0;
+    cudaError_t e = cudaMemcpyAsync(&st, status_.p, sizeof st, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e == cudaSuccess && st) {
+        e = cudaMemsetAsync(status_.p, 0, sizeof st, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    }
+    if (int rc = cuda_check(e, "kernel status read")) return rc;
+    if (!st) return OK;
+    std::string m = std::string(what) + ": a bounded wait expired in";
+    if (st & KERR_GEMM) m += " the tcgen05 GEMM";
+    if (st & KERR_ATTN) m += (st & KERR_GEMM) ? ", the tcgen05 attention" : " the tcgen05 attention";
+    if (st & KERR_SHARD) m += (st & (KERR_GEMM | KERR_ATTN)) ? ", a peer-memory exchange" : " a peer-memory exchange";
+    return fail(ERR_TIMEOUT, m + "; the output of that call is incomplete");
+}
+
+int DitB200::check_errors() {
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    cudaSetDevice(dev_);
+    if (int rc = shard_wait("check_errors", shard_ != nullptr)) return rc;
+    return take_status(stream_, "an earlier stream-ordered call");
+}
+
+int DitB200::debug_raise_kernel_error(int mask) {
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    if (mask & ~(KERR_GEMM | KERR_ATTN | KERR_SHARD)) return fail(ERR_ARG, "mask must combine 1 (GEMM), 2 (attention), 4 (exchange)");
+    cudaSetDevice(dev_);
+    status_raise(kflags_, mask, stream_);
+    return sync_check(stream_, "debug_raise_kernel_error");
 }
 
 uint64_t DitB200::device_bytes() const {
@@ -655,9 +689,9 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
         if (awa_attend_split3(B.Qp, B.Kp, B.Vp, G.view, 1.0f / sqrtf((float)HEAD_D), att, DIM, act_, B.TOUTW, s))
             return fail(ERR_CUDA, "fp32 tensor-core attention: tensor maps could not be encoded");
         launches_++;
-    } else {
-        awa_attend(B.Qp, B.Kp, B.Vp, act_, G.view, 1.0f / sqrtf((float)HEAD_D), att, DIM, act_, B.TOUTW, s,
-                   &launches_);
+    } else if (awa_attend(B.Qp, B.Kp, B.Vp, act_, G.view, 1.0f / sqrtf((float)HEAD_D), att, DIM, act_, B.TOUTW, s,
+                          &launches_)) {
+        return fail(ERR_CUDA, "bf16 tensor-core attention: tensor maps could not be encoded");
     }
     pend(s);
     pbeg(KK_OTHER, 0, (double)G.view.nwin * TXT * DIM * 4 + (double)TXT * DIM * ab, s);
@@ -799,8 +833,9 @@ int DitB200::forward_latent(const float* vid_in, int Lv, const float* txt_in, in
     }
     enqueue_temb(s);
     for (int i = l0; i < l1; i++) enqueue_layer(i, Lv, TXT, s);
+    if (do_final) enqueue_final(Lv, s);
+    fold_status(s);
     if (do_final) {
-        enqueue_final(Lv, s);
         cudaMemcpyAsync(sr_out, SR_.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToHost, s);
     } else {
         cudaMemcpyAsync(vid_lat, X_.p, (size_t)Lv * DIM * 4, cudaMemcpyDeviceToHost, s);
@@ -808,7 +843,8 @@ int DitB200::forward_latent(const float* vid_in, int Lv, const float* txt_in, in
     }
     last_launches_ = launches_;
     if (int rc = cuda_check(cudaGetLastError(), "kernel launch")) return rc;
-    return sync_check(s, "forward_latent");
+    if (int rc = sync_check(s, "forward_latent")) return rc;
+    return take_status(s, "forward_latent");
 }
 
 int DitB200::capture_full(int Lv, int TXT) {
@@ -821,6 +857,7 @@ int DitB200::capture_full(int Lv, int TXT) {
     enqueue_temb(stream_);
     for (int i = 0; i < NUM_LAYERS; i++) enqueue_layer(i, Lv, TXT, stream_);
     enqueue_final(Lv, stream_);
+    fold_status(stream_);
     cudaError_t ce = cudaStreamEndCapture(stream_, &graph);
     if (int rc = cuda_check(ce, "end capture")) return rc;
     ce = cudaGraphInstantiate(&gexec_, graph, 0);
@@ -912,7 +949,8 @@ int DitB200::forward(const float* vid_patch, int Lv, const float* txt, int TXT, 
     cudaGraphLaunch(gexec_, stream_);
     cudaMemcpyAsync(sr_out, SR_.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToHost, stream_);
     last_launches_ = graph_launches_;
-    return sync_check(stream_, "forward");
+    if (int rc = sync_check(stream_, "forward")) return rc;
+    return take_status(stream_, "forward");
 }
 
 int DitB200::time_embedding(float t, float* emb_host) {
@@ -958,11 +996,10 @@ int DitB200::linear(const float* x, int M, int K, const float* W, int N, const f
     }
     GemmEpi e; e.mode = EPI_STORE; e.bias = L.bias(); e.out = dy.p; e.ldo = N; e.out_t = ACT_F32;
     gemm(dxa.p, ld, L, M, e, stream_);
+    fold_status(stream_);
     cudaMemcpyAsync(y, dy.p, (size_t)M * N * 4, cudaMemcpyDeviceToHost, stream_);
-    if ((rc = cuda_check(cudaStreamSynchronize(stream_), "linear"))) return rc;
-    int had = 0;
-    if (act_ == ACT_BF16 && gemm_tc_error_reset(&had) == 0 && had) return fail(ERR_TIMEOUT, "tcgen05 GEMM wait expired");
-    return OK;
+    if ((rc = sync_check(stream_, "linear"))) return rc;
+    return take_status(stream_, "linear");
 }
 
 int DitB200::linear_bf16_dev(const void* x, int M, int K, const void* W, int N, const float* bias, void* y,
@@ -976,6 +1013,7 @@ int DitB200::linear_bf16_dev(const void* x, int M, int K, const void* W, int N, 
     GemmEpi e;
     e.mode = EPI_STORE; e.bias = bias; e.out = y; e.ldo = N; e.out_t = ACT_BF16;
     if (gemm_tc(x, K, W, K, M, N, K, e, s, &launches_)) return fail(ERR_UNSUPPORTED, "tcgen05 GEMM launch rejected");
+    fold_status(s);
     return cuda_check(cudaGetLastError(), "linear_bf16_dev");
 }
 
@@ -1018,13 +1056,16 @@ int DitB200::awa_run(GeomDev& G, const float* vqkv, const float* tqkv, const flo
             return fail(ERR_CUDA, "fp32 tensor-core attention: tensor maps could not be encoded");
     } else {
         awa_pack(vqkv, tqkv, ACT_F32, QKV, G.view, nqv, nkv, nqt, nkt, eps, q.p, k.p, v.p, act_, user);
-        awa_attend(q.p, k.p, v.p, act_, G.view, 1.0f / sqrtf((float)HEAD_D), vid_out, DIM, ACT_F32, tw.as<float>(),
-                   user, nullptr);
+        if (awa_attend(q.p, k.p, v.p, act_, G.view, 1.0f / sqrtf((float)HEAD_D), vid_out, DIM, ACT_F32, tw.as<float>(),
+                       user, nullptr))
+            return fail(ERR_CUDA, "bf16 tensor-core attention: tensor maps could not be encoded");
     }
     awa_coalesce(tw.as<float>(), G.view.nwin, TXT, txt_out, DIM, ACT_F32, user);
+    fold_status(user);
     if ((rc = cuda_check(cudaGetLastError(), "awa launch"))) return rc;
     // the scratch buffers above must outlive the enqueued kernels
-    return sync_check(user, "awa");
+    if ((rc = sync_check(user, "awa"))) return rc;
+    return take_status(user, "awa");
 }
 
 int DitB200::awa_forward_dev(int win_type, const float* vqkv, const float* tqkv, const float* nqv, const float* nkv,
@@ -1061,7 +1102,9 @@ int DitB200::awa_forward_dev_static(int win_type, const float* vqkv, const float
     const int rc = awa_forward_static(vqkv, tqkv, G.view, nqv, nkv, nqt, nkt, eps, 1.0f / sqrtf((float)HEAD_D), act_,
                                       vid_out, txt_out, user);
     if (rc == -1) return fail(ERR_ARG, "geometry does not fit the static scratch");
+    if (rc == -2) return fail(ERR_CUDA, "bf16 tensor-core attention: tensor maps could not be encoded");
     if (rc) return cuda_check((cudaError_t)rc, "static scratch address");
+    fold_status(user);
     return cuda_check(cudaGetLastError(), "awa_forward_dev_static");
 }
 

@@ -6,6 +6,7 @@
 #include "awa_geometry.h"
 #include "kernels.h"
 #include "shard_plan.h"
+#include "watchdog.h"
 #include <cuda_runtime.h>
 #include <string>
 #include <vector>
@@ -137,6 +138,14 @@ public:
                                const float* nkv, const float* nqt, const float* nkt, int Lv, int TXT, float eps,
                                float* vid_out, float* txt_out, cudaStream_t user);
 
+    // Status of the stream-ordered (*_dev) calls: synchronises the context's
+    // stream, then reports (and clears) the kernel error bits that the
+    // forwards folded into the context's status word since the last report.
+    int check_errors();
+    // Test hook: raises the kernel error flags named by mask (KernelErrBit)
+    // on the device, as an expired bounded wait would.
+    int debug_raise_kernel_error(int mask);
+
     int precision() const { return prec_; }
     uint64_t device_bytes() const;
     int last_launches() const { return last_launches_; }
@@ -147,9 +156,18 @@ public:
     int shard_forward(const float* vid_patch, int Lv, const float* txt, int TXT, float t, float* sr_out);
     int shard_forward_dev(const float* d_vid_patch, int Lv, const float* d_txt, int TXT, float t, float* d_sr,
                           cudaStream_t user);
+    // Collective (every rank calls it): agree on the shard-forward call number
+    // after a failed call on any rank, so the ranks' flag values match again.
+    int shard_resync();
 
 private:
     int fail(int code, const std::string& m) { err = m; return code; }
+    // Enqueue the fold of the device's kernel error flags into status_ (after
+    // the kernels it covers, on the same stream).
+    void fold_status(cudaStream_t s) { status_fold(kflags_, status_.as<int>(), s); launches_++; }
+    // With s idle: read and clear status_; ERR_TIMEOUT naming the kernel
+    // classes whose bounded waits expired, else OK.
+    int take_status(cudaStream_t s, const char* what);
     int cuda_check(cudaError_t e, const char* what);
     int sync_check(cudaStream_t s, const char* what);
     int upload_linear(Linear& L, const void* w_src, bool src_f16, const float* bias, int out, int in, ActT t,
@@ -176,6 +194,8 @@ private:
     int shard_enqueue(cudaStream_t s);
     int shard_exchange(int p, cudaStream_t s);
     int shard_capture();
+    int shard_begin_call();
+    int shard_wait(const char* what, bool nccl_in_flight);
     int shard_setup_peers(const ShardPlan& plan, int n0, int n1, int TXT);
     cudaStream_t capture_stream() const { return stream_; }
     const float* ada(int layer, int flow, int k) const {
@@ -186,6 +206,8 @@ private:
     }
 
     int dev_ = -1, prec_ = PREC_FP32;
+    DevBuf status_;         // int: KernelErrBit of every expired wait not yet reported
+    KernelFlags kflags_;    // this device's kernel error flags
     ActT act_ = ACT_F32;
     cudaStream_t stream_ = nullptr;
     bool weights_ = false;

@@ -51,6 +51,8 @@ const NcclLib* nccl_lib(std::string* err) {
         sym(lib.GroupEnd, "ncclGroupEnd");
         sym(lib.AllGather, "ncclAllGather");
         sym(lib.GetErrorString, "ncclGetErrorString");
+        sym(lib.CommGetAsyncError, "ncclCommGetAsyncError");
+        sym(lib.CommAbort, "ncclCommAbort");
         if (!ok) {
             load_err = "the NCCL library lacks an entry point this build needs";
             dlclose(h);
@@ -97,6 +99,12 @@ int DitB200::shard_init(const uint8_t id[128], int world, int rank) {
     shard_.reset();
     auto S = std::make_unique<ShardState>();
     S->world = world; S->rank = rank; S->nl = nl; S->dev = dev_;
+    // S2B_SHARD_WAIT_MS: bound of every peer-flag wait and of the NCCL-path
+    // watchdog (default 4000 ms; a 1080p forward takes ~20 ms)
+    if (const char* w = std::getenv("S2B_SHARD_WAIT_MS")) {
+        const long ms = std::strtol(w, nullptr, 10);
+        if (ms > 0) S->wait_ns = (uint64_t)ms * 1000000ull;
+    }
     ncclUniqueId uid;
     static_assert(sizeof(uid.internal) == 128, "ncclUniqueId is 128 bytes");
     std::memcpy(uid.internal, id, 128);
@@ -247,14 +255,15 @@ int DitB200::shard_setup_peers(const ShardPlan& plan, int n0, int n1, int TXT) {
     if ((rc = cuda_check(S.EPOCH.ensure(16), "cudaMalloc(shard epoch)"))) return rc;
     cudaMemset(S.FLAGS.p, 0, S.FLAGS.bytes);
     cudaMemset(S.EPOCH.p, 0, S.EPOCH.bytes);
-    // this rank's 4 handles (TXTP, FLAGS, X[0], X[1]) + whether it wants peer mode
-    struct Rec { cudaIpcMemHandle_t h[4]; int want; int pad[15]; };
+    // this rank's 5 handles (TXTP, FLAGS, X[0], X[1], SRFULL) + whether it wants peer mode
+    constexpr int NH = 5;
+    struct Rec { cudaIpcMemHandle_t h[NH]; int want; int pad[15]; };
     static_assert(sizeof(Rec) % 16 == 0, "record size");
     Rec mine;
     std::memset(&mine, 0, sizeof mine);
     mine.want = want ? 1 : 0;
-    void* bases[4] = {S.TXTP.p, S.FLAGS.p, S.X[0].p, S.X[1].p};
-    for (int k = 0; k < 4 && mine.want; k++)
+    void* bases[NH] = {S.TXTP.p, S.FLAGS.p, S.X[0].p, S.X[1].p, S.SRFULL.p};
+    for (int k = 0; k < NH && mine.want; k++)
         if (cudaIpcGetMemHandle(&mine.h[k], bases[k]) != cudaSuccess) mine.want = 0;
     cudaGetLastError();
     DevBuf dev_recs;
@@ -272,10 +281,10 @@ int DitB200::shard_setup_peers(const ShardPlan& plan, int n0, int n1, int TXT) {
     for (const Rec& r : recs) all = all && r.want;
     int ok = all ? 1 : 0;
     ShardPeers P;
-    P.world = S.world; P.rank = S.rank;
+    P.world = S.world; P.rank = S.rank; P.wait_ns = S.wait_ns;
     for (int q = 0; q < S.world && ok; q++) {
-        void* ptr[4];
-        for (int k = 0; k < 4; k++) {
+        void* ptr[NH];
+        for (int k = 0; k < NH; k++) {
             if (q == S.rank) { ptr[k] = bases[k]; continue; }
             if (cudaIpcOpenMemHandle(&ptr[k], recs[q].h[k], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
                 cudaGetLastError();
@@ -287,6 +296,7 @@ int DitB200::shard_setup_peers(const ShardPlan& plan, int n0, int n1, int TXT) {
         if (!ok) break;
         P.txtp[q] = (float*)ptr[0]; P.flags[q] = (uint32_t*)ptr[1];
         P.x[0][q] = (float*)ptr[2]; P.x[1][q] = (float*)ptr[3];
+        P.sr[q] = (float*)ptr[4];
     }
     // every rank must have mapped every peer
     DevBuf dev_ok;
@@ -382,7 +392,6 @@ int DitB200::shard_enqueue(cudaStream_t s) {
     const int TXT = S.TXT, n0 = S.plan.n_local(0);
     launches_ = 0;
     S.act = act_;
-    if (S.p2p) { shard_epoch_inc(S.EPOCH.as<uint32_t>(), s); launches_++; }
     // vid_in (this rank's patches of the layer-0 layout) and txt_in, src/dit_vk.cpp:494-497
     copy_rows_f32(S.VIDIN.as<float>(), PATCH_IN, S.tok0.as<int>(), S.VIDLOC.as<float>(), PATCH_IN, nullptr, n0,
                   PATCH_IN, s);
@@ -425,19 +434,85 @@ int DitB200::shard_enqueue(cudaStream_t s) {
     launches_++;
     GemmEpi f; f.mode = EPI_STORE; f.out_t = ACT_F32; f.ldo = OUT_CH; f.bias = vid_out_.bias(); f.out = S.SRLOC.p;
     gemm(S.Xn.p, DIM, vid_out_, nl, f, s);
+    if (S.p2p) {
+        // every rank stores its rows into every rank's output (bounded flag wait)
+        shard_gather_sr(S.peers, S.SRLOC.as<float>(), S.tok1.as<int>(), nl, S.EPOCH.as<uint32_t>(), s);
+        launches_ += 2;
+        fold_status(s);
+        return OK;
+    }
     cudaMemsetAsync(S.SRFULL.p, 0, (size_t)S.Lv * OUT_CH * 4, s);
     copy_rows_f32(S.SRLOC.as<float>(), OUT_CH, nullptr, S.SRFULL.as<float>(), OUT_CH, S.tok1.as<int>(), nl, OUT_CH, s);
     launches_++;
-    return S.nccl_check(S.nl->AllReduce(S.SRFULL.p, S.SRFULL.p, (size_t)S.Lv * OUT_CH, ncclFloat32, ncclSum, S.comm, s),
-                        "ncclAllReduce(sr)", err);
+    const int rc = S.nccl_check(S.nl->AllReduce(S.SRFULL.p, S.SRFULL.p, (size_t)S.Lv * OUT_CH, ncclFloat32, ncclSum,
+                                                S.comm, s), "ncclAllReduce(sr)", err);
+    fold_status(s);
+    return rc;
+}
+
+// Waits for the context's stream.  On the NCCL path a peer that stops leaves
+// an NCCL kernel waiting for good, so the wait is a watchdog: it polls the
+// stream and the communicator's asynchronous error, and after S.wait_ns (or on
+// an NCCL error) aborts the communicator, which ends the NCCL kernels; the
+// shard state then needs shard_init again.
+int DitB200::shard_wait(const char* what, bool nccl_in_flight) {
+    ShardState* S = shard_.get();
+    if (!S || !nccl_in_flight || !S->comm) return sync_check(stream_, what);
+    ncclResult_t async_r = ncclSuccess;
+    const int r = watch_completion(
+        [&] {
+            const cudaError_t e = cudaStreamQuery(stream_);
+            return e == cudaSuccess ? WATCH_Q_DONE : e == cudaErrorNotReady ? WATCH_Q_PENDING : WATCH_Q_ERROR;
+        },
+        [&] { return S->nl->CommGetAsyncError(S->comm, &async_r) == ncclSuccess && async_r != ncclSuccess; },
+        [&] {
+            S->nl->CommAbort(S->comm);
+            S->comm = nullptr;
+            S->aborted = true;
+        },
+        S->wait_ns, 200000ull);
+    if (r == WATCH_DONE) return sync_check(stream_, what);
+    if (r == WATCH_STREAM_ERROR) return sync_check(stream_, what);
+    cudaStreamSynchronize(stream_);   // the abort ended the NCCL kernels
+    cudaGetLastError();
+    return fail(r == WATCH_ASYNC_ERROR ? ERR_NCCL : ERR_TIMEOUT,
+                std::string(what) + (r == WATCH_ASYNC_ERROR ? ": NCCL reported an asynchronous error"
+                                                            : ": the NCCL exchange did not finish in time") +
+                    "; the communicator was aborted (call shard_init again)");
+}
+
+int DitB200::shard_begin_call() {
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    if (!shard_) return fail(ERR_STATE, "shard_init has not run");
+    shard_->calls++;     // counted before any check: a failed call still uses its number
+    if (shard_->aborted) return fail(ERR_STATE, "the communicator was aborted by the watchdog: call shard_init again");
+    return OK;
+}
+
+int DitB200::shard_resync() {
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    if (!shard_ || !shard_->comm) return fail(ERR_STATE, "shard_init has not run (or the communicator was aborted)");
+    cudaSetDevice(dev_);
+    ShardState& S = *shard_;
+    if (int rc = cuda_check(S.EPOCH.ensure(16), "cudaMalloc(shard epoch)")) return rc;
+    uint32_t* d = S.EPOCH.as<uint32_t>() + 1;
+    set_u32(d, S.calls, stream_);
+    if (int rc = S.nccl_check(S.nl->AllReduce(d, d, 1, ncclUint32, ncclMax, S.comm, stream_), "ncclAllReduce(resync)", err))
+        return rc;
+    uint32_t mx = 0;
+    cudaMemcpyAsync(&mx, d, 4, cudaMemcpyDeviceToHost, stream_);
+    if (int rc = shard_wait("shard_resync", true)) return rc;
+    S.calls = mx;
+    return OK;
 }
 
 int DitB200::shard_forward(const float* vid_patch, int Lv, const float* txt, int TXT, float t, float* sr_out) {
+    if (int rc = shard_begin_call()) return rc;
     if (!vid_patch || !txt || !sr_out) return fail(ERR_ARG, "null buffer");
-    if (dev_ < 0) return fail(ERR_STATE, "context not created");
     cudaSetDevice(dev_);
     if (int rc = shard_prepare(Lv, TXT)) return rc;
     ShardState& S = *shard_;
+    if (S.p2p) set_u32(S.EPOCH.as<uint32_t>(), S.calls, stream_);
     float temb[TEMB_IN];
     sinusoidal256(t, temb);
     cudaMemcpyAsync(temb_in_.p, temb, sizeof temb, cudaMemcpyHostToDevice, stream_);
@@ -447,23 +522,20 @@ int DitB200::shard_forward(const float* vid_patch, int Lv, const float* txt, int
     int rc = prof_on_ ? shard_enqueue(stream_) : shard_capture();
     if (!rc && !prof_on_) rc = cuda_check(cudaGraphLaunch(S.gexec, stream_), "shard graph launch");
     if (rc) {
-        cudaStreamSynchronize(stream_);
+        shard_wait("shard_forward", !S.p2p);
         return rc;
     }
     cudaMemcpyAsync(sr_out, S.SRFULL.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToHost, stream_);
-    last_launches_ = prof_on_ ? launches_ : S.graph_launches;
+    last_launches_ = (prof_on_ ? launches_ : S.graph_launches) + (S.p2p ? 1 : 0);
     if (int rc = cuda_check(cudaGetLastError(), "kernel launch")) return rc;
-    if (int rc = cuda_check(cudaStreamSynchronize(stream_), "shard_forward")) return rc;
-    int expired = 0;
-    if (S.p2p && shard_error_reset(&expired) == 0 && expired)
-        return fail(ERR_TIMEOUT, "a peer-memory exchange wait expired (a rank fell behind or stopped)");
-    return OK;
+    if (int rc = shard_wait("shard_forward", !S.p2p)) return rc;
+    return take_status(stream_, "shard_forward");
 }
 
 int DitB200::shard_forward_dev(const float* d_vid, int Lv, const float* d_txt, int TXT, float t, float* d_sr,
                                cudaStream_t user) {
+    if (int rc = shard_begin_call()) return rc;
     if (!d_vid || !d_txt || !d_sr) return fail(ERR_ARG, "null buffer");
-    if (dev_ < 0) return fail(ERR_STATE, "context not created");
     cudaSetDevice(dev_);
     if (int rc = shard_prepare(Lv, TXT)) return rc;
     ShardState& S = *shard_;
@@ -478,13 +550,14 @@ int DitB200::shard_forward_dev(const float* d_vid, int Lv, const float* d_txt, i
     cudaMemcpyAsync(S.VIDIN.p, d_vid, (size_t)Lv * PATCH_IN * 4, cudaMemcpyDeviceToDevice, stream_);
     cudaMemcpyAsync(S.TXTIN.p, d_txt, (size_t)TXT * TXT_IN * 4, cudaMemcpyDeviceToDevice, stream_);
     int rc = shard_capture();
+    if (!rc && S.p2p) set_u32(S.EPOCH.as<uint32_t>(), S.calls, stream_);
     if (!rc) rc = cuda_check(cudaGraphLaunch(S.gexec, stream_), "shard graph launch");
     if (!rc) cudaMemcpyAsync(d_sr, S.SRFULL.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToDevice, stream_);
     cudaEventRecord(ev_out, stream_);
     cudaStreamWaitEvent(user, ev_out, 0);
     cudaEventDestroy(ev_in);
     cudaEventDestroy(ev_out);
-    last_launches_ = S.graph_launches;
+    last_launches_ = S.graph_launches + (S.p2p ? 1 : 0);
     if (rc) return rc;
     return cuda_check(cudaGetLastError(), "shard_forward_dev");
 }

@@ -22,6 +22,8 @@ struct NcclLib {
     ncclResult_t (*GroupEnd)() = nullptr;
     ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     const char* (*GetErrorString)(ncclResult_t) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
 };
 // Loads the library once per process; null (and *err set) when it is missing.
 const NcclLib* nccl_lib(std::string* err);
@@ -55,7 +57,10 @@ struct DitB200::ShardState {
     // when every pair of ranks can map each other's memory.
     bool p2p = false;
     ActT act = ACT_BF16;            // activation type of the context
-    DevBuf TXTP, FLAGS, EPOCH;      // [2][TXT*2560] partials, flags, forward counter
+    DevBuf TXTP, FLAGS, EPOCH;      // [2][TXT*2560] partials, flags, this forward's call number
+    uint32_t calls = 0;             // shard-forward calls on this rank, failed ones included
+    uint64_t wait_ns = 4000000000ull;   // bound of every flag wait and of the NCCL watchdog
+    bool aborted = false;           // the watchdog aborted the communicator: shard_init again
     ShardPeers peers;
     std::vector<void*> opened;      // IPC mappings of the other ranks' buffers
     DevBuf xr_src[2], xr_rank[2], xr_dst[2];   // peer-store exchange lists per parity

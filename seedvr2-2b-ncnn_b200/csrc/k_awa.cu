@@ -279,13 +279,15 @@ void awa_pack_split3(const void* vqkv, const void* tqkv, ActT in_t, int ldq, con
 int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, const AwaDev& g, float scale, void* att, int ld_att,
                   ActT at, float* toutw, cudaStream_t s);
 
-void awa_attend(const void* Qp, const void* Kp, const void* Vp, ActT pt, const AwaDev& g, float scale,
-                void* att, int ld_att, ActT at, float* toutw, cudaStream_t s, int* launches) {
-    if (g.nwin <= 0) return;
-    // bf16 operands: tensor-core kernel (k_awa_tc.cu); fp32: SIMT kernel below
-    if (pt == ACT_BF16 && awa_attend_tc(Qp, Kp, Vp, g, scale, att, ld_att, at, toutw, s) == 0) {
+int awa_attend(const void* Qp, const void* Kp, const void* Vp, ActT pt, const AwaDev& g, float scale,
+               void* att, int ld_att, ActT at, float* toutw, cudaStream_t s, int* launches) {
+    if (g.nwin <= 0) return 0;
+    // bf16 operands: the tensor-core kernel (k_awa_tc.cu), and nothing else;
+    // fp32 operands: the SIMT kernel below
+    if (pt == ACT_BF16) {
+        if (awa_attend_tc(Qp, Kp, Vp, g, scale, att, ld_att, at, toutw, s) != 0) return -1;
         if (launches) (*launches)++;
-        return;
+        return 0;
     }
     dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
     const size_t smem = 2 * KT * 128 * sizeof(float);
@@ -298,6 +300,7 @@ void awa_attend(const void* Qp, const void* Kp, const void* Vp, ActT pt, const A
     else
         k_awa_attn_simt<bf16, bf16><<<grid, 256, smem, s>>>((const bf16*)Qp, (const bf16*)Kp, (const bf16*)Vp, g, scale, (bf16*)att, ld_att, toutw);
     if (launches) (*launches)++;
+    return 0;
 }
 
 int awa_init_device() {

@@ -60,7 +60,9 @@ int awa_static_scratch(void** out) {
 }
 
 // pack -> attention -> txt coalesce on the caller's stream, scratch in
-// g_awa_scratch.  Returns 0, or -1 when the geometry does not fit.
+// g_awa_scratch.  Returns 0, -1 when the geometry does not fit, -2 when the
+// bf16 attention's tensor maps cannot be encoded (the pack was enqueued, the
+// attention was not), or a cudaError_t value.
 int awa_forward_static(const float* vqkv, const float* tqkv, const AwaDev& g, const float* nqv, const float* nkv,
                        const float* nqt, const float* nkt, float eps, float scale, ActT pt, float* vid_out,
                        float* txt_out, cudaStream_t s) {
@@ -74,7 +76,7 @@ int awa_forward_static(const float* vqkv, const float* tqkv, const AwaDev& g, co
     void* Vp = p + 2 * qkv;
     float* toutw = reinterpret_cast<float*>(p + 3 * qkv);
     awa_pack(vqkv, tqkv, ACT_F32, 3 * 2560, g, nqv, nkv, nqt, nkt, eps, Qp, Kp, Vp, pt, s);
-    awa_attend(Qp, Kp, Vp, pt, g, scale, vid_out, 2560, ACT_F32, toutw, s, nullptr);
+    if (awa_attend(Qp, Kp, Vp, pt, g, scale, vid_out, 2560, ACT_F32, toutw, s, nullptr)) return -2;
     awa_coalesce(toutw, g.nwin, g.TXT, txt_out, 2560, ACT_F32, s);
     return 0;
 }

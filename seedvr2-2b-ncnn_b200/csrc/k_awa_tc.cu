@@ -866,13 +866,6 @@ int awa_tc_poly_exp() {
     return (e && e[0] == '2') ? 2 : (e && e[0] == '1') ? 1 : 0;
 }
 
-int awa_tc_error_reset(int* had_error) {
-    int v = 0;
-    cudaError_t e = cudaMemcpyFromSymbol(&v, g_attn_err, sizeof v);
-    if (e != cudaSuccess) return (int)e;
-    if (had_error) *had_error = v;
-    const int zero = 0;
-    return (int)cudaMemcpyToSymbol(g_attn_err, &zero, sizeof zero);
-}
+int awa_tc_flag_ptr(int** p) { return (int)cudaGetSymbolAddress((void**)p, g_attn_err); }
 
 }  // namespace s2b

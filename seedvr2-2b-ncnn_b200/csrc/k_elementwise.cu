@@ -270,4 +270,41 @@ void ingest_weight(const void* src, bool src_f16, int out, int in, void* dst, Ac
     else k_ingest<bf16><<<blocks, 256, 0, s>>>(src, src_f16, out, in, (bf16*)dst, ld, blk_rows, blk_stride, row_off);
 }
 
+// ---------------------------------------------------------------- kernel error status
+__global__ void k_status_fold(int* status, int* f_gemm, int* f_attn, int* f_shard) {
+    const int m = (*f_gemm ? KERR_GEMM : 0) | (*f_attn ? KERR_ATTN : 0) | (*f_shard ? KERR_SHARD : 0);
+    if (m) {
+        *status |= m;
+        *f_gemm = 0; *f_attn = 0; *f_shard = 0;
+    }
+}
+
+__global__ void k_status_raise(int mask, int* f_gemm, int* f_attn, int* f_shard) {
+    if (mask & KERR_GEMM) atomicExch(f_gemm, 1);
+    if (mask & KERR_ATTN) atomicExch(f_attn, 1);
+    if (mask & KERR_SHARD) atomicExch(f_shard, 1);
+}
+
+__global__ void k_set_u32(uint32_t* p, uint32_t v) { *p = v; }
+
+int gemm_tc_flag_ptr(int** p);
+int awa_tc_flag_ptr(int** p);
+int shard_flag_ptr(int** p);
+
+int kernel_flags_get(KernelFlags* f) {
+    if (int e = gemm_tc_flag_ptr(&f->gemm)) return e;
+    if (int e = awa_tc_flag_ptr(&f->attn)) return e;
+    return shard_flag_ptr(&f->shard);
+}
+
+void status_fold(const KernelFlags& f, int* status, cudaStream_t s) {
+    k_status_fold<<<1, 1, 0, s>>>(status, f.gemm, f.attn, f.shard);
+}
+
+void status_raise(const KernelFlags& f, int mask, cudaStream_t s) {
+    k_status_raise<<<1, 1, 0, s>>>(mask, f.gemm, f.attn, f.shard);
+}
+
+void set_u32(uint32_t* p, uint32_t v, cudaStream_t s) { k_set_u32<<<1, 1, 0, s>>>(p, v); }
+
 }  // namespace s2b

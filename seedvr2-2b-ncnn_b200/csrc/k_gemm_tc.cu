@@ -980,14 +980,7 @@ int gemm_tc_grouped(const void* A0, int lda0, const void* W0, int ldw0, int M0, 
     return 0;
 }
 
-int gemm_tc_error_reset(int* had_error) {
-    int v = 0;
-    cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_err, sizeof v);
-    if (e != cudaSuccess) return (int)e;
-    if (had_error) *had_error = v;
-    const int zero = 0;
-    return (int)cudaMemcpyToSymbol(g_tc_err, &zero, sizeof zero);
-}
+int gemm_tc_flag_ptr(int** p) { return (int)cudaGetSymbolAddress((void**)p, g_tc_err); }
 
 int awa_init_device();
 int awa_tc_init_device();

@@ -81,9 +81,6 @@ int gemm_tf32x3(const void* A2, int lda2, const void* W2, int ldw2, int M, int N
                 cudaStream_t s, int* launches);
 // dst[r][0..cols) = tf32(src[r][c]) (round to nearest), dst[r][cols..2cols) = src - that.
 void split_tf32(const float* src, int ld_src, int rows, int cols, float* dst, int ld_dst, cudaStream_t s);
-// Reads and clears the current device's tcgen05-kernel error flag (set when a
-// bounded wait expired).  Returns a cudaError_t value.
-int gemm_tc_error_reset(int* had_error);
 
 // ---------------------------------------------------------------- elementwise
 // Row RMSNorm (eps, optional affine weight) + adaLN modulate.  Rows < split
@@ -109,6 +106,23 @@ void ingest_weight(const void* src, bool src_f16, int out, int in, void* dst, Ac
                    int blk_stride, int row_off, cudaStream_t s);
 // Per-device one-time kernel attributes (dynamic shared memory opt-ins).
 int kernels_init_device();
+// *p = v on stream s (one thread; the value travels as a kernel argument).
+void set_u32(uint32_t* p, uint32_t v, cudaStream_t s);
+
+// ---------------------------------------------------------------- kernel error status
+// Every bounded wait of the tcgen05 GEMM, the tcgen05 attention and the
+// peer-memory exchanges sets its kernel class's device flag when it expires
+// (the kernel then returns early, leaving its output incomplete).  The flags
+// are module globals of the device, shared by every context on it.
+enum KernelErrBit { KERR_GEMM = 1, KERR_ATTN = 2, KERR_SHARD = 4 };
+struct KernelFlags { int* gemm = nullptr; int* attn = nullptr; int* shard = nullptr; };
+// Device addresses of the three flags on the current device (cudaError_t value).
+int kernel_flags_get(KernelFlags* f);
+// One thread, stream-ordered after the kernels it covers: *status |= the
+// KernelErrBit of every raised flag, then the flags are cleared.
+void status_fold(const KernelFlags& f, int* status, cudaStream_t s);
+// Test hook: raise the flags named by mask (KernelErrBit) from one thread.
+void status_raise(const KernelFlags& f, int mask, cudaStream_t s);
 
 // ---------------------------------------------------------------- AWA
 struct AwaDev {
@@ -139,7 +153,9 @@ void awa_pack_split3(const void* vqkv, const void* tqkv, ActT in_t, int ldq, con
 int awa_attend_split3(const void* Q3, const void* K3, const void* V3, const AwaDev& g, float scale, void* att,
                       int ld_att, ActT at, float* toutw, cudaStream_t s);
 // Per-window SDPA.  vid rows scattered to att[vidx]; txt rows to toutw[wi][i].
-void awa_attend(const void* Qp, const void* Kp, const void* Vp, ActT pt, const AwaDev& g, float scale,
+// bf16 operands run the tcgen05 kernel only: -1 (nothing launched) when its
+// tensor maps cannot be encoded.  fp32 operands run the SIMT kernel.
+int awa_attend(const void* Qp, const void* Kp, const void* Vp, ActT pt, const AwaDev& g, float scale,
                 void* att, int ld_att, ActT at, float* toutw, cudaStream_t s, int* launches);
 // att_txt[i, d] = sum_w toutw[w][i][d] / nwin
 void awa_coalesce(const float* toutw, int nwin, int TXT, void* att_txt, int ld_att, ActT at, cudaStream_t s);
@@ -158,10 +174,10 @@ struct ShardPeers {
     float* txtp[8] = {};          // [2 slots][TXT * 2560] txt partial sums
     uint32_t* flags[8] = {};      // [2 kinds][2 slots][world] ready flags
     float* x[2][8] = {};          // residual of each layout parity, [rows][2560]
+    float* sr[8] = {};            // assembled [Lv][64] output
     int world = 1, rank = 0;
+    uint64_t wait_ns = 4000000000ull;   // bound of every flag wait
 };
-// Forward counter (flag values grow across forwards).
-void shard_epoch_inc(uint32_t* epoch, cudaStream_t s);
 // Publish this rank's partial of `layer`, wait for all ranks', write their
 // rank-ordered sum / divisor to the TXT rows at out (stride ld).
 void shard_txt_reduce(const ShardPeers& P, const uint32_t* epoch, int layer, int TXT, float divisor, void* out, int ld,
@@ -170,8 +186,10 @@ void shard_txt_reduce(const ShardPeers& P, const uint32_t* epoch, int layer, int
 // and a wait until every rank's rows of this exchange have arrived.
 void shard_exchange_rows(const ShardPeers& P, int p, const int* src, const int* rank_of, const int* dst, int n,
                          const uint32_t* epoch, int layer, cudaStream_t s);
-// Reads and clears the flag a timed-out wait sets.  Returns a cudaError_t value.
-int shard_error_reset(int* had_error);
+// Rows k < n of sr_local (64 wide) -> row tok[k] of every rank's sr buffer;
+// then flags and a wait until every rank's rows have arrived.
+void shard_gather_sr(const ShardPeers& P, const float* sr_local, const int* tok, int n, const uint32_t* epoch,
+                     cudaStream_t s);
 
 // ---------------------------------------------------------------- grid / engine formats (k_engine.cu)
 // (T, H, W, 33) -> (T*H/2*W/2, 132) and (T*H/2*W/2, 64) -> (T, H, W, 16), src/dit_vk.cpp:717-750.

@@ -109,6 +109,10 @@ def lib() -> ctypes.CDLL:
                                       ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), _I32P],
         "s2b_shard_plan": [ctypes.POINTER(s2b_win), ctypes.POINTER(s2b_win), ip, ip, _I32P, _I32P, _I32P, _I32P,
                            _I32P, _I32P, _I32P],
+        "s2b_shard_resync": [vp],
+        "s2b_check_errors": [vp],
+        "s2b_debug_raise_kernel_error": [vp, ip],
+        "s2b_debug_watchdog_selftest": [ip, ip, _I32P, _I32P],
     }
     for name, args in sig.items():
         fn = getattr(L, name)
@@ -461,6 +465,20 @@ class DitB200:
 
     def shard_forward_dev(self, d_vid: int, Lv: int, d_txt: int, TXT: int, timestep: float, d_sr: int, stream: int):
         self._c(lib().s2b_shard_forward_dev(self._ctx, d_vid, Lv, d_txt, TXT, timestep, d_sr, stream))
+
+    def shard_resync(self):
+        """Collective: after a failed shard call on any rank, every rank calls
+        this before the next shard forward."""
+        self._c(lib().s2b_shard_resync(self._ctx))
+
+    def check_errors(self):
+        """Raises S2BError(S2B_ERR_TIMEOUT) if a bounded kernel wait expired in
+        a stream-ordered (_dev) call since the last report."""
+        self._c(lib().s2b_check_errors(self._ctx))
+
+    def debug_raise_kernel_error(self, mask: int):
+        """Test hook: raise the device's kernel error flags (1 GEMM, 2 attention, 4 exchange)."""
+        self._c(lib().s2b_debug_raise_kernel_error(self._ctx, mask))
 
     def last_launches(self) -> int:
         n = ctypes.c_int()

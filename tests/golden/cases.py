@@ -97,3 +97,23 @@ def compare(a, b):
     b = np.asarray(b, np.float64).ravel()
     cos = float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-300))
     return cos, float(np.abs(a - b).max() / (np.abs(b).max() + 1e-300))
+
+
+# Full 32-layer forwards at BASELINE's grids (reference CPU forward_latent,
+# run layer by layer so every layer boundary is stored).  Weights: synthetic
+# m5 seed 1234; inputs: seed 42; t = 1000; windows (4,3,3).
+#   cfg2  720p  (45x53 tokens, windows 9/9)    all 32 layers, fp32 bar per layer
+#   cfg3  1080p (68x80 tokens, windows 16/25)  all 32 layers, bf16 vs fp32 sr
+#   cfg5  2160p (135x159 tokens, windows 64/64, ragged edge windows) layers [0,2)
+DIT_FULL = {
+    "cfg2": dict(T=1, H=45, W=53, l1=32, full_sr=True),
+    "cfg3": dict(T=1, H=68, W=80, l1=32, full_sr=True),
+    "cfg5": dict(T=1, H=135, W=159, l1=2, full_sr=False),
+}
+DIT_FULL_SEEDS = dict(wseed=1234, iseed=42, t=1000.0, TXT=58)
+N_VID_SAMPLES, N_TXT_SAMPLES, N_SR_SAMPLES = 8192, 2048, 65536
+
+
+def full_golden_path(name: str) -> str:
+    import os
+    return os.path.join(os.path.dirname(os.path.abspath(__file__)), f"dit_{name}.npz")

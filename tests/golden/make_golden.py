@@ -11,7 +11,17 @@ cases of cases.py and stores its outputs:
                     synthetic weights: layers [0,2) init+final (sr), layers
                     [0,2) latents (sampled), layers [30,32) final from the
                     [0,2) latent (sr)
-Usage: python tests/golden/make_golden.py   (takes a few minutes)
+  dit_cfg2.npz / dit_cfg3.npz / dit_cfg5.npz  (`full` mode)
+                    DitVk::forward_latent (CPU mode) over the BASELINE grids
+                    (720p, 1080p, 2160p; cases.DIT_FULL) with the seed-1234
+                    synthetic m5 weights, run one layer at a time: per layer
+                    boundary a fixed sample of the vid / txt latents plus
+                    their stats, and the final sr (full, or sampled for
+                    2160p).  The sampled indices come from cases.sample_index.
+Usage: python tests/golden/make_golden.py          (small fixtures, a few minutes)
+       python tests/golden/make_golden.py full [cfg2 cfg3 cfg5]
+                                                   (reference CPU forwards of
+                                                    the full grids: ~15 min on 8 cores)
 """
 from __future__ import annotations
 
@@ -20,6 +30,7 @@ import json
 import os
 import sys
 import tempfile
+import time
 
 import numpy as np
 
@@ -84,5 +95,49 @@ def main():
     print("golden fixtures written to", HERE)
 
 
+def full(names):
+    """Reference forward_latent over cases.DIT_FULL, one layer per call."""
+    S = cases.DIT_FULL_SEEDS
+    TXT = S["TXT"]
+    R = po.Ref()
+    with tempfile.TemporaryDirectory() as md:
+        s2b.synth_write_m5(md, S["wseed"], 0, 32)
+        R.load(md)
+        for name in names:
+            D = cases.DIT_FULL[name]
+            T, H, W = D["T"], D["H"], D["W"]
+            Lv = T * H * W
+            gns = (T, H, W, TXT) + R.make_win(T, H, W, (4, 3, 3), TXT, 0)
+            gsh = (T, H, W, TXT) + R.make_win(T, H, W, (4, 3, 3), TXT, 1)
+            vp = s2b.patchify_grid(s2b.synth_vid_grid(T, 2 * H, 2 * W, S["iseed"]))
+            txt = s2b.synth_txt(TXT, S["iseed"])
+            iv = cases.sample_index(Lv * 2560, cases.N_VID_SAMPLES)
+            it = cases.sample_index(TXT * 2560, cases.N_TXT_SAMPLES)
+            vs, ts, vst, tst = [], [], [], []
+            vl, tl, _ = R.forward_latent(gns, gsh, vp, txt, S["t"], 0, 0, True, False)
+            for layer in range(D["l1"] + 1):
+                vs.append(vl.ravel()[iv]); ts.append(tl.ravel()[it])
+                vst.append(cases.stats(vl)); tst.append(cases.stats(tl))
+                if layer == D["l1"]:
+                    break
+                t0 = time.time()
+                vl, tl, _ = R.forward_latent(gns, gsh, vl, tl, S["t"], layer, layer + 1, False, False)
+                print(f"{name} layer {layer} {time.time() - t0:.1f} s", flush=True)
+            _, _, sr = R.forward_latent(gns, gsh, vl, tl, S["t"], D["l1"], D["l1"], False, True)
+            out = dict(vid_idx=iv, txt_idx=it, vid_val=np.stack(vs), txt_val=np.stack(ts),
+                       vid_stats=np.stack(vst), txt_stats=np.stack(tst), sr_stats=cases.stats(sr))
+            if D["full_sr"]:
+                out["sr"] = sr
+            else:
+                isr = cases.sample_index(sr.size, cases.N_SR_SAMPLES)
+                out.update(sr_idx=isr, sr_val=sr.ravel()[isr])
+            np.savez_compressed(cases.full_golden_path(name), **out)
+            print("written", cases.full_golden_path(name), flush=True)
+        R.close()
+
+
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) > 1 and sys.argv[1] == "full":
+        full(sys.argv[2:] or list(cases.DIT_FULL))
+    else:
+        main()

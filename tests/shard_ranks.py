@@ -97,3 +97,99 @@ def nccl_forward(rank: int, world: int, uid: bytes, prec: int, grid, out_dir: st
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **out)
     finally:
         ctx.close()
+
+
+def timeout_recover(rank: int, world: int, uid: bytes, port: int, grid, out_dir: str):
+    """A rank that skips a shard call between steps: its peer's bounded flag
+    waits run out (S2B_SHARD_WAIT_MS), the peer's call returns S2B_ERR_TIMEOUT
+    (host call) or reports it through s2b_check_errors (_dev call), a call
+    made with diverged call numbers fails on both ranks, and after
+    s2b_shard_resync on every rank the forward is clean again.  The ranks
+    agree on what happened over a gloo group on the host; no rank leaves with
+    kernels in flight, NVLS is off and the exchanges use plain peer stores."""
+    os.environ["S2B_SHARD_P2P"] = "1"
+    os.environ["S2B_SHARD_WAIT_MS"] = "500"
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import time
+    import torch
+    import torch.distributed as dist
+    import s2b
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    T, H, W = grid
+    Lv, TXT = T * H * W, 58
+    ctx = s2b.DitB200(rank, s2b.PREC_BF16)
+    rec = {}
+
+    def call(fn):
+        t0 = time.monotonic()
+        try:
+            out = fn()
+            return 0, out, time.monotonic() - t0
+        except s2b.S2BError as e:
+            return e.code, None, time.monotonic() - t0
+
+    def any_failed(code):
+        t = torch.tensor([1 if code else 0])
+        dist.all_reduce(t)
+        return int(t.item()) > 0
+
+    try:
+        ctx.init_synth(1234)
+        ctx.set_windows(s2b.make_win(T, H, W, (4, 3, 3), TXT, False), s2b.make_win(T, H, W, (4, 3, 3), TXT, True))
+        vid = s2b.patchify_grid(s2b.synth_vid_grid(T, 2 * H, 2 * W, 42))
+        txt = s2b.synth_txt(TXT, 7)
+        ctx.shard_init(uid, world, rank)
+        fwd = lambda: ctx.shard_forward(vid, Lv, txt, TXT, 1000.0)
+        rc, sr_a, _ = call(fwd)
+        rec["clean"] = rc
+        # 1) host call: rank 1 skips, rank 0's call times out
+        if rank == 0:
+            rc, _, dt = call(fwd)
+            rec["skip_rc"], rec["skip_s"] = rc, dt
+        dist.barrier()
+        if any_failed(rec.get("skip_rc", 0)):
+            ctx.shard_resync()
+        rc, sr_b, _ = call(fwd)
+        rec["after_resync"] = rc
+        # 2) _dev call: rank 1 skips, rank 0 learns it from check_errors
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        st = torch.cuda.current_stream(dev)
+        d_vid, d_txt = torch.from_numpy(vid).to(dev), torch.from_numpy(txt).to(dev)
+        d_sr = torch.zeros(Lv, 64, device=dev)
+        fwd_dev = lambda: ctx.shard_forward_dev(d_vid.data_ptr(), Lv, d_txt.data_ptr(), TXT, 1000.0, d_sr.data_ptr(),
+                                                st.cuda_stream)
+        code = 0
+        if rank == 0:
+            rc, _, _ = call(fwd_dev)
+            rec["dev_enqueue_rc"] = rc
+            st.synchronize()
+            code, _, _ = call(ctx.check_errors)
+            rec["dev_check_rc"] = code
+        dist.barrier()
+        if any_failed(code):
+            ctx.shard_resync()
+        rc, _, _ = call(fwd_dev)
+        st.synchronize()
+        rc2, _, _ = call(ctx.check_errors)
+        rec["dev_after_resync"] = rc or rc2
+        sr_c = d_sr.cpu().numpy()
+        # 3) rank 0 makes one extra failed call and nobody resyncs: the ranks'
+        #    call numbers differ, so the next call fails on BOTH ranks (rank 1
+        #    sees a newer flag at once, rank 0 waits out its bound)
+        if rank == 0:
+            call(fwd)
+        dist.barrier()
+        rc, _, dt = call(fwd)
+        rec["diverged_rc"], rec["diverged_s"] = rc, dt
+        if any_failed(rc):
+            ctx.shard_resync()
+        rc, sr_d, _ = call(fwd)
+        rec["final"] = rc
+        np.savez(os.path.join(out_dir, f"rank{rank}.npz"), sr_a=sr_a, sr_b=sr_b, sr_c=sr_c, sr_d=sr_d,
+                 **{k: np.array(v) for k, v in rec.items()})
+    finally:
+        ctx.close()
+        dist.destroy_process_group()

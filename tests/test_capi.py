@@ -98,3 +98,27 @@ def test_cpp_dropin_header_compiles_and_links(tmp_path):
         # without a GPU the wrapper fails loudly (bool + message), never silently
         r = subprocess.run([exe, str(tmp_path), str(tmp_path / "out.bin")], capture_output=True, text=True)
         assert r.returncode == 1 and "[DitB200]" in r.stderr
+
+
+def test_nccl_watchdog_host_logic():
+    """The NCCL-path watchdog on simulated work (host only): it returns when
+    the work finishes, aborts the communicator once on an asynchronous error
+    or after its bound, and reports a failed stream without aborting."""
+    L = s2b.lib()
+    polls, aborted = ctypes.c_int(), ctypes.c_int()
+    import time
+    # 0: finishes after a few polls
+    assert L.s2b_debug_watchdog_selftest(0, 1000, ctypes.byref(polls), ctypes.byref(aborted)) == 0
+    assert polls.value == 4 and aborted.value == 0
+    # 1: never finishes -> expires after ~timeout, aborts exactly once
+    t0 = time.monotonic()
+    assert L.s2b_debug_watchdog_selftest(1, 50, ctypes.byref(polls), ctypes.byref(aborted)) == 2
+    dt = time.monotonic() - t0
+    assert aborted.value == 1 and 0.04 <= dt < 2.0, dt
+    # 2: the communicator reports an asynchronous error -> abort at once
+    assert L.s2b_debug_watchdog_selftest(2, 10000, ctypes.byref(polls), ctypes.byref(aborted)) == 1
+    assert aborted.value == 1 and polls.value == 2
+    # 3: the stream itself failed -> reported, no abort
+    assert L.s2b_debug_watchdog_selftest(3, 10000, ctypes.byref(polls), ctypes.byref(aborted)) == 3
+    assert aborted.value == 0
+    assert L.s2b_debug_watchdog_selftest(7, 10, None, None) == -1

@@ -1,0 +1,153 @@
+"""The whole 32-layer forward against the reference at BASELINE's grids.
+
+Goldens (tests/golden/dit_cfg{2,3,5}.npz, made by make_golden.py `full` from
+the reference's own CPU DitVk::forward_latent, src/dit_vk.cpp:486-699, run one
+layer per call) hold, per layer boundary, a fixed sample of the vid / txt
+residual latents and their stats, and the final sr.
+
+Bars (north star): fp32 path cos >= 0.99999 and max|d|/max|ref| <= 1e-4 per
+layer; bf16 path cos >= 0.9999 against the reference fp32.  "max rel err" is
+max|d| / max|ref| over the compared values (a normalised absolute error)."""
+import os
+import tempfile
+
+import numpy as np
+import pytest
+
+import cases
+import s2b
+
+pytestmark = pytest.mark.gpu
+S = cases.DIT_FULL_SEEDS
+TXT, TS = S["TXT"], S["t"]
+
+
+def gold(name):
+    return np.load(cases.full_golden_path(name))
+
+
+def geom(name):
+    D = cases.DIT_FULL[name]
+    return D["T"], D["H"], D["W"]
+
+
+def inputs(name):
+    T, H, W = geom(name)
+    vp = s2b.patchify_grid(s2b.synth_vid_grid(T, 2 * H, 2 * W, S["iseed"]))
+    return vp, s2b.synth_txt(TXT, S["iseed"])
+
+
+def ctx_for(name, prec, lo=0, hi=32):
+    T, H, W = geom(name)
+    c = s2b.DitB200(0, prec)
+    c.init_synth(S["wseed"], lo, hi)
+    c.set_windows(s2b.make_win(T, H, W, (4, 3, 3), TXT, False), s2b.make_win(T, H, W, (4, 3, 3), TXT, True))
+    return c
+
+
+def bar_fp32(a, b, what):
+    cos, rel = cases.compare(a, b)
+    assert cos >= 0.99999 and rel <= 1e-4, (what, cos, rel)
+    return cos, rel
+
+
+def test_cfg2_fp32_chained_every_layer_and_sr():
+    """720p fp32: the GPU's own 32-layer chain, checked at every layer
+    boundary against the reference's sampled latents, and the final sr."""
+    g = gold("cfg2")
+    vp, txt = inputs("cfg2")
+    T, H, W = geom("cfg2")
+    Lv = T * H * W
+    c = ctx_for("cfg2", s2b.PREC_FP32)
+    try:
+        vl, tl, _ = c.forward_latent(vp, Lv, txt, TXT, TS, 0, 0, True, False)
+        worst = (1.0, 0.0)
+        for layer in range(33):
+            cv = bar_fp32(vl.ravel()[g["vid_idx"]], g["vid_val"][layer], f"vid after {layer} layers")
+            ct = bar_fp32(tl.ravel()[g["txt_idx"]], g["txt_val"][layer], f"txt after {layer} layers")
+            worst = (min(worst[0], cv[0], ct[0]), max(worst[1], cv[1], ct[1]))
+            if layer < 32:
+                vl, tl, _ = c.forward_latent(vl, Lv, tl, TXT, TS, layer, layer + 1, False, False)
+        _, _, sr = c.forward_latent(vl, Lv, tl, TXT, TS, 32, 32, False, True)
+        bar_fp32(sr, g["sr"], "sr")
+        # the captured 32-layer graph gives the same sr within the same bar
+        bar_fp32(c.forward(vp, Lv, txt, TXT, TS), g["sr"], "sr (graph)")
+        print(f"cfg2 fp32 chained: worst cos {worst[0]:.8f} worst rel {worst[1]:.2e}")
+    finally:
+        c.close()
+
+
+def test_cfg2_fp32_each_layer_fed_reference_input(ref):
+    """720p fp32: every layer run on the REFERENCE's own input for that layer
+    (the reference's CPU forward_latent, run here one layer at a time), its
+    output compared with the reference's output of the same layer.  The
+    reference run itself is checked against the committed golden samples."""
+    g = gold("cfg2")
+    vp, txt = inputs("cfg2")
+    T, H, W = geom("cfg2")
+    Lv = T * H * W
+    gns = (T, H, W, TXT) + ref.make_win(T, H, W, (4, 3, 3), TXT, 0)
+    gsh = (T, H, W, TXT) + ref.make_win(T, H, W, (4, 3, 3), TXT, 1)
+    c = ctx_for("cfg2", s2b.PREC_FP32)
+    worst = (1.0, 0.0)
+    try:
+        with tempfile.TemporaryDirectory() as md:
+            s2b.synth_write_m5(md, S["wseed"], 0, 32)
+            ref.load(md)
+            rv, rt, _ = ref.forward_latent(gns, gsh, vp, txt, TS, 0, 0, True, False)
+            for layer in range(32):
+                np.testing.assert_allclose(rv.ravel()[g["vid_idx"]], g["vid_val"][layer], rtol=1e-5, atol=1e-5)
+                gv, gt, _ = c.forward_latent(rv, Lv, rt, TXT, TS, layer, layer + 1, False, False)
+                rv, rt, _ = ref.forward_latent(gns, gsh, rv, rt, TS, layer, layer + 1, False, False)
+                cv = bar_fp32(gv, rv, f"layer {layer} vid")
+                ct = bar_fp32(gt, rt, f"layer {layer} txt")
+                worst = (min(worst[0], cv[0], ct[0]), max(worst[1], cv[1], ct[1]))
+            ref.close()
+        print(f"cfg2 fp32 per layer: worst cos {worst[0]:.8f} worst rel {worst[1]:.2e}")
+    finally:
+        c.close()
+
+
+@pytest.mark.parametrize("prec", [s2b.PREC_BF16, s2b.PREC_FP32], ids=["bf16", "fp32"])
+def test_cfg3_1080p_full_forward_vs_reference_fp32(prec):
+    """1080p: the captured 32-layer forward (the path bench.py times) against
+    the reference fp32 sr; bf16 at cos >= 0.9999, fp32 at the fp32 bar."""
+    g = gold("cfg3")
+    vp, txt = inputs("cfg3")
+    T, H, W = geom("cfg3")
+    c = ctx_for("cfg3", prec)
+    try:
+        sr = c.forward(vp, T * H * W, txt, TXT, TS)
+    finally:
+        c.close()
+    cos, rel = cases.compare(sr, g["sr"])
+    print(f"cfg3 prec={prec}: cos {cos:.8f} rel {rel:.2e}")
+    if prec == s2b.PREC_FP32:
+        assert cos >= 0.99999 and rel <= 1e-4, (cos, rel)
+    else:
+        assert cos >= 0.9999, (cos, rel)
+
+
+@pytest.mark.parametrize("prec", [s2b.PREC_FP32, s2b.PREC_BF16], ids=["fp32", "bf16"])
+def test_cfg5_2160p_layer_pair_vs_reference(prec):
+    """2160p (135x159 tokens, 64/64 windows with ragged edge windows): input
+    projections, layers 0 and 1 and the final projection."""
+    g = gold("cfg5")
+    vp, txt = inputs("cfg5")
+    T, H, W = geom("cfg5")
+    Lv = T * H * W
+    c = ctx_for("cfg5", prec, 0, 2)
+    try:
+        vl, tl, _ = c.forward_latent(vp, Lv, txt, TXT, TS, 0, 2, True, False)
+        _, _, sr = c.forward_latent(vl, Lv, tl, TXT, TS, 2, 2, False, True)
+    finally:
+        c.close()
+    pairs = [(vl.ravel()[g["vid_idx"]], g["vid_val"][2], "vid after 2 layers"),
+             (tl.ravel()[g["txt_idx"]], g["txt_val"][2], "txt after 2 layers"),
+             (sr.ravel()[g["sr_idx"]], g["sr_val"], "sr")]
+    for a, b, what in pairs:
+        cos, rel = cases.compare(a, b)
+        if prec == s2b.PREC_FP32:
+            assert cos >= 0.99999 and rel <= 1e-4, (what, cos, rel)
+        else:
+            assert cos >= 0.9999, (what, cos, rel)

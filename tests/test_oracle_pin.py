@@ -115,3 +115,41 @@ def test_patchify_roundtrip_matches_port():
     P.L.or_unpatchify.argtypes = [F, ctypes.c_int, ctypes.c_int, ctypes.c_int, F]
     P.L.or_unpatchify(lat.ctypes.data_as(F), 1, 6, 10, theirs.ctypes.data_as(F))
     assert np.array_equal(back, theirs)
+
+
+def test_full_forward_goldens_are_consistent():
+    """dit_cfg{2,3,5}.npz (reference forward_latent at the BASELINE grids): one
+    sample row per layer boundary, finite, within the stored absolute maxima."""
+    for name in cases.DIT_FULL:
+        path = cases.full_golden_path(name)
+        if not os.path.exists(path):
+            pytest.fail(f"{path} missing: python tests/golden/make_golden.py full {name}")
+        g = np.load(path)
+        assert g["vid_val"].shape == (cases.DIT_FULL[name]["l1"] + 1, cases.N_VID_SAMPLES)
+        assert g["txt_val"].shape == (cases.DIT_FULL[name]["l1"] + 1, cases.N_TXT_SAMPLES)
+        assert np.isfinite(g["vid_val"]).all() and np.isfinite(g["txt_val"]).all()
+        assert np.all(np.abs(g["vid_val"]).max(1) <= g["vid_stats"][:, 2])
+        assert np.all(np.abs(g["txt_val"]).max(1) <= g["txt_stats"][:, 2])
+
+
+def test_port_pinned_to_cfg2_layer0_golden(port, tmp_path):
+    """The C restatement's input projections and layer 0 at 720p (45x53
+    tokens, 9 windows) against the reference's golden samples."""
+    S = cases.DIT_FULL_SEEDS
+    D = cases.DIT_FULL["cfg2"]
+    T, H, W, TXT = D["T"], D["H"], D["W"], S["TXT"]
+    g = np.load(cases.full_golden_path("cfg2"))
+    s2b.synth_write_m5(str(tmp_path), S["wseed"], 0, 1)
+    vp = s2b.patchify_grid(s2b.synth_vid_grid(T, 2 * H, 2 * W, S["iseed"]))
+    txt = s2b.synth_txt(TXT, S["iseed"])
+    gns = (T, H, W, TXT) + port.make_win(T, H, W, (4, 3, 3), TXT, False)
+    gsh = (T, H, W, TXT) + port.make_win(T, H, W, (4, 3, 3), TXT, True)
+    port.load(str(tmp_path), 0, 1)
+    vl, tl, _ = port.forward_latent(gns, gsh, vp, txt, S["t"], 0, 0, True, False)
+    for layer in (0, 1):
+        for a, b in ((vl.ravel()[g["vid_idx"]], g["vid_val"][layer]), (tl.ravel()[g["txt_idx"]], g["txt_val"][layer])):
+            cos, rel = cases.compare(a, b)
+            assert cos > 1 - 1e-9 and rel < 1e-5, (layer, cos, rel)
+        if layer == 0:
+            vl, tl, _ = port.forward_latent(gns, gsh, vl, tl, S["t"], 0, 1, False, False)
+    port.close()

@@ -130,3 +130,29 @@ def test_nccl_shard_forward_matches_single_gpu(tmp_path, prec, p2p):
         assert cos >= 0.99999 and rel <= 1e-4, (cos, rel)
     else:
         assert cos >= 0.9999 and rel <= 5e-2, (cos, rel)
+
+
+@pytest.mark.gpu
+def test_peer_wait_timeout_and_resync(tmp_path):
+    """2 GPUs: a rank that skips a shard call makes its peer's bounded waits
+    expire (S2B_ERR_TIMEOUT from the host call, and from s2b_check_errors
+    after a _dev call); diverged call numbers fail on both ranks; after
+    s2b_shard_resync every rank's forward equals the clean one."""
+    if _gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import shard_ranks
+    uid = s2b.nccl_unique_id()
+    _run_ranks(shard_ranks.timeout_recover, 2, (uid, _free_port(), (1, 24, 28), str(tmp_path)), 600)
+    o = [np.load(tmp_path / f"rank{r}.npz") for r in range(2)]
+    TIMEOUT = 7
+    assert int(o[0]["clean"]) == 0 and int(o[1]["clean"]) == 0
+    assert int(o[0]["skip_rc"]) == TIMEOUT and float(o[0]["skip_s"]) < 5.0
+    assert int(o[0]["dev_enqueue_rc"]) == 0 and int(o[0]["dev_check_rc"]) == TIMEOUT
+    for r in range(2):
+        assert int(o[r]["after_resync"]) == 0 and int(o[r]["dev_after_resync"]) == 0
+        assert int(o[r]["diverged_rc"]) == TIMEOUT
+        assert int(o[r]["final"]) == 0
+        for k in ("sr_b", "sr_c", "sr_d"):
+            np.testing.assert_array_equal(o[r][k], o[0]["sr_a"])
+    # the rank that was behind saw the newer flag at once, not after its bound
+    assert float(o[1]["diverged_s"]) < 0.45
