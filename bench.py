@@ -15,12 +15,20 @@ e2e    = the same through the public host-buffer call s2b_forward (pinned
          host input -> device, forward, device -> host result), wall clock;
 roofline = the tcgen05 GEMM (the dominant kernel class) from the library's
          CUDA-event per-kernel profile of the same forward;
+fp32   = (N=1) sub-records for the fp32 path: BASELINE cfg2 (720p) and 1080p,
+         3xTF32 GEMMs and split3 attention against their derived peaks;
+image  = (N>1) sub-record: BASELINE cfg3 window-sharded over the N GPUs (one
+         frame on all ranks, strong scaling), its parity against the
+         single-GPU forward and the per-layer time of the exchanges;
 cpu_baseline = the reference's own CPU forward_latent (src/dit_vk.cpp,
-         compiled unchanged against the CPU ncnn stand-in) on this host:
-         one 1080p layer timed, scaled to 32 layers plus the measured
-         init + final projection.
+         compiled unchanged against the CPU ncnn stand-in) on this host, a
+         bounded sample: one 1080p layer timed, scaled to 32 layers plus the
+         measured init + final projection.
 
---impl reference runs only that reference CPU path (rank 0; other ranks exit).
+--impl reference times one whole 32-layer 1080p forward_latent of the
+reference's CPU path (rank 0; other ranks exit) on all host cores; that
+process loads only the oracle libraries (oracle/_build, oracle/_ref), never
+the product library.
 """
 from __future__ import annotations
 
@@ -127,66 +135,226 @@ def dist_env():
 
 
 # ---------------------------------------------------------------- reference CPU path
-def reference_sample(workdir: str, steps: int = 1):
-    """Times the reference's own CPU forward_latent: init + final once, then
-    `steps` single 1080p layers.  Returns (per-step estimated ms/frame, info)."""
-    import numpy as np
-    import s2b
+def _ref_setup(workdir: str, lo: int, hi: int):
+    """Synthetic model (layers [lo, hi)) and seed-42 inputs written by the
+    oracle's restated generator, loaded into the reference's own CPU DitVk."""
     from oracle import pyoracle as po
     if not po.have_ref():
         raise RuntimeError("oracle/_ref/libref_dit.so is missing")
+    P = po.Port()
     T, H, W = GRID
-    s2b.synth_write_m5(workdir, WEIGHT_SEED, 10, 10 + min(steps, 4))
+    P.synth_write_m5(workdir, WEIGHT_SEED, lo, hi)
     R = po.Ref()
     R.load(workdir)
     gns = (T, H, W, TXT) + R.make_win(T, H, W, (4, 3, 3), TXT, 0)
     gsh = (T, H, W, TXT) + R.make_win(T, H, W, (4, 3, 3), TXT, 1)
-    vp = s2b.patchify_grid(s2b.synth_vid_grid(T, 2 * H, 2 * W, 42))
-    txt = s2b.synth_txt(TXT, 42)
+    vp = P.patchify_grid(P.synth_vid_grid(T, 2 * H, 2 * W, 42))
+    txt = P.synth_txt(TXT, 42)
+    return R, gns, gsh, vp, txt
+
+
+def reference_layer_sample(workdir: str):
+    """Bounded sample of the reference CPU forward_latent: init + final once,
+    then one layer; returns (32 x layer + init/final ms, info)."""
+    R, gns, gsh, vp, txt = _ref_setup(workdir, 10, 11)
     t0 = time.perf_counter()
     vl, tl, _ = R.forward_latent(gns, gsh, vp, txt, TIMESTEP, 0, 0, True, False)   # vid_in, txt_in, time emb
-    _, _, sr = R.forward_latent(gns, gsh, vl, tl, TIMESTEP, 0, 0, False, True)     # time emb + final projection
+    R.forward_latent(gns, gsh, vl, tl, TIMESTEP, 0, 0, False, True)                 # time emb + final projection
     init_final_ms = (time.perf_counter() - t0) * 1e3
-    out = []
-    for k in range(steps):
-        layer = 10 + (k % 4)
-        t0 = time.perf_counter()
-        R.forward_latent(gns, gsh, vl, tl, TIMESTEP, layer, layer + 1, False, False)
-        layer_ms = (time.perf_counter() - t0) * 1e3
-        out.append(32 * layer_ms + init_final_ms)
+    t0 = time.perf_counter()
+    R.forward_latent(gns, gsh, vl, tl, TIMESTEP, 10, 11, False, False)
+    layer_ms = (time.perf_counter() - t0) * 1e3
     R.close()
-    info = {"init_final_ms": init_final_ms, "layer_ms": (out[-1] - init_final_ms) / 32}
-    return out, info
+    return 32 * layer_ms + init_final_ms, {"init_final_ms": init_final_ms, "layer_ms": layer_ms}
+
+
+def reference_full_forward(workdir: str):
+    """One whole 32-layer forward_latent (init, 32 layers, final) of the
+    reference CPU path, timed; returns (ms, sr)."""
+    R, gns, gsh, vp, txt = _ref_setup(workdir, 0, 32)
+    t0 = time.perf_counter()
+    _, _, sr = R.forward_latent(gns, gsh, vp, txt, TIMESTEP, 0, 32, True, True)
+    ms = (time.perf_counter() - t0) * 1e3
+    R.close()
+    return ms, sr
 
 
 def run_reference(args):
     world, rank, local = dist_env()
     if rank != 0:
         return 0
-    cores = os.cpu_count()
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    os.environ.setdefault("OMP_NUM_THREADS", str(cores))
     with tempfile.TemporaryDirectory() as d:
         try:
-            vals, info = reference_sample(d, args.warmup_ref + args.steps)
+            ms, sr = reference_full_forward(d)
         except Exception as e:   # pragma: no cover - reported, not hidden
             print(json.dumps({"impl": "reference", "unavailable": f"reference CPU path failed: {e}"}))
             return 0
-    vals = vals[args.warmup_ref:]
-    v = statistics.mean(vals)
-    sample = (f"reference DitVk::forward_latent (CPU mode, src/dit_vk.cpp:486-699) at 1080p: one 32-layer "
-              f"estimate per step = 32 x one timed layer ({info['layer_ms']:.0f} ms) + measured init/final "
-              f"({info['init_final_ms']:.0f} ms); GEMMs via this repo's CPU ncnn stand-in (fp32, OpenMP)")
-    line = {"metric": METRIC, "value": v, "unit": "ms/frame", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": v, "higher_is_better": False, "scaling": "weak",
+    import numpy as np
+    sample = (f"one whole 32-layer reference DitVk::forward_latent (CPU mode, src/dit_vk.cpp:486-699) at "
+              f"{args.res}: vid_in/txt_in, time embedding, 32 MM-DiT blocks with the reference's own CPU AWA, "
+              f"final projection; GEMMs through this repo's CPU ncnn stand-in (fp32, OpenMP, "
+              f"{cores} threads); the arm times exactly one forward whatever --steps says")
+    line = {"metric": METRIC, "value": ms, "unit": "ms/frame", "n_gpus": world, "steps": 1,
+            "warmup": 0, "requested_steps": args.steps, "requested_warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": False, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": "cfg3: 1080p 32-layer NaDiT DiT forward, 68x80 tokens, 58 txt, windows 16/25",
+            "config": {"workload": f"{CFG[args.res]}: {args.res} 32-layer NaDiT DiT forward, "
+                                   f"{GRID[1]}x{GRID[2]} tokens, 58 txt, reference CPU forward_latent",
                        "precision": "fp32 (reference CPU path)", "grid": list(GRID), "txt": TXT},
-            "cpu_baseline": {"value": v, "unit": "ms/frame", "cores": cores, "kind": "reference", "sample": sample},
-            "e2e": {"value": v, "unit": "ms/frame", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "sr_checksum": [float(np.float64(sr).sum()), float(np.abs(sr).max())],
+            "cpu_baseline": {"value": ms, "unit": "ms/frame", "cores": cores, "kind": "reference", "sample": sample},
+            "e2e": {"value": ms, "unit": "ms/frame", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
     return 0
 
 
 # ---------------------------------------------------------------- our path
+def _kernel_table(prof):
+    return {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
+                "tflops": (v["flops"] / (v["ms"] * 1e-3) / 1e12) if v["ms"] and v["flops"] else None,
+                "gbs": (v["bytes"] / (v["ms"] * 1e-3) / 1e9) if v["ms"] and v["bytes"] else None}
+            for k, v in prof.items() if v["launches"]}
+
+
+def _tflops(k):
+    return k["flops"] / (k["ms"] * 1e-3) / 1e12 if k["ms"] > 0 else None
+
+
+def fp32_records(steps: int):
+    """fp32 path (N=1): BASELINE cfg2 (720p) and 1080p forwards of one fp32
+    context; 3xTF32 GEMMs and split3 attention against derived peaks."""
+    import torch
+    import s2b
+    pk, src = peaks()
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+    ctx = s2b.DitB200(0, s2b.PREC_FP32)
+    out = {}
+    try:
+        ctx.init_synth(WEIGHT_SEED, 0, 32)
+        for res in ("720p", "1080p"):
+            T, H, W = GRIDS[res]
+            Lv = T * H * W
+            ctx.set_windows(s2b.make_win(T, H, W, (4, 3, 3), TXT, False), s2b.make_win(T, H, W, (4, 3, 3), TXT, True))
+            vid = s2b.patchify_grid(s2b.synth_vid_grid(T, 2 * H, 2 * W, 42))
+            txt = s2b.synth_txt(TXT, 42)
+            d_vid, d_txt = torch.from_numpy(vid).to(dev), torch.from_numpy(txt).to(dev)
+            d_sr = torch.empty(Lv, 64, device=dev)
+            fwd = lambda: ctx.forward_dev(d_vid.data_ptr(), Lv, d_txt.data_ptr(), TXT, TIMESTEP, d_sr.data_ptr(),
+                                          stream.cuda_stream)
+            for _ in range(3):
+                fwd()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(steps):
+                fwd()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = e0.elapsed_time(e1) / steps
+            ctx.check_errors()
+            h_vid, h_txt = torch.from_numpy(vid).pin_memory(), torch.from_numpy(txt).pin_memory()
+            ctx.forward(h_vid.numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
+            w0 = time.perf_counter()
+            for _ in range(steps):
+                ctx.forward(h_vid.numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
+            e2e = (time.perf_counter() - w0) * 1e3 / steps
+            prof = ctx.forward_profile(vid, Lv, txt, TXT, TIMESTEP)
+            g, a = prof["gemm_tcgen05"] if prof["gemm_tcgen05"]["launches"] else prof["gemm_fp32"], prof["attention"]
+            # 3xTF32: kind::tf32 MMAs run at half the bf16 rate, three per product;
+            # split3 attention: six bf16 MMAs per product
+            gemm_peak = pk["bf16_tflops_sustained"] / 2 / 3
+            attn_peak = pk["bf16_tflops"] / 6
+            gt, at = _tflops(g), _tflops(a)
+            out[res] = {"workload": f"{CFG[res]}: {res} 32-layer forward, fp32 path", "grid": [T, H, W],
+                        "ms_per_frame": ms, "e2e_ms_per_frame": e2e, "steps": steps,
+                        "gemm": {"kernel": "k_gemm_tc_pair<..., KIND_TF32X3> (3xTF32)", "ms": g["ms"],
+                                 "useful_tflops": gt, "peak": gemm_peak,
+                                 "peak_source": f"{src} bf16_tflops_sustained / 2 (tf32 rate) / 3 (MMAs per product)",
+                                 "frac": gt / gemm_peak if gt else None},
+                        "attention": {"kernel": "k_awa_attn_x3 (split3)", "ms": a["ms"], "useful_tflops": at,
+                                      "peak": attn_peak,
+                                      "peak_source": f"{src} bf16_tflops / 6 (bf16 MMAs per product)",
+                                      "frac": at / attn_peak if at else None},
+                        "kernels": _kernel_table(prof)}
+    finally:
+        ctx.close()
+    return out
+
+
+def image_record(ctx, args, world, rank, local, frames, txt):
+    """(N>1) BASELINE cfg3 window-sharded over the ranks: one frame on all
+    ranks per step, its parity against the single-GPU forward (rank 0, outside
+    the timed region) and the per-layer time of the exchanges."""
+    import numpy as np
+    import torch
+    import s2b
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    T, H, W = GRID
+    Lv = T * H * W
+    uid = [s2b.nccl_unique_id() if rank == 0 else None]
+    torch.distributed.broadcast_object_list(uid, src=0)
+    ctx.shard_init(uid[0], world, rank)
+    d_txt = torch.from_numpy(txt).to(dev)
+    d_vid = [torch.from_numpy(f).to(dev) for f in frames]
+    d_sr = torch.empty(Lv, 64, device=dev)
+    step = lambda i: ctx.shard_forward_dev(d_vid[i % len(frames)].data_ptr(), Lv, d_txt.data_ptr(), TXT, TIMESTEP,
+                                           d_sr.data_ptr(), stream.cuda_stream)
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    ctx.check_errors()
+    launches = ctx.last_launches()
+    torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    torch.distributed.barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ctx.check_errors()
+    ms = float(t.item()) / args.steps
+    # e2e through the host-buffer call (the whole frame in, the whole sr out on every rank)
+    h_vid, h_txt = torch.from_numpy(frames[0]).pin_memory(), torch.from_numpy(txt).pin_memory()
+    sr_shard = ctx.shard_forward(h_vid.numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
+    torch.distributed.barrier()
+    w0 = time.perf_counter()
+    for i in range(args.steps):
+        ctx.shard_forward(h_vid.numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
+    te = torch.tensor([(time.perf_counter() - w0) * 1e3 / args.steps], device=dev, dtype=torch.float64)
+    torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+    prof = ctx.forward_profile(frames[0], Lv, txt, TXT, TIMESTEP, sharded=True)
+    ex = torch.tensor([prof["exchange"]["ms"]], device=dev, dtype=torch.float64)
+    torch.distributed.all_reduce(ex, op=torch.distributed.ReduceOp.MAX)
+    rec = None
+    if rank == 0:
+        sr_single = ctx.forward(frames[0], Lv, txt, TXT, TIMESTEP)
+        a, b = sr_shard.ravel().astype(np.float64), sr_single.ravel().astype(np.float64)
+        ns = s2b.make_win(T, H, W, (4, 3, 3), TXT, False)
+        sh = s2b.make_win(T, H, W, (4, 3, 3), TXT, True)
+        owned = [len(s2b.shard_plan(ns, sh, world, r).tokens[0]) for r in range(world)]
+        rec = {"workload": f"{CFG[args.res]}: one {args.res} frame, windows sharded over {world} GPUs "
+                           "(txt mean + residual rows exchanged per layer over NVLink peer memory)",
+               "value": ms, "unit": "ms/frame", "scaling": "strong", "steps": args.steps,
+               "e2e": {"value": float(te.item()), "unit": "ms/frame",
+                       "h2d_bytes_per_step": frames[0].nbytes + txt.nbytes, "d2h_bytes_per_step": Lv * 64 * 4},
+               "gpu_launches": launches * args.steps,
+               "parity_vs_single_gpu": {"cos": float(a @ b / np.linalg.norm(a) / np.linalg.norm(b)),
+                                        "max_abs_over_max_ref": float(np.abs(a - b).max() / np.abs(b).max())},
+               "exchange_ms_per_forward_max_rank": float(ex.item()),
+               "exchange_ms_per_layer": float(ex.item()) / 32,
+               "rank0_kernels": _kernel_table(prof),
+               "tokens_per_rank_layer0": owned}
+    return rec
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -237,6 +405,7 @@ def run_ours(args):
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
+    ctx.check_errors()
     launches_per_fwd = ctx.last_launches()
     clocks.wait_first()
 
@@ -251,6 +420,7 @@ def run_ours(args):
     torch.cuda.synchronize(dev)
     clocks.mark_end()
     barrier()
+    ctx.check_errors()
     ms = e0.elapsed_time(e1)
     clk = clocks.stop()
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -263,14 +433,13 @@ def run_ours(args):
     # e2e through the host-buffer public API: pinned input -> forward -> host result
     h_vid = [torch.from_numpy(f).pin_memory() for f in frames]
     h_txt = torch.from_numpy(txt).pin_memory()
-    h_sr = torch.empty(Lv, 64).pin_memory()
     host_fwd = ctx.shard_forward if image else ctx.forward
     for i in range(2):
         host_fwd(h_vid[i % len(frames)].numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
     barrier()
     w0 = time.perf_counter()
     for i in range(args.steps):
-        sr = host_fwd(h_vid[i % len(frames)].numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
+        host_fwd(h_vid[i % len(frames)].numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
     w1 = time.perf_counter()
     barrier()
     te = torch.tensor([(w1 - w0) * 1e3], device=dev, dtype=torch.float64)
@@ -284,9 +453,8 @@ def run_ours(args):
     prof = ctx.forward_profile(frames[0], Lv, txt, TXT, TIMESTEP, sharded=image)
     pk, src = peaks()
     g = prof["gemm_tcgen05"] if prec == s2b.PREC_BF16 else prof["gemm_fp32"]
-    gemm_tflops = g["flops"] / (g["ms"] * 1e-3) / 1e12 if g["ms"] > 0 else None
-    a = prof["attention"]
-    awa_tflops = a["flops"] / (a["ms"] * 1e-3) / 1e12 if a["ms"] > 0 else None
+    gemm_tflops = _tflops(g)
+    awa_tflops = _tflops(prof["attention"])
     total_prof_ms = sum(v["ms"] for v in prof.values())
     peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")) if prec == s2b.PREC_BF16 else None
     traffic = None
@@ -302,17 +470,31 @@ def run_ours(args):
                 "traffic": traffic, "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside the forward)",
                 "flops_per_launch": g["flops"] / max(g["launches"], 1),
                 "ms_per_launch": g["ms"] / max(g["launches"], 1)}
+    attn = {"kernel": "k_awa_attn_tc4 (tcgen05 bf16 attention)", "achieved": awa_tflops,
+            "peak": pk.get("bf16_tflops"), "unit": "TFLOP/s",
+            "frac": awa_tflops / pk["bf16_tflops"] if awa_tflops and pk.get("bf16_tflops") else None,
+            "peak_source": f"{src} bf16_tflops (burst)"}
+
+    image_rec = None
+    if world > 1 and not image and not args.no_image:
+        image_rec = image_record(ctx, args, world, rank, local, frames, txt)
+    ctx.close()
+
+    fp32 = None
+    if world == 1 and prec == s2b.PREC_BF16 and not args.no_fp32:
+        fp32 = fp32_records(max(3, min(args.steps, 10)))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import pyoracle as po
         if po.have_ref():
             with tempfile.TemporaryDirectory() as d:
-                vals, info = reference_sample(d, 1)
-            cpu = {"value": vals[0], "unit": "ms/frame", "cores": os.cpu_count(), "kind": "reference",
+                v, info = reference_layer_sample(d)
+            cpu = {"value": v, "unit": "ms/frame", "cores": len(os.sched_getaffinity(0)), "kind": "reference",
                    "sample": f"one 1080p layer of the reference CPU forward_latent ({info['layer_ms']:.0f} ms) x 32 "
                              f"+ measured init/final ({info['init_final_ms']:.0f} ms); GEMMs via this repo's "
-                             f"CPU ncnn stand-in (fp32 OpenMP), AWA the reference's own scalar loop"}
+                             f"CPU ncnn stand-in (fp32 OpenMP), AWA the reference's own scalar loop; "
+                             f"bench.py --impl reference times a whole forward"}
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "ms/frame", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": False,
@@ -332,16 +514,17 @@ def run_ours(args):
                 "e2e": {"value": e2e_value, "unit": "ms/frame", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
                 "gpu_launches": launches_per_fwd * args.steps,
                 "roofline": roofline,
+                "attention": attn,
                 "awa_tflops": awa_tflops,
-                "kernels": {k: {"ms": round(v["ms"], 3), "launches": v["launches"],
-                                "tflops": (v["flops"] / (v["ms"] * 1e-3) / 1e12) if v["ms"] and v["flops"] else None,
-                                "gbs": (v["bytes"] / (v["ms"] * 1e-3) / 1e9) if v["ms"] and v["bytes"] else None}
-                            for k, v in prof.items()},
+                "kernels": _kernel_table(prof),
                 "profile_forward_ms": total_prof_ms,
                 "clocks": clk,
                 "cpu_baseline": cpu}
+        if image_rec:
+            line["image"] = image_rec
+        if fp32:
+            line["fp32"] = fp32
         print(json.dumps(line))
-    ctx.close()
     if world > 1:
         torch.distributed.destroy_process_group()
     return 0
@@ -462,6 +645,8 @@ def main():
                     help="frames: independent frames dealt round-robin (weak scaling); image: one frame's "
                          "windows sharded over the GPUs (strong scaling)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the reference CPU baseline leg")
+    ap.add_argument("--no-fp32", action="store_true", help="skip the fp32 sub-records (N=1)")
+    ap.add_argument("--no-image", action="store_true", help="skip the window-sharded sub-record (N>1)")
     args = ap.parse_args()
     args.warmup_ref = 0
     global GRID
@@ -471,7 +656,7 @@ def main():
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
-        # each reference step is a bounded sample (one 1080p layer)
+        # one whole reference CPU forward, whatever --steps says
         return run_reference(args)
     return run_ours(args)
 

@@ -114,6 +114,13 @@ int s2b_set_windows(s2b_ctx* ctx, const s2b_win* ns, const s2b_win* sh);
 int s2b_forward_latent(s2b_ctx* ctx, const float* vid_in, int Lv, const float* txt_in, int TXT,
                        float timestep, int l0, int l1, int do_init, int do_final,
                        float* vid_lat, float* txt_lat, float* sr_out);
+/* Semantics of the last layer (31) for the txt rows.  0 (default):
+ * DitVk::forward_latent's vid_only block -- txt is not modulated, not gated
+ * and skips its MLP (src/dit_vk.cpp:523-625).  1: the chunked graph that
+ * DitVk::forward_graph runs (export/export_dit_graph.py:155-226) -- txt is
+ * treated as in every other layer, which changes the txt K/V of the last
+ * attention and so the vid output.  Applies to every forward entry point. */
+int s2b_set_last_layer_semantics(s2b_ctx* ctx, int graph);
 /* Replaces DitVk::forward (src/dit_vk.cpp:710-715) and DitVk::forward_graph
  * (src/dit_graph.cpp:264-549): all 32 layers, replayed from one captured CUDA
  * graph per (Lv, TXT) with weights resident. */
@@ -215,9 +222,9 @@ int s2b_ada_compose(s2b_ctx* ctx, const float* emb, float* out);
  * (g_lin_time / g_awa_time, src/dit_vk.cpp:23-24, 688-697).  This runs the
  * 32-layer forward_latent with CUDA events around every kernel on the launch
  * stream and returns, per kernel class (0 tcgen05 GEMM, 1 fp32 GEMM,
- * 2 attention, 3 qk-norm/RoPE pack, 4 norm/convert, 5 other), the summed
- * device milliseconds, algorithmic FLOPs and bytes, and launch counts
- * (arrays of 6). */
+ * 2 attention, 3 qk-norm/RoPE pack, 4 norm/convert, 5 other, 6 multi-GPU
+ * exchange: always 0 here), the summed device milliseconds, algorithmic FLOPs
+ * and bytes, and launch counts (arrays of 7). */
 int s2b_forward_profile(s2b_ctx* ctx, const float* vid_patch, int Lv, const float* txt, int TXT, float timestep,
                         double* ms, double* flops, double* bytes, int* launches);
 
@@ -305,8 +312,9 @@ int s2b_shard_resync(s2b_ctx* ctx);
  *   in ascending grid-token order per pair.
  * No reference counterpart (the reference runs a frame on one device,
  * src/dit_vk.cpp:481-676). */
-/* s2b_forward_profile over this rank's part of s2b_shard_forward (its
- * kernels only; the NCCL transfers are not a kernel class of their own). */
+/* s2b_forward_profile over this rank's part of s2b_shard_forward (arrays of
+ * 7; class 6 is the exchanges: the cross-rank txt combine, the residual row
+ * exchange and the output assembly, including time spent waiting for peers). */
 int s2b_shard_forward_profile(s2b_ctx* ctx, const float* vid_patch, int Lv, const float* txt, int TXT,
                               float timestep, double* ms, double* flops, double* bytes, int* launches);
 int s2b_shard_plan(const s2b_win* ns, const s2b_win* sh, int world, int rank, int* bounds, int* n_local,

@@ -233,7 +233,10 @@ struct or_model {
     float *von_w, *voa_shift, *voa_scale;
     branch_t br[NUM_LAYERS][2];
     block_t blk[NUM_LAYERS][2];   /* [i][0]=vid or all, [i][1]=txt or all (aliases for shared) */
+    int graph_last;               /* last layer with the chunked graph's txt semantics */
 };
+
+void or_model_set_graph_last_layer(or_model* m, int on) { if (m) m->graph_last = on != 0; }
 
 static float h2f(uint16_t h) {
     uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 0x1f, m = h & 0x3ff, f;
@@ -427,7 +430,10 @@ int or_forward_latent(or_model* m, const or_win* ns, const or_win* shw, const fl
         const branch_t* vR = &m->br[i][0]; const branch_t* tR = &m->br[i][1];
         const block_t* bv = &m->blk[i][0]; const block_t* bt = &m->blk[i][1];
         if (!bv->loaded) { rc = -1; break; }
-        const int last = (i == NUM_LAYERS - 1);
+        /* forward_latent's vid_only last layer (:523-525); with graph_last the
+         * chunked graph's semantics (export/export_dit_graph.py:155-226): txt
+         * is modulated, gated and runs its MLP in every layer */
+        const int last = (i == NUM_LAYERS - 1) && !m->graph_last;
         norm_mod(vid, Lv, emb, 1, 0, vR->a_scale, vR->a_shift, 1, van);          /* :529-537 */
         norm_mod(txt, TXT, emb, 1, 0, tR->a_scale, tR->a_shift, !last, tan_);    /* :538-545 */
         or_linear(van, Lv, DIM, bv->qkv.W, QKV, NULL, vqkv);                    /* :321-322 */

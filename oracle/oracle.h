@@ -39,6 +39,10 @@ void or_linear(const float* x, int M, int K, const float* W, int N, const float*
 
 or_model* or_model_load(const char* m5_dir, int l0, int l1);
 void or_model_free(or_model* m);
+/* Last layer (31): 0 = forward_latent's vid_only semantics (txt unmodulated,
+ * ungated, no txt MLP; src/dit_vk.cpp:523-623, the default); 1 = the chunked
+ * graph's (export/export_dit_graph.py:155-226: txt like every other layer). */
+void or_model_set_graph_last_layer(or_model* m, int on);
 /* src/dit_vk.cpp:295-309 */
 int or_time_embedding(or_model* m, float t, float* emb);
 /* src/dit_vk.cpp:486-699 */
@@ -48,6 +52,14 @@ int or_forward_latent(or_model* m, const or_win* ns, const or_win* sh, const flo
 /* src/dit_vk.cpp:717-750 */
 void or_patchify(const float* grid, int T, int H, int W, float* out);
 void or_unpatchify(const float* lat, int T, int H, int W, float* out);
+
+/* Seeded synthetic model and inputs (synth_oracle.c): the product's
+ * generator restated, so CPU reference runs need no product library. */
+#include <stdint.h>
+void or_synth_normal(float* out, long n, uint64_t seed, const char* stream, float mean, float stdv);
+int or_synth_write_m5(const char* dir, uint64_t seed, int lo, int hi);
+void or_synth_vid_grid(float* grid, int T, int H, int W, uint64_t seed);
+void or_synth_txt(float* txt, int TXT, uint64_t seed);
 
 #ifdef __cplusplus
 }

@@ -61,12 +61,48 @@ class Port:
         L.or_model_load.restype = ctypes.c_void_p
         L.or_model_free.argtypes = [ctypes.c_void_p]
         L.or_time_embedding.argtypes = [ctypes.c_void_p, ctypes.c_float, _F]
+        L.or_model_set_graph_last_layer.argtypes = [ctypes.c_void_p, ctypes.c_int]
         L.or_forward_latent.argtypes = [ctypes.c_void_p, ctypes.POINTER(or_win), ctypes.POINTER(or_win), _F,
                                         ctypes.c_int, _F, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int,
                                         ctypes.c_int, ctypes.c_int, _F, _F, _F]
         L.or_forward_latent.restype = ctypes.c_int
+        L.or_patchify.argtypes = [_F, ctypes.c_int, ctypes.c_int, ctypes.c_int, _F]
+        L.or_synth_normal.argtypes = [_F, ctypes.c_long, ctypes.c_uint64, ctypes.c_char_p, ctypes.c_float,
+                                      ctypes.c_float]
+        L.or_synth_write_m5.argtypes = [ctypes.c_char_p, ctypes.c_uint64, ctypes.c_int, ctypes.c_int]
+        L.or_synth_write_m5.restype = ctypes.c_int
+        L.or_synth_vid_grid.argtypes = [_F, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64]
+        L.or_synth_txt.argtypes = [_F, ctypes.c_int, ctypes.c_uint64]
         self.L = L
         self._model = None
+
+    # synthetic model and inputs (the product's generator, restated) ------
+    def synth_normal(self, shape, seed, stream, mean=0.0, std=1.0):
+        out = np.zeros(int(np.prod(shape)), np.float32)
+        self.L.or_synth_normal(_p(out), out.size, seed, stream.encode(), mean, std)
+        return out.reshape(shape)
+
+    def synth_write_m5(self, path, seed, lo=0, hi=32):
+        rc = self.L.or_synth_write_m5(path.encode(), seed, lo, hi)
+        assert rc == 0, f"could not write the synthetic model to {path}"
+
+    def synth_vid_grid(self, T, H, W, seed):
+        g = np.zeros((T, H, W, 33), np.float32)
+        self.L.or_synth_vid_grid(_p(g), T, H, W, seed)
+        return g
+
+    def synth_txt(self, TXT, seed):
+        t = np.zeros((TXT, 5120), np.float32)
+        self.L.or_synth_txt(_p(t), TXT, seed)
+        return t
+
+    def patchify_grid(self, grid):
+        g = _f32(grid)
+        T, H, W, C = g.shape
+        assert C == 33 and H % 2 == 0 and W % 2 == 0
+        out = np.zeros((T * (H // 2) * (W // 2), 132), np.float32)
+        self.L.or_patchify(_p(g), T, H, W, _p(out))
+        return out
 
     # geometry -----------------------------------------------------------
     def make_win(self, t, h, w, nw=(4, 3, 3), txt_len=58, shifted=False):
@@ -111,6 +147,10 @@ class Port:
             self.L.or_model_free(self._model)
         self._model = self.L.or_model_load(m5_dir.encode(), l0, l1)
         assert self._model, f"oracle could not load {m5_dir}"
+
+    def set_graph_last_layer(self, on: bool):
+        """Layer 31 with the chunked graph's txt semantics (see oracle.h)."""
+        self.L.or_model_set_graph_last_layer(self._model, int(on))
 
     def time_embedding(self, t):
         e = np.zeros(15360, np.float32)

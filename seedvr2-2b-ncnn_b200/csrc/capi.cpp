@@ -330,6 +330,11 @@ int s2b_shard_resync(s2b_ctx* ctx) {
     return ctx->dit.shard_resync();
 }
 
+int s2b_set_last_layer_semantics(s2b_ctx* ctx, int graph) {
+    if (!ctx || (graph != 0 && graph != 1)) return S2B_ERR_ARG;
+    return ctx->dit.set_graph_last_layer(graph == 1);
+}
+
 int s2b_check_errors(s2b_ctx* ctx) {
     if (!ctx) return S2B_ERR_ARG;
     return ctx->dit.check_errors();

@@ -93,6 +93,16 @@ int DitB200::check_errors() {
     return take_status(stream_, "an earlier stream-ordered call");
 }
 
+int DitB200::set_graph_last_layer(bool on) {
+    if (dev_ < 0) return fail(ERR_STATE, "context not created");
+    if (graph_last_ == on) return OK;
+    graph_last_ = on;
+    cudaSetDevice(dev_);
+    if (gexec_) { cudaGraphExecDestroy(gexec_); gexec_ = nullptr; graph_Lv_ = -1; }
+    shard_invalidate_graph();
+    return OK;
+}
+
 int DitB200::debug_raise_kernel_error(int mask) {
     if (dev_ < 0) return fail(ERR_STATE, "context not created");
     if (mask & ~(KERR_GEMM | KERR_ATTN | KERR_SHARD)) return fail(ERR_ARG, "mask must combine 1 (GEMM), 2 (attention), 4 (exchange)");
@@ -623,7 +633,9 @@ int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s) {
 }
 
 int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const LayerBufs& B) {
-    const bool dual = i < MM_LAYERS, last = (i == NUM_LAYERS - 1);
+    // the last layer is vid_only as forward_latent runs it (src/dit_vk.cpp:523-625), unless the
+    // chunked graph's semantics were selected (export/export_dit_graph.py:155-226: txt as in every layer)
+    const bool dual = i < MM_LAYERS, last = (i == NUM_LAYERS - 1) && !graph_last_;
     const int M = Lv + TXT;
     const size_t ab = act_bytes(act_);
     GeomDev& G = *B.geom[i % 2];
@@ -699,6 +711,8 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
         // window-sharded: sum this rank's windows, then combine the ranks'
         // partials and divide by the global window count
         awa_coalesce_div(B.TOUTW, G.view.nwin, TXT, B.txt_partial(B.shard_ctx, i), DIM, ACT_F32, 0.f, s);
+        pend(s);
+        pbeg(KK_EXCHANGE, 0, (double)TXT * DIM * 4, s);
         if (int rc = B.txt_finish(B.shard_ctx, i, att + (size_t)Lv * DIM * ab, s)) return rc;
         launches_ += 2;
     } else {

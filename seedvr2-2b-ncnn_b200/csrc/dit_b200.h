@@ -89,7 +89,8 @@ struct LayerBufs {
 void sinusoidal256(float t, float* e);
 
 // Kernel classes of the per-kernel profile (s2b_forward_profile).
-enum KernelKind { KK_GEMM_TC = 0, KK_GEMM_SIMT = 1, KK_ATTN = 2, KK_PACK = 3, KK_NORM = 4, KK_OTHER = 5, KK_COUNT = 6 };
+enum KernelKind { KK_GEMM_TC = 0, KK_GEMM_SIMT = 1, KK_ATTN = 2, KK_PACK = 3, KK_NORM = 4, KK_OTHER = 5,
+                  KK_EXCHANGE = 6, KK_COUNT = 7 };
 
 class DitB200 {
 public:
@@ -146,6 +147,11 @@ public:
     // on the device, as an expired bounded wait would.
     int debug_raise_kernel_error(int mask);
 
+    // Last layer (31) txt semantics: false = forward_latent's vid_only (the
+    // default, the oracle's), true = the chunked graph's (txt modulated, gated
+    // and through its MLP as in every other layer).  Recaptures the graphs.
+    int set_graph_last_layer(bool on);
+
     int precision() const { return prec_; }
     uint64_t device_bytes() const;
     int last_launches() const { return last_launches_; }
@@ -195,6 +201,7 @@ private:
     int shard_exchange(int p, cudaStream_t s);
     int shard_capture();
     int shard_begin_call();
+    void shard_invalidate_graph();
     int shard_wait(const char* what, bool nccl_in_flight);
     int shard_setup_peers(const ShardPlan& plan, int n0, int n1, int TXT);
     cudaStream_t capture_stream() const { return stream_; }
@@ -212,6 +219,7 @@ private:
     cudaStream_t stream_ = nullptr;
     bool weights_ = false;
     int layer_lo_ = 0, layer_hi_ = 0;
+    bool graph_last_ = false;
 
     Linear vid_in_, txt_in_, emb_in_, emb_hid_, emb_out_, vid_out_;
     Block blk_[NUM_LAYERS][2];

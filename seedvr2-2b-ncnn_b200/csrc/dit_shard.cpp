@@ -416,6 +416,7 @@ int DitB200::shard_enqueue(cudaStream_t s) {
             return rc;
         }
         if (i + 1 < NUM_LAYERS) {
+            pbeg(KK_EXCHANGE, 0, (double)S.n_xr[p] * DIM * 4, s);
             if (S.p2p) {
                 shard_exchange_rows(S.peers, p, S.xr_src[p].as<int>(), S.xr_rank[p].as<int>(), S.xr_dst[p].as<int>(),
                                     S.n_xr[p], S.EPOCH.as<uint32_t>(), i, s);
@@ -423,6 +424,7 @@ int DitB200::shard_enqueue(cudaStream_t s) {
             } else if (int rc = shard_exchange(p, s)) {
                 return rc;
             }
+            pend(s);
         }
     }
     // final norm + vid_out_proj on this rank's rows (src/dit_vk.cpp:657-675),
@@ -436,7 +438,9 @@ int DitB200::shard_enqueue(cudaStream_t s) {
     gemm(S.Xn.p, DIM, vid_out_, nl, f, s);
     if (S.p2p) {
         // every rank stores its rows into every rank's output (bounded flag wait)
+        pbeg(KK_EXCHANGE, 0, (double)nl * OUT_CH * 4 * S.world, s);
         shard_gather_sr(S.peers, S.SRLOC.as<float>(), S.tok1.as<int>(), nl, S.EPOCH.as<uint32_t>(), s);
+        pend(s);
         launches_ += 2;
         fold_status(s);
         return OK;
@@ -479,6 +483,12 @@ int DitB200::shard_wait(const char* what, bool nccl_in_flight) {
                 std::string(what) + (r == WATCH_ASYNC_ERROR ? ": NCCL reported an asynchronous error"
                                                             : ": the NCCL exchange did not finish in time") +
                     "; the communicator was aborted (call shard_init again)");
+}
+
+void DitB200::shard_invalidate_graph() {
+    if (!shard_) return;
+    if (shard_->gexec) { cudaGraphExecDestroy(shard_->gexec); shard_->gexec = nullptr; }
+    shard_->graph_gen = -1;
 }
 
 int DitB200::shard_begin_call() {

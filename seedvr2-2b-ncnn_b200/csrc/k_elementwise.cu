@@ -178,19 +178,26 @@ __global__ void k_to_f32(const TI* __restrict__ src, size_t n, float* __restrict
     if (i < n) dst[i] = Cvt<TI>::to_f(src[i]);
 }
 
-// hi = x rounded to the nearest tf32 (10 explicit mantissa bits, ties to
-// even), lo = x - hi (exact in fp32).
+// x rounded to the nearest tf32 (10 explicit mantissa bits, ties to even).
+__device__ __forceinline__ float round_tf32(float x) {
+    uint32_t b = __float_as_uint(x);
+    if ((b & 0x7F800000u) != 0x7F800000u) b = (b + 0xFFFu + ((b >> 13) & 1u)) & 0xFFFFE000u;
+    return __uint_as_float(b);
+}
+
+// hi = tf32(x), lo = tf32(x - hi) (x - hi is exact in fp32).  Rounding lo to
+// tf32 here, rather than leaving the tensor core to drop its low 13 mantissa
+// bits, makes hi + lo carry x to within half a unit of its 22nd significant
+// bit instead of a whole one.
 __global__ void k_split_tf32(const float* __restrict__ src, int ld_src, int rows, int cols, float* __restrict__ dst,
                              int ld_dst) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)rows * cols) return;
     const int r = (int)(i / cols), c = (int)(i % cols);
     const float x = src[(size_t)r * ld_src + c];
-    uint32_t b = __float_as_uint(x);
-    if ((b & 0x7F800000u) != 0x7F800000u) b = (b + 0xFFFu + ((b >> 13) & 1u)) & 0xFFFFE000u;
-    const float hi = __uint_as_float(b);
+    const float hi = round_tf32(x);
     dst[(size_t)r * ld_dst + c] = hi;
-    dst[(size_t)r * ld_dst + cols + c] = __fsub_rn(x, hi);
+    dst[(size_t)r * ld_dst + cols + c] = round_tf32(__fsub_rn(x, hi));
 }
 
 }  // namespace

@@ -110,6 +110,7 @@ def lib() -> ctypes.CDLL:
         "s2b_shard_plan": [ctypes.POINTER(s2b_win), ctypes.POINTER(s2b_win), ip, ip, _I32P, _I32P, _I32P, _I32P,
                            _I32P, _I32P, _I32P],
         "s2b_shard_resync": [vp],
+        "s2b_set_last_layer_semantics": [vp, ip],
         "s2b_check_errors": [vp],
         "s2b_debug_raise_kernel_error": [vp, ip],
         "s2b_debug_watchdog_selftest": [ip, ip, _I32P, _I32P],
@@ -436,14 +437,14 @@ class DitB200:
         self._c(lib().s2b_ada_compose(self._ctx, _p(e), _p(out)))
         return out
 
-    KERNEL_KINDS = ("gemm_tcgen05", "gemm_fp32", "attention", "awa_pack", "norm_convert", "other")
+    KERNEL_KINDS = ("gemm_tcgen05", "gemm_fp32", "attention", "awa_pack", "norm_convert", "other", "exchange")
 
     def forward_profile(self, vid_patch, Lv, txt, TXT, timestep=1000.0, sharded=False) -> dict:
         """Per kernel class: device ms, algorithmic FLOPs / bytes, launches (CUDA events).
         sharded: this rank's part of the window-sharded forward."""
         v, t = _f32(vid_patch), _f32(txt)
-        D6 = ctypes.c_double * 6
-        ms, fl, by, n = D6(), D6(), D6(), (ctypes.c_int * 6)()
+        D7 = ctypes.c_double * 7
+        ms, fl, by, n = D7(), D7(), D7(), (ctypes.c_int * 7)()
         fn = lib().s2b_shard_forward_profile if sharded else lib().s2b_forward_profile
         self._c(fn(self._ctx, _p(v), Lv, _p(t), TXT, timestep, ms, fl, by, n))
         return {k: dict(ms=ms[i], flops=fl[i], bytes=by[i], launches=n[i]) for i, k in enumerate(self.KERNEL_KINDS)}
@@ -465,6 +466,10 @@ class DitB200:
 
     def shard_forward_dev(self, d_vid: int, Lv: int, d_txt: int, TXT: int, timestep: float, d_sr: int, stream: int):
         self._c(lib().s2b_shard_forward_dev(self._ctx, d_vid, Lv, d_txt, TXT, timestep, d_sr, stream))
+
+    def set_last_layer_semantics(self, graph: bool):
+        """Layer 31 txt: False = forward_latent's vid_only (default), True = the chunked graph's."""
+        self._c(lib().s2b_set_last_layer_semantics(self._ctx, int(graph)))
 
     def shard_resync(self):
         """Collective: after a failed shard call on any rank, every rank calls

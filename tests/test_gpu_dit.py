@@ -245,3 +245,37 @@ def test_temporal_windows_vs_port(port, m5_small, prec):
         assert cos >= 0.99999 and rel <= 1e-4, (cos, rel)
     else:
         assert cos >= 0.9999, (cos, rel)
+
+
+@pytest.mark.parametrize("prec", [s2b.PREC_FP32, s2b.PREC_BF16], ids=["fp32", "bf16"])
+def test_last_layer_graph_semantics_vs_port(port, m5_small, inputs, prec):
+    """s2b_set_last_layer_semantics(1): layer 31 with the chunked graph's txt
+    semantics (export/export_dit_graph.py:155-226) against the port with the
+    same switch; the switch changes the output, and switching back restores
+    forward_latent's."""
+    vp, txt, gns, gsh = inputs[:4]
+    port.load(m5_small, 0, 2)
+    v0, t0, _ = port.forward_latent(gns, gsh, vp, txt, TS, 0, 2, True, False)
+    port.load(m5_small, 30, 32)
+    _, _, sr_default = port.forward_latent(gns, gsh, v0, t0, TS, 30, 32, False, True)
+    port.set_graph_last_layer(True)
+    gv, gt, _ = port.forward_latent(gns, gsh, v0, t0, TS, 30, 32, False, False)
+    _, _, sr_graph = port.forward_latent(gns, gsh, v0, t0, TS, 30, 32, False, True)
+    port.set_graph_last_layer(False)
+    assert cases.compare(sr_graph, sr_default)[1] > 1e-3        # the semantics differ visibly
+    c = make_ctx(prec, m5_small, 30, 32, inputs)
+    try:
+        c.set_last_layer_semantics(True)
+        vl, tl, _ = c.forward_latent(v0, Lv, t0, TXT, TS, 30, 32, False, False)
+        _, _, sr = c.forward_latent(v0, Lv, t0, TXT, TS, 30, 32, False, True)
+        c.set_last_layer_semantics(False)
+        _, _, sr_back = c.forward_latent(v0, Lv, t0, TXT, TS, 30, 32, False, True)
+    finally:
+        c.close()
+    if prec == s2b.PREC_FP32:
+        assert_fp32(sr, sr_graph, "sr graph semantics")
+        assert_fp32(tl, gt, "txt graph semantics")
+        assert_fp32(sr_back, sr_default, "sr default semantics")
+    else:
+        assert cases.compare(sr, sr_graph)[0] >= 0.9999
+        assert cases.compare(sr_back, sr_default)[0] >= 0.9999

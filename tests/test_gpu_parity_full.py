@@ -61,20 +61,25 @@ def test_cfg2_fp32_chained_every_layer_and_sr():
     c = ctx_for("cfg2", s2b.PREC_FP32)
     try:
         vl, tl, _ = c.forward_latent(vp, Lv, txt, TXT, TS, 0, 0, True, False)
-        worst = (1.0, 0.0)
+        rows = []
         for layer in range(33):
-            cv = bar_fp32(vl.ravel()[g["vid_idx"]], g["vid_val"][layer], f"vid after {layer} layers")
-            ct = bar_fp32(tl.ravel()[g["txt_idx"]], g["txt_val"][layer], f"txt after {layer} layers")
-            worst = (min(worst[0], cv[0], ct[0]), max(worst[1], cv[1], ct[1]))
+            cv = cases.compare(vl.ravel()[g["vid_idx"]], g["vid_val"][layer])
+            ct = cases.compare(tl.ravel()[g["txt_idx"]], g["txt_val"][layer])
+            rows.append((layer,) + cv + ct)
             if layer < 32:
                 vl, tl, _ = c.forward_latent(vl, Lv, tl, TXT, TS, layer, layer + 1, False, False)
         _, _, sr = c.forward_latent(vl, Lv, tl, TXT, TS, 32, 32, False, True)
-        bar_fp32(sr, g["sr"], "sr")
-        # the captured 32-layer graph gives the same sr within the same bar
-        bar_fp32(c.forward(vp, Lv, txt, TXT, TS), g["sr"], "sr (graph)")
-        print(f"cfg2 fp32 chained: worst cos {worst[0]:.8f} worst rel {worst[1]:.2e}")
+        sr_graph = c.forward(vp, Lv, txt, TXT, TS)
     finally:
         c.close()
+    for r in rows:
+        print("after %2d layers: vid cos %.9f rel %.2e | txt cos %.9f rel %.2e" % r)
+    print("sr:", cases.compare(sr, g["sr"]), "sr (graph):", cases.compare(sr_graph, g["sr"]))
+    for r in rows:
+        assert r[1] >= 0.99999 and r[2] <= 1e-4 and r[3] >= 0.99999 and r[4] <= 1e-4, r
+    bar_fp32(sr, g["sr"], "sr")
+    # the captured 32-layer graph gives the same sr within the same bar
+    bar_fp32(sr_graph, g["sr"], "sr (graph)")
 
 
 def test_cfg2_fp32_each_layer_fed_reference_input(ref):

@@ -153,3 +153,23 @@ def test_port_pinned_to_cfg2_layer0_golden(port, tmp_path):
         if layer == 0:
             vl, tl, _ = port.forward_latent(gns, gsh, vl, tl, S["t"], 0, 1, False, False)
     port.close()
+
+
+def test_oracle_synth_matches_product_generator(port, tmp_path):
+    """The oracle's restated generator (used by bench.py's reference arm so
+    that it never loads the product library) writes the same model files and
+    inputs as the product's, bit for bit."""
+    for shape, seed, stream, mean, std in (((1001,), 5, "x", 0.0, 1.0), ((7, 33), 42, "vid_noise", 1.0, 0.02)):
+        np.testing.assert_array_equal(port.synth_normal(shape, seed, stream, mean, std),
+                                      s2b.synth_normal(shape, seed, stream, mean, std))
+    np.testing.assert_array_equal(port.synth_vid_grid(1, 6, 8, 42), s2b.synth_vid_grid(1, 6, 8, 42))
+    np.testing.assert_array_equal(port.synth_txt(5, 42), s2b.synth_txt(5, 42))
+    g = s2b.synth_vid_grid(2, 6, 8, 3)
+    np.testing.assert_array_equal(port.patchify_grid(g), s2b.patchify_grid(g))
+    a, b = tmp_path / "oracle", tmp_path / "product"
+    port.synth_write_m5(str(a), 1234, 9, 11)      # layer 9 (vid/txt weights) and 10 (shared)
+    s2b.synth_write_m5(str(b), 1234, 9, 11)
+    names = sorted(os.listdir(b))
+    assert sorted(os.listdir(a)) == names and len(names) > 300
+    for n in names:
+        assert (a / n).read_bytes() == (b / n).read_bytes(), n
