@@ -119,7 +119,45 @@ static void rope(const float* fr, const float* q, float* out) { /* src/dit_vk.cp
     for (int k = ROPE_ROT; k < HEAD_D; k++) out[k] = q[k];
 }
 
+/* ------------------------------------------------------------ operand rounding (emulation) */
+/* 0: fp32 (the reference).  1 / 2: every GEMM operand and every attention
+ * operand (q, k, v, p) rounded to bf16 / fp16 (nearest even) before use, the
+ * arithmetic itself fp32 -- an emulation of a reduced-precision operand path,
+ * used to tell the rounding a bf16 path cannot avoid from errors of its own. */
+static int g_round = 0;
+void or_set_operand_rounding(int mode) { g_round = (mode == 1 || mode == 2) ? mode : 0; }
+
+static float round_operand(float x) {
+    if (g_round == 1) {
+        uint32_t b; memcpy(&b, &x, 4);
+        if ((b & 0x7F800000u) != 0x7F800000u) b = (b + 0x7FFFu + ((b >> 16) & 1u)) & 0xFFFF0000u;
+        memcpy(&x, &b, 4);
+        return x;
+    }
+    if (g_round == 2) return (float)(_Float16)x;
+    return x;
+}
+static void round_rows(float* x, size_t n) {
+    if (!g_round) return;
+    #pragma omp parallel for schedule(static)
+    for (long i = 0; i < (long)n; i++) x[i] = round_operand(x[i]);
+}
+
+static void linear_f32(const float* x, int M, int K, const float* W, int N, const float* b, float* y);
+
 void or_linear(const float* x, int M, int K, const float* W, int N, const float* b, float* y) {
+    if (!g_round) { linear_f32(x, M, K, W, N, b, y); return; }
+    float* xr = (float*)malloc(sizeof(float) * (size_t)M * K);
+    float* wr = (float*)malloc(sizeof(float) * (size_t)N * K);
+    memcpy(xr, x, sizeof(float) * (size_t)M * K);
+    memcpy(wr, W, sizeof(float) * (size_t)N * K);
+    round_rows(xr, (size_t)M * K);
+    round_rows(wr, (size_t)N * K);
+    linear_f32(xr, M, K, wr, N, b, y);
+    free(xr); free(wr);
+}
+
+static void linear_f32(const float* x, int M, int K, const float* W, int N, const float* b, float* y) {
     /* ncnn InnerProduct semantics (src/dit_vk.cpp:270-293): y = x W^T + b, fp32. */
     const int MB = 4, NB = 64;
     const int mt = (M + MB - 1) / MB, nt = (N + NB - 1) / NB;
@@ -197,6 +235,12 @@ void or_awa(const float* vqkv, const float* tqkv, int Lv, int TXT, const or_win*
                     rope(fr, nrm, k + (size_t)a * HEAD_D);
                 }
                 memcpy(v + (size_t)a * HEAD_D, row + 2 * DIM + hh * HEAD_D, HEAD_D * sizeof(float));
+                if (g_round)
+                    for (int d = 0; d < HEAD_D; d++) {
+                        q[(size_t)a * HEAD_D + d] = round_operand(q[(size_t)a * HEAD_D + d]);
+                        k[(size_t)a * HEAD_D + d] = round_operand(k[(size_t)a * HEAD_D + d]);
+                        v[(size_t)a * HEAD_D + d] = round_operand(v[(size_t)a * HEAD_D + d]);
+                    }
             }
             float mx = -1e30f;                                 /* :420-428 */
             for (int a = 0; a < S; a++)
@@ -208,7 +252,7 @@ void or_awa(const float* vqkv, const float* tqkv, int Lv, int TXT, const or_win*
             for (int a = 0; a < S; a++) {                      /* :429-437 */
                 float sm = 0, o[HEAD_D];
                 for (int b = 0; b < S; b++) { float e = expf(sc[(size_t)a * S + b] - mx); p[b] = e; sm += e; }
-                for (int b = 0; b < S; b++) p[b] /= sm;
+                for (int b = 0; b < S; b++) p[b] = round_operand(p[b] / sm);
                 for (int d = 0; d < HEAD_D; d++) o[d] = 0;
                 for (int b = 0; b < S; b++) for (int d = 0; d < HEAD_D; d++) o[d] += p[b] * v[(size_t)b * HEAD_D + d];
                 if (a < f) memcpy(vid_out + (size_t)vidx[cumf[wi] + a] * DIM + hh * HEAD_D, o, sizeof o);
@@ -376,9 +420,10 @@ int or_time_embedding(or_model* m, float t, float* emb) {    /* src/dit_vk.cpp:2
         float freq = (j < half) ? (float)exp(-logf(10000.f) * j / half) : (float)exp(-logf(10000.f) * (j - half) / half);
         e[j] = (j < half) ? sinf(t * freq) : cosf(t * freq);
     }
-    or_linear(e, 1, 256, m->emb_in.W, DIM, m->emb_in.b, h1); silu_inplace(h1, DIM);
-    or_linear(h1, 1, DIM, m->emb_hid.W, DIM, m->emb_hid.b, h2); silu_inplace(h2, DIM);
-    or_linear(h2, 1, DIM, m->emb_out.W, 6 * DIM, m->emb_out.b, emb);
+    /* the timestep MLP stays fp32 in every operand mode (the product keeps it fp32) */
+    linear_f32(e, 1, 256, m->emb_in.W, DIM, m->emb_in.b, h1); silu_inplace(h1, DIM);
+    linear_f32(h1, 1, DIM, m->emb_hid.W, DIM, m->emb_hid.b, h2); silu_inplace(h2, DIM);
+    linear_f32(h2, 1, DIM, m->emb_out.W, 6 * DIM, m->emb_out.b, emb);
     return 0;
 }
 

@@ -34,6 +34,10 @@ void or_build_freqs(const int* sl6, int nwin, int txt_len, float* vf, float* tf)
 void or_awa(const float* vqkv, const float* tqkv, int Lv, int TXT, const or_win* win,
             const float* nqv, const float* nkv, const float* nqt, const float* nkt, float eps,
             float* vid_out, float* txt_out);
+/* Operand rounding emulation for every later call (process-wide): 0 fp32
+ * (the reference's arithmetic), 1 bf16, 2 fp16 -- GEMM operands and the
+ * attention's q, k, v, p rounded to that type, arithmetic in fp32. */
+void or_set_operand_rounding(int mode);
 /* y[M,N] = x[M,K] W[N,K]^T + b (fp32 accumulate). */
 void or_linear(const float* x, int M, int K, const float* W, int N, const float* b, float* y);
 

@@ -62,6 +62,7 @@ class Port:
         L.or_model_free.argtypes = [ctypes.c_void_p]
         L.or_time_embedding.argtypes = [ctypes.c_void_p, ctypes.c_float, _F]
         L.or_model_set_graph_last_layer.argtypes = [ctypes.c_void_p, ctypes.c_int]
+        L.or_set_operand_rounding.argtypes = [ctypes.c_int]
         L.or_forward_latent.argtypes = [ctypes.c_void_p, ctypes.POINTER(or_win), ctypes.POINTER(or_win), _F,
                                         ctypes.c_int, _F, ctypes.c_int, ctypes.c_float, ctypes.c_int, ctypes.c_int,
                                         ctypes.c_int, ctypes.c_int, _F, _F, _F]
@@ -147,6 +148,10 @@ class Port:
             self.L.or_model_free(self._model)
         self._model = self.L.or_model_load(m5_dir.encode(), l0, l1)
         assert self._model, f"oracle could not load {m5_dir}"
+
+    def set_operand_rounding(self, mode: int):
+        """0 fp32, 1 bf16, 2 fp16 operands (emulation; process-wide)."""
+        self.L.or_set_operand_rounding(int(mode))
 
     def set_graph_last_layer(self, on: bool):
         """Layer 31 with the chunked graph's txt semantics (see oracle.h)."""

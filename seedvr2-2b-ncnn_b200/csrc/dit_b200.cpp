@@ -656,6 +656,7 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
     pend(s);
     // 2. qkv projection (no bias), then qk-norm + RoPE + window packing
     const bool fused_pack = act_ == ACT_BF16 && BV.qkv.t == ACT_BF16 && G.structured &&
+                            G.cs.bytes >= (size_t)G.npos * 21 * sizeof(float2) &&
                             gemm_tc_supported(M, QKV, DIM, DIM, DIM);
     if (fused_pack) {
         // one tcgen05 GEMM epilogue writes the packed Q/K/V directly (no qkv buffer)
