@@ -22,6 +22,10 @@ Usage: python tests/golden/make_golden.py          (small fixtures, a few minute
        python tests/golden/make_golden.py full [cfg2 cfg3 cfg5]
                                                    (reference CPU forwards of
                                                     the full grids: ~15 min on 8 cores)
+       python tests/golden/make_golden.py emul [cfg2 cfg3]
+                                                   (the oracle port's own fp32 /
+                                                    bf16- / fp16-operand forwards,
+                                                    stored as sr_port_*: ~30 min)
 """
 from __future__ import annotations
 
@@ -136,8 +140,44 @@ def full(names):
         R.close()
 
 
+def emul(names, modes):
+    """The oracle port's own 32-layer forwards of cases.DIT_FULL (fp32, and
+    with bf16 / fp16 operand rounding emulated), added to the goldens as
+    sr_port_<mode>: the drift two correct fp32 implementations show after 32
+    layers, and the error that rounding every operand to bf16 / fp16 costs by
+    itself (the floor for any path with those operands)."""
+    S = cases.DIT_FULL_SEEDS
+    TXT = S["TXT"]
+    P = po.Port()
+    with tempfile.TemporaryDirectory() as md:
+        P.synth_write_m5(md, S["wseed"], 0, 32)
+        P.load(md, 0, 32)
+        for name in names:
+            D = cases.DIT_FULL[name]
+            T, H, W = D["T"], D["H"], D["W"]
+            gns = (T, H, W, TXT) + P.make_win(T, H, W, (4, 3, 3), TXT, False)
+            gsh = (T, H, W, TXT) + P.make_win(T, H, W, (4, 3, 3), TXT, True)
+            vp = P.patchify_grid(P.synth_vid_grid(T, 2 * H, 2 * W, S["iseed"]))
+            txt = P.synth_txt(TXT, S["iseed"])
+            path = cases.full_golden_path(name)
+            out = dict(np.load(path))
+            ref = out["sr"] if D["full_sr"] else out["sr_val"]
+            for mode in modes:
+                P.set_operand_rounding({"fp32": 0, "bf16": 1, "fp16": 2}[mode])
+                t0 = time.time()
+                _, _, sr = P.forward_latent(gns, gsh, vp, txt, S["t"], 0, D["l1"], True, True)
+                P.set_operand_rounding(0)
+                out[f"sr_port_{mode}"] = sr if D["full_sr"] else sr.ravel()[out["sr_idx"]]
+                print(f"{name} {mode}: {time.time() - t0:.0f} s, vs reference",
+                      cases.compare(out[f"sr_port_{mode}"], ref), flush=True)
+                np.savez_compressed(path, **out)
+        P.close()
+
+
 if __name__ == "__main__":
-    if len(sys.argv) > 1 and sys.argv[1] == "full":
+    if len(sys.argv) > 1 and sys.argv[1] == "emul":
+        emul(sys.argv[2:] or ["cfg2", "cfg3"], ["fp32", "bf16", "fp16"])
+    elif len(sys.argv) > 1 and sys.argv[1] == "full":
         full(sys.argv[2:] or list(cases.DIT_FULL))
     else:
         main()
