@@ -298,6 +298,10 @@ def image_record(ctx, args, world, rank, local, frames, txt):
     uid = [s2b.nccl_unique_id() if rank == 0 else None]
     torch.distributed.broadcast_object_list(uid, src=0)
     ctx.shard_init(uid[0], world, rank)
+    # every rank passes the same whole frames (frame k: seed 42 + k); frame
+    # mode dealt different frames to the ranks
+    T, H, W = GRID
+    frames = [s2b.patchify_grid(s2b.synth_vid_grid(T, 2 * H, 2 * W, 42 + k)) for k in range(len(frames))]
     d_txt = torch.from_numpy(txt).to(dev)
     d_vid = [torch.from_numpy(f).to(dev) for f in frames]
     d_sr = torch.empty(Lv, 64, device=dev)

@@ -340,6 +340,21 @@ int DitB200::load_weights(const char* dir_c, bool synth, uint64_t seed, int lo, 
     if (int rc = cuda_check(cudaMemcpy(branch_.p, branch.data(), branch.size() * 4, cudaMemcpyHostToDevice), "upload vectors")) return rc;
     if (int rc = cuda_check(cudaMemcpy(qknorm_.p, qkn.data(), qkn.size() * 4, cudaMemcpyHostToDevice), "upload vectors")) return rc;
     if (int rc = cuda_check(cudaMemcpy(von_w_.p, von.data(), DIM * 4, cudaMemcpyHostToDevice), "upload vectors")) return rc;
+    // folded norms: bf16 contexts whose shared layers modulate vid and txt
+    // alike (one GEMM serves both flows there)
+    {
+        const char* fe = std::getenv("S2B_NORM_FUSE");
+        bool same = true;
+        for (int i = MM_LAYERS; i < NUM_LAYERS && same; i++)
+            for (int k : {0, 1, 3, 4})
+                same = same && std::memcmp(&branch[((size_t)(i * 12 + k)) * DIM], &branch[((size_t)(i * 12 + 6 + k)) * DIM],
+                                           DIM * 4) == 0;
+        norm_fuse_ = act_ == ACT_BF16 && same && !(fe && fe[0] == '0');
+        shift_ok_ = false;
+        if (norm_fuse_)
+            if (int rc = cuda_check(shift_.ensure((size_t)NUM_LAYERS * 2 * (QKV + 2 * MLP_DIM) * 4), "cudaMalloc(shift)"))
+                return rc;
+    }
     // shared layers: the txt flow uses the same Linear objects
     layer_lo_ = lo; layer_hi_ = hi;
     weights_ = true;
@@ -500,6 +515,7 @@ int DitB200::ensure_acts(int Lv, int TXT) {
     if (need_hg && (rc = cuda_check(HG_.ensure(M * 2 * MLP_DIM * 4), "cudaMalloc(HG)"))) return rc;
     if (act_ == ACT_F32 && tf32x3_ && (rc = cuda_check(A2_.ensure(M * 2 * MLP_DIM * 4), "cudaMalloc(A2)"))) return rc;
     if ((rc = cuda_check(Hs_.ensure(M * MLP_DIM * ab), "cudaMalloc(Hs)"))) return rc;
+    if (norm_fuse_ && (rc = cuda_check(SQ_.ensure(M * SQ_SLOTS * 4), "cudaMalloc(SQ)"))) return rc;
     if ((rc = cuda_check(VPIN_.ensure((size_t)Lv * PATCH_IN_PAD * ab), "cudaMalloc(VPIN)"))) return rc;
     if ((rc = cuda_check(TIN_.ensure((size_t)TXT * TXT_IN * ab), "cudaMalloc(TIN)"))) return rc;
     if ((rc = cuda_check(SR_.ensure((size_t)Lv * OUT_CH * 4), "cudaMalloc(SR)"))) return rc;
@@ -628,8 +644,45 @@ LayerBufs DitB200::default_bufs() {
     return b;
 }
 
-int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s) {
-    return enqueue_layer_on(i, Lv, TXT, s, default_bufs());
+bool DitB200::attn_norm_foldable(int j) const {
+    // layer 0 reads the input projections; layer 31 leaves txt unmodulated
+    // (forward_latent's vid_only block); the fused QKV pack applies the fold
+    const GeomDev& G = geom_[j % 2];
+    return norm_fuse_ && shift_ok_ && j >= 1 && j <= NUM_LAYERS - 2 && G.structured &&
+           G.cs.bytes >= (size_t)G.npos * 21 * sizeof(float2);
+}
+
+int DitB200::enqueue_layer(int i, int Lv, int TXT, cudaStream_t s, int l0, int l1) {
+    LayerBufs b = default_bufs();
+    b.SQ = SQ_.as<float>();
+    b.fuse_mlp = norm_fuse_ && shift_ok_;
+    b.fuse_attn_in = i > l0 && attn_norm_foldable(i);
+    b.fuse_attn_out = i + 1 < l1 && attn_norm_foldable(i + 1);
+    return enqueue_layer_on(i, Lv, TXT, s, b);
+}
+
+// The folded norms need, per layer and flow, the adaLN shift carried through
+// the following Linear: c = W . shift (the norm's output is rs * (x * scale) +
+// shift, so its GEMM is rs * ((x * scale) W^T) + W . shift).  The shifts depend
+// only on the timestep, so c is computed once per timestep: the time
+// embedding and AdaCompose for t, then one bf16 GEMV per Linear.
+int DitB200::prepare_shift(float t, cudaStream_t s) {
+    if (!norm_fuse_ || (shift_ok_ && t == shift_t_)) return OK;
+    float temb[TEMB_IN];
+    sinusoidal256(t, temb);
+    cudaMemcpyAsync(temb_in_.p, temb, sizeof temb, cudaMemcpyHostToDevice, s);
+    enqueue_temb(s);
+    for (int i = layer_lo_; i < layer_hi_; i++)
+        for (int f = 0; f < (i < MM_LAYERS ? 2 : 1); f++) {
+            const Block& B = blk_[i][f];
+            gemv_bf16(B.qkv.w.p, B.qkv.ld, QKV, DIM, ada(i, f, 1), const_cast<float*>(shift_qkv(i, f)), s);
+            gemv_bf16(B.mlp_hg.w.p, B.mlp_hg.ld, 2 * MLP_DIM, DIM, ada(i, f, 4), const_cast<float*>(shift_hg(i, f)), s);
+            launches_ += 2;
+        }
+    if (int rc = cuda_check(cudaGetLastError(), "shift biases")) return rc;
+    shift_ok_ = true;
+    shift_t_ = t;
+    return OK;
 }
 
 int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const LayerBufs& B) {
@@ -648,12 +701,27 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
     float* X = B.X;
 
     const double norm_bytes = (double)DIM * (4 + ab);
-    // 1. attention norm + modulate (txt unmodulated on the last layer, src/dit_vk.cpp:538)
-    pbeg(KK_NORM, 0, norm_bytes * M, s);
-    rmsnorm_mod(X, DIM, M, Lv, ada(i, 0, 0), ada(i, 0, 1), last ? nullptr : ada(i, 1, 0), ada(i, 1, 1), nullptr,
-                NORM_EPS, B.Xn, DIM, act_, s);
-    launches_++;
-    pend(s);
+    // 1. attention norm + modulate (txt unmodulated on the last layer, src/dit_vk.cpp:538); folded into
+    //    the previous layer's last GEMM (operand) and this layer's QKV GEMM (row factor, shift) when
+    //    B.fuse_attn_in
+    if (!B.fuse_attn_in) {
+        pbeg(KK_NORM, 0, norm_bytes * M, s);
+        rmsnorm_mod(X, DIM, M, Lv, ada(i, 0, 0), ada(i, 0, 1), last ? nullptr : ada(i, 1, 0), ada(i, 1, 1), nullptr,
+                    NORM_EPS, B.Xn, DIM, act_, s);
+        launches_++;
+        pend(s);
+    }
+    // the folded-norm fields of a GEMM consuming a fused operand (rows from row0)
+    auto fold_in = [&](GemmEpi& e, const float* shift, int row0) {
+        e.sq_in = B.SQ + (size_t)row0 * SQ_SLOTS; e.sq_n = SQ_SLOTS; e.rs_dim = (float)DIM; e.rs_eps = NORM_EPS;
+        e.bias = shift;
+    };
+    // ... and of a gate/residual GEMM producing one for the next norm (scale sc0 for rows < split)
+    auto fold_out = [&](GemmEpi& e, const float* sc0, const float* sc1, int split, int row0) {
+        e.mod_out = (char*)B.Xn + (size_t)row0 * DIM * ab; e.ldm = DIM;
+        e.mod_sc0 = sc0; e.mod_sc1 = sc1; e.mod_split = split;
+        e.sq_out = B.SQ + (size_t)row0 * SQ_SLOTS;
+    };
     // 2. qkv projection (no bias), then qk-norm + RoPE + window packing
     const bool fused_pack = act_ == ACT_BF16 && BV.qkv.t == ACT_BF16 && G.structured &&
                             G.cs.bytes >= (size_t)G.npos * 21 * sizeof(float2) &&
@@ -669,9 +737,12 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
         if (dual) {
             GemmEpi et = e;
             k.row_base = 0; et.pk.row_base = Lv;
+            if (B.fuse_attn_in) { fold_in(e, shift_qkv(i, 0), 0); fold_in(et, shift_qkv(i, 1), Lv); }
             gemm2(xn, DIM, BV.qkv, Lv, e, xn + (size_t)Lv * DIM * ab, DIM, BT.qkv, TXT, et, s);
         } else {
-            k.row_base = 0; gemm(xn, DIM, BV.qkv, M, e, s);
+            k.row_base = 0;
+            if (B.fuse_attn_in) fold_in(e, shift_qkv(i, 0), 0);
+            gemm(xn, DIM, BV.qkv, M, e, s);
         }
     } else {
         GemmEpi e; e.mode = EPI_STORE; e.out_t = act_; e.ldo = QKV;
@@ -728,37 +799,51 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
         g.resid = X; g.bias = BV.out.bias(); g.gate0 = ada(i, 0, 2); g.gate_split = M;
         gt.resid = X + (size_t)Lv * DIM; gt.bias = BT.out.bias(); gt.gate0 = last ? nullptr : ada(i, 1, 2);
         gt.gate_split = M;
+        if (B.fuse_mlp) { fold_out(g, ada(i, 0, 3), nullptr, M, 0); fold_out(gt, ada(i, 1, 3), nullptr, M, Lv); }
         gemm2(att, DIM, BV.out, Lv, g, att + (size_t)Lv * DIM * ab, DIM, BT.out, TXT, gt, s);
     } else {
         g.resid = X; g.bias = BV.out.bias(); g.gate0 = ada(i, 0, 2); g.gate1 = last ? nullptr : ada(i, 1, 2);
         g.gate_split = Lv;
+        if (B.fuse_mlp) fold_out(g, ada(i, 0, 3), ada(i, 1, 3), Lv, 0);
         gemm(att, DIM, BV.out, M, g, s);
     }
-    // 5. MLP norm + modulate; txt skips the MLP on the last layer (src/dit_vk.cpp:579-620)
+    // 5. MLP norm + modulate; txt skips the MLP on the last layer (src/dit_vk.cpp:579-620); folded
+    //    into the out-projection (operand) and the SwiGLU GEMM (row factor, shift) when B.fuse_mlp
     const int Mm = last ? Lv : M;
-    pbeg(KK_NORM, 0, norm_bytes * Mm, s);
-    rmsnorm_mod(X, DIM, Mm, Lv, ada(i, 0, 3), ada(i, 0, 4), ada(i, 1, 3), ada(i, 1, 4), nullptr, NORM_EPS, B.Xn, DIM,
-                act_, s);
-    launches_++;
-    pend(s);
+    if (!B.fuse_mlp) {
+        pbeg(KK_NORM, 0, norm_bytes * Mm, s);
+        rmsnorm_mod(X, DIM, Mm, Lv, ada(i, 0, 3), ada(i, 0, 4), ada(i, 1, 3), ada(i, 1, 4), nullptr, NORM_EPS, B.Xn,
+                    DIM, act_, s);
+        launches_++;
+        pend(s);
+    }
     // 6. SwiGLU: proj_out(silu(proj_in_gate x) * proj_in x)
     GemmEpi sw; sw.mode = EPI_SWIGLU; sw.out_t = act_; sw.ldo = MLP_DIM;
     GemmEpi mo; mo.mode = EPI_GATE_RESID; mo.ldr = DIM;
+    // the next layer's attention-norm operand (scale a_sc of layer i + 1) from the last GEMM
+    const int nx = i + 1 < NUM_LAYERS ? i + 1 : i;
     if (dual && !last) {
         GemmEpi swt = sw, mot = mo;
         sw.out = hs;
         swt.out = hs + (size_t)Lv * MLP_DIM * ab;
+        if (B.fuse_mlp) { fold_in(sw, shift_hg(i, 0), 0); fold_in(swt, shift_hg(i, 1), Lv); }
         gemm2(xn, DIM, BV.mlp_hg, Lv, sw, xn + (size_t)Lv * DIM * ab, DIM, BT.mlp_hg, TXT, swt, s);
         mo.resid = X; mo.gate0 = ada(i, 0, 5); mo.gate_split = M;
         mot.resid = X + (size_t)Lv * DIM; mot.gate0 = ada(i, 1, 5); mot.gate_split = M;
+        if (B.fuse_attn_out) { fold_out(mo, ada(nx, 0, 0), nullptr, M, 0); fold_out(mot, ada(nx, 1, 0), nullptr, M, Lv); }
         gemm2(hs, MLP_DIM, BV.mlp_out, Lv, mo, hs + (size_t)Lv * MLP_DIM * ab, MLP_DIM, BT.mlp_out, TXT, mot, s);
     } else if (dual) {
-        sw.out = hs; gemm(xn, DIM, BV.mlp_hg, Lv, sw, s);
+        sw.out = hs;
+        if (B.fuse_mlp) fold_in(sw, shift_hg(i, 0), 0);
+        gemm(xn, DIM, BV.mlp_hg, Lv, sw, s);
         mo.resid = X; mo.gate0 = ada(i, 0, 5); mo.gate_split = M;
         gemm(hs, MLP_DIM, BV.mlp_out, Lv, mo, s);
     } else {
-        sw.out = hs; gemm(xn, DIM, BV.mlp_hg, Mm, sw, s);
+        sw.out = hs;
+        if (B.fuse_mlp) fold_in(sw, shift_hg(i, 0), 0);
+        gemm(xn, DIM, BV.mlp_hg, Mm, sw, s);
         mo.resid = X; mo.gate0 = ada(i, 0, 5); mo.gate1 = ada(i, 1, 5); mo.gate_split = Lv;
+        if (B.fuse_attn_out) fold_out(mo, ada(nx, 0, 0), ada(nx, 1, 0), Lv, 0);
         gemm(hs, MLP_DIM, BV.mlp_out, Mm, mo, s);
     }
     return OK;
@@ -847,7 +932,8 @@ int DitB200::forward_latent(const float* vid_in, int Lv, const float* txt_in, in
         cudaMemcpyAsync(X_.as<float>() + (size_t)Lv * DIM, txt_in, (size_t)TXT * DIM * 4, cudaMemcpyHostToDevice, s);
     }
     enqueue_temb(s);
-    for (int i = l0; i < l1; i++) enqueue_layer(i, Lv, TXT, s);
+    if (int rc = prepare_shift(t, s)) return rc;
+    for (int i = l0; i < l1; i++) enqueue_layer(i, Lv, TXT, s, l0, l1);
     if (do_final) enqueue_final(Lv, s);
     fold_status(s);
     if (do_final) {
@@ -870,7 +956,7 @@ int DitB200::capture_full(int Lv, int TXT) {
     if (int rc = cuda_check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "begin capture")) return rc;
     enqueue_init(Lv, TXT, stream_);
     enqueue_temb(stream_);
-    for (int i = 0; i < NUM_LAYERS; i++) enqueue_layer(i, Lv, TXT, stream_);
+    for (int i = 0; i < NUM_LAYERS; i++) enqueue_layer(i, Lv, TXT, stream_, 0, NUM_LAYERS);
     enqueue_final(Lv, stream_);
     fold_status(stream_);
     cudaError_t ce = cudaStreamEndCapture(stream_, &graph);
@@ -891,6 +977,7 @@ int DitB200::forward_dev(const float* d_vid, int Lv, const float* d_txt, int TXT
     if (!d_vid || !d_txt || !d_sr) return fail(ERR_ARG, "null buffer");
     cudaSetDevice(dev_);
     if (int rc = ensure_acts(Lv, TXT)) return rc;
+    if (int rc = prepare_shift(t, stream_)) return rc;
     if (int rc = capture_full(Lv, TXT)) return rc;
     // Order the internal stream after the caller's work, run, then order the
     // caller after us.
@@ -925,6 +1012,7 @@ int DitB200::forward_grid_dev(const float* d_grid, int T, int H, int W, const fl
     if (Lv != geom_[0].view.Lv || TXT != geom_[0].view.TXT || TXT <= 0) return fail(ERR_ARG, "grid / TXT do not match the windows");
     cudaSetDevice(dev_);
     if (int rc = ensure_acts(Lv, TXT)) return rc;
+    if (int rc = prepare_shift(t, stream_)) return rc;
     if (int rc = capture_full(Lv, TXT)) return rc;
     cudaEvent_t ev_in, ev_out;
     cudaEventCreateWithFlags(&ev_in, cudaEventDisableTiming);
@@ -954,6 +1042,7 @@ int DitB200::forward(const float* vid_patch, int Lv, const float* txt, int TXT, 
     if (Lv != geom_[0].view.Lv || TXT != geom_[0].view.TXT || TXT <= 0) return fail(ERR_ARG, "Lv/TXT do not match the windows");
     cudaSetDevice(dev_);
     if (int rc = ensure_acts(Lv, TXT)) return rc;
+    if (int rc = prepare_shift(t, stream_)) return rc;
     if (int rc = capture_full(Lv, TXT)) return rc;
     // the graph reads its inputs from VIDIN_F_/TXTIN_F_/temb_in_ and leaves sr in SR_
     float temb[TEMB_IN];

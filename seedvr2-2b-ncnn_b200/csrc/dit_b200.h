@@ -83,6 +83,14 @@ struct LayerBufs {
     float* (*txt_partial)(void* ctx, int layer) = nullptr;
     int (*txt_finish)(void* ctx, int layer, void* att_txt, cudaStream_t s) = nullptr;
     void* shard_ctx = nullptr;
+    // RMSNorm + adaLN folded into the neighbouring GEMMs (bf16 contexts): the
+    // gate/residual epilogue before a norm writes Xn = resid * scale and per-row
+    // partial sums of squares (SQ, [rows][SQ_SLOTS]); the GEMM after it applies
+    // the row factor and the shift (as a bias through its weights).
+    float* SQ = nullptr;
+    bool fuse_attn_in = false;    // this layer's attention-norm operand came from the previous layer
+    bool fuse_attn_out = false;   // this layer's last GEMM writes the next layer's attention-norm operand
+    bool fuse_mlp = false;        // the out-projection writes the MLP-norm operand
 };
 
 // 256-wide sinusoidal timestep features (src/dit_vk.cpp:295-302).
@@ -192,7 +200,12 @@ private:
     // Enqueue the pieces of forward_latent on stream s (device inputs already staged).
     int enqueue_init(int Lv, int TXT, cudaStream_t s);
     int enqueue_temb(cudaStream_t s);
-    int enqueue_layer(int i, int Lv, int TXT, cudaStream_t s);
+    int enqueue_layer(int i, int Lv, int TXT, cudaStream_t s, int l0, int l1);
+    // the shift biases of the folded norms for timestep t (recomputed only when t changes)
+    int prepare_shift(float t, cudaStream_t s);
+    // layer j's attention norm can take its operand from layer j - 1 (txt is
+    // modulated there and the QKV GEMM runs the fused pack epilogue)
+    bool attn_norm_foldable(int j) const;
     int enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const LayerBufs& B);
     LayerBufs default_bufs();
     int enqueue_final(int Lv, cudaStream_t s);
@@ -208,11 +221,21 @@ private:
     const float* ada(int layer, int flow, int k) const {
         return ada_.as<float>() + ((size_t)(layer * 12 + flow * 6 + k)) * DIM;
     }
+    const float* shift_qkv(int layer, int flow) const {
+        return shift_.as<float>() + ((size_t)(layer * 2 + flow)) * (QKV + 2 * MLP_DIM);
+    }
+    const float* shift_hg(int layer, int flow) const { return shift_qkv(layer, flow) + QKV; }
     const float* normw(int layer, int flow, int which) const {
         return qknorm_.as<float>() + ((size_t)((layer * 2 + flow) * 2 + which)) * HEAD_D;
     }
 
     int dev_ = -1, prec_ = PREC_FP32;
+    // folded norms (bf16): S2B_NORM_FUSE=0 turns them off
+    bool norm_fuse_ = false;
+    DevBuf shift_;          // [32][2 flows][qkv 7680 | hg 13824] shift biases (W . adaLN shift)
+    DevBuf SQ_;             // [rows][SQ_SLOTS] partial sums of squares
+    bool shift_ok_ = false;
+    float shift_t_ = 0.f;
     DevBuf status_;         // int: KernelErrBit of every expired wait not yet reported
     KernelFlags kflags_;    // this device's kernel error flags
     ActT act_ = ACT_F32;

@@ -206,6 +206,7 @@ int DitB200::shard_prepare(int Lv, int TXT) {
     if ((rc = alloc(S.QKV, Mmax * QKV * ab, "cudaMalloc(shard QKV)"))) return rc;
     if ((rc = alloc(S.ATT, Mmax * DIM * ab, "cudaMalloc(shard ATT)"))) return rc;
     if ((rc = alloc(S.Hs, Mmax * MLP_DIM * ab, "cudaMalloc(shard Hs)"))) return rc;
+    if ((rc = alloc(S.SQ, Mmax * SQ_SLOTS * 4, "cudaMalloc(shard SQ)"))) return rc;
     if ((rc = alloc(S.Qp, sumS * DIM * attn_elem_bytes(), "cudaMalloc(shard Qp)"))) return rc;
     if ((rc = alloc(S.Kp, sumS * DIM * attn_elem_bytes(), "cudaMalloc(shard Kp)"))) return rc;
     if ((rc = alloc(S.Vp, sumS * DIM * attn_elem_bytes(), "cudaMalloc(shard Vp)"))) return rc;
@@ -411,6 +412,10 @@ int DitB200::shard_enqueue(cudaStream_t s) {
         B.Qp = S.Qp.p; B.Kp = S.Kp.p; B.Vp = S.Vp.p; B.TOUTW = S.TOUTW.as<float>();
         B.geom[0] = &S.geom[0]; B.geom[1] = &S.geom[1];
         B.txt_partial = shard_txt_partial; B.txt_finish = shard_txt_finish; B.shard_ctx = &S;
+        // the MLP norm folds within a layer; the attention norm's operand would have to
+        // follow the residual rows through the exchange between layers, so it stays a kernel
+        B.SQ = S.SQ.as<float>();
+        B.fuse_mlp = norm_fuse_ && shift_ok_;
         if (int rc = enqueue_layer_on(i, S.plan.n_local(p), TXT, s, B)) {
             if (rc == ERR_NCCL) err = "ncclAllReduce of the txt attention sums failed";
             return rc;
@@ -529,7 +534,8 @@ int DitB200::shard_forward(const float* vid_patch, int Lv, const float* txt, int
     cudaMemcpyAsync(S.VIDIN.p, vid_patch, (size_t)Lv * PATCH_IN * 4, cudaMemcpyHostToDevice, stream_);
     cudaMemcpyAsync(S.TXTIN.p, txt, (size_t)TXT * TXT_IN * 4, cudaMemcpyHostToDevice, stream_);
     // the per-kernel profile records events around each launch: no graph then
-    int rc = prof_on_ ? shard_enqueue(stream_) : shard_capture();
+    int rc = prepare_shift(t, stream_);
+    if (!rc) rc = prof_on_ ? shard_enqueue(stream_) : shard_capture();
     if (!rc && !prof_on_) rc = cuda_check(cudaGraphLaunch(S.gexec, stream_), "shard graph launch");
     if (rc) {
         shard_wait("shard_forward", !S.p2p);
@@ -559,7 +565,8 @@ int DitB200::shard_forward_dev(const float* d_vid, int Lv, const float* d_txt, i
     cudaMemcpyAsync(temb_in_.p, temb, sizeof temb, cudaMemcpyHostToDevice, stream_);
     cudaMemcpyAsync(S.VIDIN.p, d_vid, (size_t)Lv * PATCH_IN * 4, cudaMemcpyDeviceToDevice, stream_);
     cudaMemcpyAsync(S.TXTIN.p, d_txt, (size_t)TXT * TXT_IN * 4, cudaMemcpyDeviceToDevice, stream_);
-    int rc = shard_capture();
+    int rc = prepare_shift(t, stream_);
+    if (!rc) rc = shard_capture();
     if (!rc && S.p2p) set_u32(S.EPOCH.as<uint32_t>(), S.calls, stream_);
     if (!rc) rc = cuda_check(cudaGraphLaunch(S.gexec, stream_), "shard graph launch");
     if (!rc) cudaMemcpyAsync(d_sr, S.SRFULL.p, (size_t)Lv * OUT_CH * 4, cudaMemcpyDeviceToDevice, stream_);

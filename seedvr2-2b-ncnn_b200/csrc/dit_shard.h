@@ -42,7 +42,7 @@ struct DitB200::ShardState {
 
     // residual of parity p's layout: [n_local(p) vid rows | TXT txt rows] x 2560 fp32
     DevBuf X[2];
-    DevBuf Xn, QKV, ATT, Hs, Qp, Kp, Vp, TOUTW, TXTSUM;
+    DevBuf Xn, QKV, ATT, Hs, Qp, Kp, Vp, TOUTW, TXTSUM, SQ;
     DevBuf VIDIN, VIDLOC, VPIN, TXTIN, TIN, SRLOC, SRFULL;
     DevBuf tok0, tok1;          // init gather / final scatter token lists
     // exchange after a layer of parity p: rows to other ranks (gathered into

@@ -314,4 +314,29 @@ void status_raise(const KernelFlags& f, int mask, cudaStream_t s) {
 
 void set_u32(uint32_t* p, uint32_t v, cudaStream_t s) { k_set_u32<<<1, 1, 0, s>>>(p, v); }
 
+// ---------------------------------------------------------------- bf16 GEMV
+// One warp per output row: lanes take 8-element slices of the row in a fixed
+// order, then a fixed butterfly sum.
+__global__ void k_gemv_bf16(const bf16* __restrict__ W, int ld, int N, int K, const float* __restrict__ x,
+                            float* __restrict__ y) {
+    const int n = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (n >= N) return;
+    const bf16* w = W + (size_t)n * ld;
+    float a = 0.f;
+    for (int k = lane * 8; k < K; k += 256) {
+        const uint4 u = *reinterpret_cast<const uint4*>(w + k);
+        const bf16* wb = reinterpret_cast<const bf16*>(&u);
+        #pragma unroll
+        for (int j = 0; j < 8; j++) a = fmaf(__bfloat162float(wb[j]), __ldg(x + k + j), a);
+    }
+    #pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) y[n] = a;
+}
+
+void gemv_bf16(const void* W, int ld, int N, int K, const float* x, float* y, cudaStream_t s) {
+    if (N <= 0) return;
+    k_gemv_bf16<<<(N + 7) / 8, 256, 0, s>>>((const bf16*)W, ld, N, K, x, y);
+}
+
 }  // namespace s2b

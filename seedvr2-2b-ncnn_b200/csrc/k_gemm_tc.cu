@@ -152,6 +152,17 @@ __device__ __forceinline__ void rope64(float* x, int d0, const float2* cs, int p
     }
 }
 
+// Row factor of an RMSNorm folded behind the GEMM (GemmEpi::sq_in): the
+// partial sums of squares the producing epilogue wrote, summed in order in
+// double (as the reference sums squares, src/dit_vk.cpp:48-52).
+__device__ __forceinline__ float row_rs(const GemmEpi& e, int row, bool row_ok) {
+    if (!e.sq_in || !row_ok) return 1.f;
+    const float* sq = e.sq_in + (size_t)row * SQ_SLOTS;
+    double t = 0.0;
+    for (int b = 0; b < e.sq_n; b++) t += (double)__ldg(sq + b);
+    return (float)(1.0 / sqrt(t / (double)e.rs_dim + (double)e.rs_eps));
+}
+
 // EPI_QKV_PACK: the tile's 256 columns are two heads of one of q / k / v.
 // q and k heads get RMSNorm over their 128 dims (x / sqrt(mean(x^2)+eps) * w,
 // the division as a reciprocal multiply: this epilogue serves the bf16 path)
@@ -176,6 +187,9 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
     if (!vid) { ti = gr - k.Lv; p0 = p1 = p2 = ti; }
     const float* w = nullptr;
     if (sec < 2) w = vid ? (sec == 0 ? k.nq0 : k.nk0) : (sec == 0 ? k.nq1 : k.nk1);
+    // folded RMSNorm (row factor) and adaLN shift (bias) of a fused operand
+    const float rs = row_rs(p.e, row, row_ok);
+    const float* cb = p.e.bias;
     // two passes over each head's 128 TMEM columns (sum of squares, then
     // normalise + rotate + store 64 dims at a time) keep 64 values live
     #pragma unroll 1
@@ -188,6 +202,11 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
             for (int c = 0; c < 2; c++) {
                 float x[64];
                 sm100::tmem_ld64(th + c * 64, x);
+                if (cb) {
+                    const float* cc = cb + n0 + hh * 128 + c * 64;
+                    #pragma unroll
+                    for (int d = 0; d < 64; d++) x[d] = fmaf(x[d], rs, __ldg(cc + d));
+                }
                 #pragma unroll
                 for (int d = 0; d < 64; d++) sq = fmaf(x[d], x[d], sq);
             }
@@ -203,6 +222,11 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
             float x[64];
             sm100::tmem_ld64(th + c * 64, x);
             if (!row_ok) continue;
+            if (cb) {
+                const float* cc = cb + n0 + hh * 128 + c * 64;
+                #pragma unroll
+                for (int d = 0; d < 64; d++) x[d] = fmaf(x[d], rs, __ldg(cc + d));
+            }
             if (sec < 2) {
                 #pragma unroll
                 for (int d = 0; d < 64; d += 4) {
@@ -238,12 +262,23 @@ __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, 
     const bool row_ok = row < p.M;
     if constexpr (MODE == EPI_SWIGLU) {
         // column block [h 128 | g 128] -> 128 outputs at n0 / 2
+        const float rs = row_rs(e, row, row_ok);
         #pragma unroll 1
         for (int jc = 0; jc < 4; jc++) {
             float h[32], g[32];
             sm100::tmem_ld32(taddr + jc * 32, h);
             sm100::tmem_ld32(taddr + 128 + jc * 32, g);
             if (!row_ok) continue;
+            if (e.bias) {
+                // folded RMSNorm (row factor) and adaLN shift (bias) of a fused operand
+                const float* bh = e.bias + n0 + jc * 32;
+                const float* bg = e.bias + n0 + 128 + jc * 32;
+                #pragma unroll
+                for (int j = 0; j < 32; j++) {
+                    h[j] = fmaf(h[j], rs, __ldg(bh + j));
+                    g[j] = fmaf(g[j], rs, __ldg(bg + j));
+                }
+            }
             #pragma unroll
             for (int j = 0; j < 32; j++) h[j] = __fmul_rn(silu_f(g[j]), h[j]);
             const size_t off = (size_t)row * e.ldo + n0 / 2 + jc * 32;
@@ -258,6 +293,8 @@ __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, 
         // together, before the TMEM load, so their latency overlaps it and the
         // loads never queue behind the previous chunk's stores.
         float* __restrict__ rrow = e.resid + (size_t)row * e.ldr;
+        const float* msc = (row < e.mod_split) ? e.mod_sc0 : e.mod_sc1;
+        float sq = 0.f;
         #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 32) {
             if (n0 + c0 >= p.N) break;         // warp-uniform
@@ -285,6 +322,20 @@ __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, 
                 }
                 #pragma unroll
                 for (int j = 0; j < 8; j++) __stcg(reinterpret_cast<float4*>(rrow + col) + j, r[j]);
+                if (e.mod_out) {
+                    float m[32];
+                    #pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const float4 s4 = msc ? __ldg(reinterpret_cast<const float4*>(msc + col) + j)
+                                              : make_float4(1.f, 1.f, 1.f, 1.f);
+                        sq = fmaf(r[j].x, r[j].x, sq); sq = fmaf(r[j].y, r[j].y, sq);
+                        sq = fmaf(r[j].z, r[j].z, sq); sq = fmaf(r[j].w, r[j].w, sq);
+                        m[4 * j] = r[j].x * s4.x; m[4 * j + 1] = r[j].y * s4.y;
+                        m[4 * j + 2] = r[j].z * s4.z; m[4 * j + 3] = r[j].w * s4.w;
+                    }
+                    store32((bf16*)e.mod_out + (size_t)row * e.ldm + col, m);
+                    if (((col + 32) & 127) == 0) { e.sq_out[(size_t)row * SQ_SLOTS + col / 128] = sq; sq = 0.f; }
+                }
             } else {
                 for (int j = 0; j < 32 && col + j < p.N; j++) {
                     float t = v[j];
@@ -356,6 +407,9 @@ __device__ __forceinline__ bool epilogue_resid_tma(const TcParams& p, const CUte
     const int row = r0 + lane;
     const float* gate = (row < e.gate_split) ? e.gate0 : e.gate1;
     const int nch = min(bn / 32, (p.N - n0) / 32);
+    const bool mod = e.mod_out != nullptr && row < p.M;
+    const float* msc = (row < e.mod_split) ? e.mod_sc0 : e.mod_sc1;
+    float sq = 0.f;
     // the box ring runs one chunk ahead; pull the next tile's boxes into L2
     // now, a whole mainloop before they are loaded (groups share N)
     if (lane == 0 && next_n0 >= 0) {
@@ -387,6 +441,17 @@ __device__ __forceinline__ bool epilogue_resid_tma(const TcParams& p, const CUte
             if (gate) { t0 = __fmul_rn(t0, g4.x); t1 = __fmul_rn(t1, g4.y); t2 = __fmul_rn(t2, g4.z); t3 = __fmul_rn(t3, g4.w); }
             r.x = __fadd_rn(t0, r.x); r.y = __fadd_rn(t1, r.y); r.z = __fadd_rn(t2, r.z); r.w = __fadd_rn(t3, r.w);
             *q = r;
+            if (mod) {
+                // the next RMSNorm's operand: resid * adaLN scale, and the row's sum of squares
+                const float4 s4 = msc ? __ldg(reinterpret_cast<const float4*>(msc + col) + j)
+                                      : make_float4(1.f, 1.f, 1.f, 1.f);
+                sq = fmaf(r.x, r.x, sq); sq = fmaf(r.y, r.y, sq); sq = fmaf(r.z, r.z, sq); sq = fmaf(r.w, r.w, sq);
+                v[4 * j] = r.x * s4.x; v[4 * j + 1] = r.y * s4.y; v[4 * j + 2] = r.z * s4.z; v[4 * j + 3] = r.w * s4.w;
+            }
+        }
+        if (mod) {
+            store32((bf16*)e.mod_out + (size_t)row * e.ldm + col, v);
+            if (((col + 32) & 127) == 0) { e.sq_out[(size_t)row * SQ_SLOTS + col / 128] = sq; sq = 0.f; }
         }
         sm100::fence_proxy_async_smem();      // generic-proxy writes -> the TMA store's reads
         __syncwarp();

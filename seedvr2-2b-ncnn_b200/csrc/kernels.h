@@ -49,7 +49,27 @@ struct GemmEpi {
     const float* gate0 = nullptr;    // rows < gate_split (null: gate 1)
     const float* gate1 = nullptr;    // rows >= gate_split (null: gate 1)
     int gate_split = 0;
+    // EPI_GATE_RESID fused with the next RMSNorm + adaLN scale (bf16 operand):
+    // also mod_out[r][c] = bf16(resid_new[r][c] * sc[c]) (sc = mod_sc0 for rows
+    // < mod_split, else mod_sc1; null: 1) and per row the sum of squares of
+    // resid_new over every 128-column block: sq_out[r * SQ_SLOTS + c / 128].
+    void* mod_out = nullptr;
+    int ldm = 0;
+    const float* mod_sc0 = nullptr;
+    const float* mod_sc1 = nullptr;
+    int mod_split = 0;
+    float* sq_out = nullptr;
+    // EPI_QKV_PACK / EPI_SWIGLU on such an operand: acc is first scaled per row
+    // by rs = 1 / sqrt(sum_b sq_in[r * SQ_SLOTS + b] / rs_dim + rs_eps) (the
+    // RMSNorm, applied after the GEMM since it is one factor per row), then the
+    // bias (there: the adaLN shift folded through the weights) is added.
+    const float* sq_in = nullptr;
+    int sq_n = 0;
+    float rs_dim = 2560.f;
+    float rs_eps = 1e-5f;
 };
+// Row slots of the fused-norm partial sums of squares (2560 / 128).
+constexpr int SQ_SLOTS = 20;
 
 // C = A[M,K] (row stride lda) x W[N,K]^T (row stride ldw), fp32 accumulate,
 // fused epilogue.  SIMT kernel; any M, N, K.
@@ -104,6 +124,9 @@ void convert_to_f32(const void* src, ActT t, size_t n, float* dst, cudaStream_t 
 // destination row (r / blk_rows) * blk_stride + row_off + r % blk_rows.
 void ingest_weight(const void* src, bool src_f16, int out, int in, void* dst, ActT t, int ld, int blk_rows,
                    int blk_stride, int row_off, cudaStream_t s);
+// y[n] = sum_k W[n][k] x[k] for bf16 W (row stride ld) and fp32 x, fp32
+// accumulate in a fixed order (one warp per row).
+void gemv_bf16(const void* W, int ld, int N, int K, const float* x, float* y, cudaStream_t s);
 // Per-device one-time kernel attributes (dynamic shared memory opt-ins).
 int kernels_init_device();
 // *p = v on stream s (one thread; the value travels as a kernel argument).

@@ -156,3 +156,28 @@ def test_cfg5_2160p_layer_pair_vs_reference(prec):
             assert cos >= 0.99999 and rel <= 1e-4, (what, cos, rel)
         else:
             assert cos >= 0.9999, (what, cos, rel)
+
+
+def test_cfg2_bf16_folded_norms_vs_standalone_norms():
+    """bf16, 720p, all 32 layers: the RMSNorm + adaLN modulate folded into the
+    neighbouring GEMMs (the default: operand written by the gate/residual
+    epilogue, row factor and shift applied by the next GEMM) is as close to
+    the reference fp32 output as the standalone norm kernels
+    (S2B_NORM_FUSE=0)."""
+    g = gold("cfg2")
+    vp, txt = inputs("cfg2")
+    T, H, W = geom("cfg2")
+    res = {}
+    for fuse in ("1", "0"):
+        os.environ["S2B_NORM_FUSE"] = fuse
+        try:
+            c = ctx_for("cfg2", s2b.PREC_BF16)
+            try:
+                res[fuse] = cases.compare(c.forward(vp, T * H * W, txt, TXT, TS), g["sr"])
+            finally:
+                c.close()
+        finally:
+            os.environ.pop("S2B_NORM_FUSE", None)
+    print("folded", res["1"], "standalone", res["0"])
+    assert res["1"][0] >= res["0"][0] - 5e-5, res
+    assert res["1"][0] >= 0.9995, res
