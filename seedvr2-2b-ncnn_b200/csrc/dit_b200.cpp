@@ -340,8 +340,11 @@ int DitB200::load_weights(const char* dir_c, bool synth, uint64_t seed, int lo, 
     if (int rc = cuda_check(cudaMemcpy(branch_.p, branch.data(), branch.size() * 4, cudaMemcpyHostToDevice), "upload vectors")) return rc;
     if (int rc = cuda_check(cudaMemcpy(qknorm_.p, qkn.data(), qkn.size() * 4, cudaMemcpyHostToDevice), "upload vectors")) return rc;
     if (int rc = cuda_check(cudaMemcpy(von_w_.p, von.data(), DIM * 4, cudaMemcpyHostToDevice), "upload vectors")) return rc;
-    // folded norms: bf16 contexts whose shared layers modulate vid and txt
-    // alike (one GEMM serves both flows there)
+    // folded norms (S2B_NORM_FUSE=1): bf16 contexts whose shared layers
+    // modulate vid and txt alike (one GEMM serves both flows there).  Off by
+    // default: measured per 1080p forward, the extra work in the gate/residual
+    // and consumer epilogues (+4-6 % per GEMM launch) costs what the 62
+    // removed norm kernels saved (~1.1 ms), so the standalone kernels stay.
     {
         const char* fe = std::getenv("S2B_NORM_FUSE");
         bool same = true;
@@ -349,7 +352,7 @@ int DitB200::load_weights(const char* dir_c, bool synth, uint64_t seed, int lo, 
             for (int k : {0, 1, 3, 4})
                 same = same && std::memcmp(&branch[((size_t)(i * 12 + k)) * DIM], &branch[((size_t)(i * 12 + 6 + k)) * DIM],
                                            DIM * 4) == 0;
-        norm_fuse_ = act_ == ACT_BF16 && same && !(fe && fe[0] == '0');
+        norm_fuse_ = act_ == ACT_BF16 && same && fe && fe[0] == '1';
         shift_ok_ = false;
         if (norm_fuse_)
             if (int rc = cuda_check(shift_.ensure((size_t)NUM_LAYERS * 2 * (QKV + 2 * MLP_DIM) * 4), "cudaMalloc(shift)"))

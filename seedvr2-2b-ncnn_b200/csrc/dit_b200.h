@@ -230,7 +230,7 @@ private:
     }
 
     int dev_ = -1, prec_ = PREC_FP32;
-    // folded norms (bf16): S2B_NORM_FUSE=0 turns them off
+    // folded norms (bf16, S2B_NORM_FUSE=1; off by default, see load_weights)
     bool norm_fuse_ = false;
     DevBuf shift_;          // [32][2 flows][qkv 7680 | hg 13824] shift biases (W . adaLN shift)
     DevBuf SQ_;             // [rows][SQ_SLOTS] partial sums of squares

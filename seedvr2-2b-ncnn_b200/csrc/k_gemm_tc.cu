@@ -152,15 +152,33 @@ __device__ __forceinline__ void rope64(float* x, int d0, const float2* cs, int p
     }
 }
 
+// 32 lanes x 32 consecutive fp32 columns back into TMEM (pair with wait::st).
+__device__ __forceinline__ void tmem_st32f(uint32_t taddr, const float v[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+        ::"r"(taddr), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]),
+          "f"(v[8]), "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]),
+          "f"(v[16]), "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]),
+          "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+        : "memory");
+}
+
 // Row factor of an RMSNorm folded behind the GEMM (GemmEpi::sq_in): the
-// partial sums of squares the producing epilogue wrote, summed in order in
-// double (as the reference sums squares, src/dit_vk.cpp:48-52).
+// partial sums of squares the producing epilogue wrote (fp32 over 128
+// columns each), summed in a fixed order.  fp32 throughout: FP64 arithmetic
+// here throttled the epilogue warps on the narrow FP64 pipe.
 __device__ __forceinline__ float row_rs(const GemmEpi& e, int row, bool row_ok) {
     if (!e.sq_in || !row_ok) return 1.f;
-    const float* sq = e.sq_in + (size_t)row * SQ_SLOTS;
-    double t = 0.0;
-    for (int b = 0; b < e.sq_n; b++) t += (double)__ldg(sq + b);
-    return (float)(1.0 / sqrt(t / (double)e.rs_dim + (double)e.rs_eps));
+    const float4* sq = reinterpret_cast<const float4*>(e.sq_in + (size_t)row * SQ_SLOTS);
+    float4 q[SQ_SLOTS / 4];
+    #pragma unroll
+    for (int b = 0; b < SQ_SLOTS / 4; b++) q[b] = __ldg(sq + b);
+    float t = 0.f;
+    #pragma unroll
+    for (int b = 0; b < SQ_SLOTS / 4; b++) t += (q[b].x + q[b].y) + (q[b].z + q[b].w);
+    return 1.f / sqrtf(t / e.rs_dim + e.rs_eps);
 }
 
 // EPI_QKV_PACK: the tile's 256 columns are two heads of one of q / k / v.
@@ -196,21 +214,36 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
     for (int hh = 0; hh < BN / 128; hh++) {
         const uint32_t th = taddr + hh * 128;
         float inv = 1.f;
-        if (sec < 2) {
+        if (sec < 2 || cb) {
+            // pass 1, 32 columns at a time: a folded operand's values become
+            // rs * acc + shift in TMEM (the shift loaded before the TMEM read,
+            // so its latency is hidden), and q / k heads sum their squares
             float sq = 0.f;
-            #pragma unroll
-            for (int c = 0; c < 2; c++) {
-                float x[64];
-                sm100::tmem_ld64(th + c * 64, x);
+            #pragma unroll 1
+            for (int c = 0; c < 4; c++) {
+                float4 c4[8];
                 if (cb) {
-                    const float* cc = cb + n0 + hh * 128 + c * 64;
+                    const float4* cc = reinterpret_cast<const float4*>(cb + n0 + hh * 128 + c * 32);
                     #pragma unroll
-                    for (int d = 0; d < 64; d++) x[d] = fmaf(x[d], rs, __ldg(cc + d));
+                    for (int j = 0; j < 8; j++) c4[j] = __ldg(cc + j);
                 }
-                #pragma unroll
-                for (int d = 0; d < 64; d++) sq = fmaf(x[d], x[d], sq);
+                float x[32];
+                sm100::tmem_ld32(th + c * 32, x);
+                if (cb) {
+                    #pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        x[4 * j] = fmaf(x[4 * j], rs, c4[j].x); x[4 * j + 1] = fmaf(x[4 * j + 1], rs, c4[j].y);
+                        x[4 * j + 2] = fmaf(x[4 * j + 2], rs, c4[j].z); x[4 * j + 3] = fmaf(x[4 * j + 3], rs, c4[j].w);
+                    }
+                    tmem_st32f(th + c * 32, x);
+                }
+                if (sec < 2) {
+                    #pragma unroll
+                    for (int d = 0; d < 32; d++) sq = fmaf(x[d], x[d], sq);
+                }
             }
-            inv = 1.f / sqrtf(__fadd_rn(sq * (1.f / 128.f), k.eps));
+            if (cb) asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            if (sec < 2) inv = 1.f / sqrtf(__fadd_rn(sq * (1.f / 128.f), k.eps));
         }
         const int h = h0 + hh;
         // destination of this row: one packed slot (vid) or the first window's (txt)
@@ -222,11 +255,6 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
             float x[64];
             sm100::tmem_ld64(th + c * 64, x);
             if (!row_ok) continue;
-            if (cb) {
-                const float* cc = cb + n0 + hh * 128 + c * 64;
-                #pragma unroll
-                for (int d = 0; d < 64; d++) x[d] = fmaf(x[d], rs, __ldg(cc + d));
-            }
             if (sec < 2) {
                 #pragma unroll
                 for (int d = 0; d < 64; d += 4) {
@@ -263,20 +291,30 @@ __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, 
     if constexpr (MODE == EPI_SWIGLU) {
         // column block [h 128 | g 128] -> 128 outputs at n0 / 2
         const float rs = row_rs(e, row, row_ok);
+        const float* bias = e.bias;
         #pragma unroll 1
         for (int jc = 0; jc < 4; jc++) {
+            // folded RMSNorm (row factor) and adaLN shift (bias) of a fused
+            // operand; the shifts are loaded before the TMEM reads so their
+            // latency is hidden
+            float4 bh4[8], bg4[8];
+            if (bias) {
+                const float4* bh = reinterpret_cast<const float4*>(bias + n0 + jc * 32);
+                const float4* bg = reinterpret_cast<const float4*>(bias + n0 + 128 + jc * 32);
+                #pragma unroll
+                for (int j = 0; j < 8; j++) { bh4[j] = __ldg(bh + j); bg4[j] = __ldg(bg + j); }
+            }
             float h[32], g[32];
             sm100::tmem_ld32(taddr + jc * 32, h);
             sm100::tmem_ld32(taddr + 128 + jc * 32, g);
             if (!row_ok) continue;
-            if (e.bias) {
-                // folded RMSNorm (row factor) and adaLN shift (bias) of a fused operand
-                const float* bh = e.bias + n0 + jc * 32;
-                const float* bg = e.bias + n0 + 128 + jc * 32;
+            if (bias) {
                 #pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    h[j] = fmaf(h[j], rs, __ldg(bh + j));
-                    g[j] = fmaf(g[j], rs, __ldg(bg + j));
+                for (int j = 0; j < 8; j++) {
+                    h[4 * j] = fmaf(h[4 * j], rs, bh4[j].x); h[4 * j + 1] = fmaf(h[4 * j + 1], rs, bh4[j].y);
+                    h[4 * j + 2] = fmaf(h[4 * j + 2], rs, bh4[j].z); h[4 * j + 3] = fmaf(h[4 * j + 3], rs, bh4[j].w);
+                    g[4 * j] = fmaf(g[4 * j], rs, bg4[j].x); g[4 * j + 1] = fmaf(g[4 * j + 1], rs, bg4[j].y);
+                    g[4 * j + 2] = fmaf(g[4 * j + 2], rs, bg4[j].z); g[4 * j + 3] = fmaf(g[4 * j + 3], rs, bg4[j].w);
                 }
             }
             #pragma unroll
@@ -418,6 +456,13 @@ __device__ __forceinline__ bool epilogue_resid_tma(const TcParams& p, const CUte
     }
     for (int c = 0; c < nch; c++) {
         const int col = n0 + 32 * c;
+        // the next norm's scale, loaded ahead of the TMEM read and the box wait
+        float4 s4[8];
+        if (mod) {
+            #pragma unroll
+            for (int j = 0; j < 8; j++)
+                s4[j] = msc ? __ldg(reinterpret_cast<const float4*>(msc + col) + j) : make_float4(1.f, 1.f, 1.f, 1.f);
+        }
         float v[32];
         sm100::tmem_ld32(taddr + 32 * c, v);
         if (lane == 0) {
@@ -443,10 +488,9 @@ __device__ __forceinline__ bool epilogue_resid_tma(const TcParams& p, const CUte
             *q = r;
             if (mod) {
                 // the next RMSNorm's operand: resid * adaLN scale, and the row's sum of squares
-                const float4 s4 = msc ? __ldg(reinterpret_cast<const float4*>(msc + col) + j)
-                                      : make_float4(1.f, 1.f, 1.f, 1.f);
                 sq = fmaf(r.x, r.x, sq); sq = fmaf(r.y, r.y, sq); sq = fmaf(r.z, r.z, sq); sq = fmaf(r.w, r.w, sq);
-                v[4 * j] = r.x * s4.x; v[4 * j + 1] = r.y * s4.y; v[4 * j + 2] = r.z * s4.z; v[4 * j + 3] = r.w * s4.w;
+                v[4 * j] = r.x * s4[j].x; v[4 * j + 1] = r.y * s4[j].y;
+                v[4 * j + 2] = r.z * s4[j].z; v[4 * j + 3] = r.w * s4[j].w;
             }
         }
         if (mod) {
