@@ -284,6 +284,53 @@ def fp32_records(steps: int):
     return out
 
 
+def fp16_record(steps: int):
+    """fp16 operands (the reference's precision 1; N=1): the 1080p forward on
+    the same tcgen05 kernels with IEEE binary16 operands, the mode that meets
+    cos 0.9999 against the reference fp32 after 32 layers."""
+    import torch
+    import s2b
+    pk, src = peaks()
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+    ctx = s2b.DitB200(0, s2b.PREC_FP16)
+    try:
+        ctx.init_synth(WEIGHT_SEED, 0, 32)
+        T, H, W = GRIDS["1080p"]
+        Lv = T * H * W
+        ctx.set_windows(s2b.make_win(T, H, W, (4, 3, 3), TXT, False), s2b.make_win(T, H, W, (4, 3, 3), TXT, True))
+        vid = s2b.patchify_grid(s2b.synth_vid_grid(T, 2 * H, 2 * W, 42))
+        txt = s2b.synth_txt(TXT, 42)
+        d_vid, d_txt = torch.from_numpy(vid).to(dev), torch.from_numpy(txt).to(dev)
+        d_sr = torch.empty(Lv, 64, device=dev)
+        fwd = lambda: ctx.forward_dev(d_vid.data_ptr(), Lv, d_txt.data_ptr(), TXT, TIMESTEP, d_sr.data_ptr(),
+                                      stream.cuda_stream)
+        for _ in range(3):
+            fwd()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fwd()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / steps
+        ctx.check_errors()
+        prof = ctx.forward_profile(vid, Lv, txt, TXT, TIMESTEP)
+        g, a = prof["gemm_tcgen05"], prof["attention"]
+        gt, at = _tflops(g), _tflops(a)
+        gp, ap_ = pk.get("bf16_tflops_sustained"), pk.get("bf16_tflops")   # kind::f16 runs f16 at the bf16 rate
+        return {"workload": f"{CFG['1080p']}: 1080p 32-layer forward, fp16 operands", "grid": [T, H, W],
+                "ms_per_frame": ms, "steps": steps,
+                "gemm": {"useful_tflops": gt, "peak": gp, "frac": gt / gp if gt and gp else None,
+                         "peak_source": f"{src} bf16_tflops_sustained"},
+                "attention": {"useful_tflops": at, "peak": ap_, "frac": at / ap_ if at and ap_ else None,
+                              "peak_source": f"{src} bf16_tflops (burst)"},
+                "kernels": _kernel_table(prof)}
+    finally:
+        ctx.close()
+
+
 def image_record(ctx, args, world, rank, local, frames, txt):
     """(N>1) BASELINE cfg3 window-sharded over the ranks: one frame on all
     ranks per step, its parity against the single-GPU forward (rank 0, outside
@@ -370,7 +417,7 @@ def run_ours(args):
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=dev)
-    prec = s2b.PREC_BF16 if args.precision == "bf16" else s2b.PREC_FP32
+    prec = {"bf16": s2b.PREC_BF16, "fp16": s2b.PREC_FP16, "fp32": s2b.PREC_FP32}[args.precision]
     T, H, W = GRID
     Lv = T * H * W
     ctx = s2b.DitB200(local, prec)
@@ -456,11 +503,11 @@ def run_ours(args):
     # per-kernel profile of one forward (outside the timed region)
     prof = ctx.forward_profile(frames[0], Lv, txt, TXT, TIMESTEP, sharded=image)
     pk, src = peaks()
-    g = prof["gemm_tcgen05"] if prec == s2b.PREC_BF16 else prof["gemm_fp32"]
+    g = prof["gemm_tcgen05"] if prec != s2b.PREC_FP32 else prof["gemm_fp32"]
     gemm_tflops = _tflops(g)
     awa_tflops = _tflops(prof["attention"])
     total_prof_ms = sum(v["ms"] for v in prof.values())
-    peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")) if prec == s2b.PREC_BF16 else None
+    peak = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops")) if prec != s2b.PREC_FP32 else None
     traffic = None
     tf = os.path.join(ROOT, "profiles", "gemm_tc_traffic.json")
     if os.path.exists(tf):
@@ -468,7 +515,7 @@ def run_ours(args):
             traffic = json.load(open(tf)).get("bytes_per_launch")
         except Exception:
             traffic = None
-    roofline = {"kernel": "k_gemm_tc (tcgen05 BF16 GEMM, all Linear layers)" if prec == s2b.PREC_BF16 else "k_gemm (fp32)",
+    roofline = {"kernel": "k_gemm_tc (tcgen05 kind::f16 GEMM, all Linear layers)" if prec != s2b.PREC_FP32 else "k_gemm (fp32)",
                 "bound": "tensor", "achieved": gemm_tflops, "peak": peak, "unit": "TFLOP/s",
                 "frac": (gemm_tflops / peak) if (gemm_tflops and peak) else None,
                 "traffic": traffic, "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside the forward)",
@@ -484,9 +531,11 @@ def run_ours(args):
         image_rec = image_record(ctx, args, world, rank, local, frames, txt)
     ctx.close()
 
-    fp32 = None
+    fp32 = fp16 = None
     if world == 1 and prec == s2b.PREC_BF16 and not args.no_fp32:
         fp32 = fp32_records(max(3, min(args.steps, 10)))
+    if world == 1 and prec == s2b.PREC_BF16 and not args.no_fp16:
+        fp16 = fp16_record(max(3, min(args.steps, 10)))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -514,7 +563,8 @@ def run_ours(args):
                            "windows": [s2b.make_win(T, H, W, (4, 3, 3), TXT, False).nwin,
                                        s2b.make_win(T, H, W, (4, 3, 3), TXT, True).nwin],
                            "frames_per_step_per_gpu": 1,
-                           "l2": "no flush: every forward streams 6.7 GB of bf16 weights (> 126 MB L2)"},
+                           "l2": ("no flush: every forward streams %s GB of %s weights (> 126 MB L2)"
+                                  % (("13.4", "fp32") if prec == s2b.PREC_FP32 else ("6.7", args.precision)))},
                 "e2e": {"value": e2e_value, "unit": "ms/frame", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
                 "gpu_launches": launches_per_fwd * args.steps,
                 "roofline": roofline,
@@ -528,6 +578,8 @@ def run_ours(args):
             line["image"] = image_rec
         if fp32:
             line["fp32"] = fp32
+        if fp16:
+            line["fp16"] = fp16
         print(json.dumps(line))
     if world > 1:
         torch.distributed.destroy_process_group()
@@ -642,7 +694,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
+    ap.add_argument("--precision", choices=["bf16", "fp16", "fp32"], default="bf16")
     ap.add_argument("--res", choices=sorted(GRIDS), default="1080p",
                     help="output resolution of the workload (the metric is quoted at 1080p)")
     ap.add_argument("--mode", choices=["frames", "image"], default="frames",
@@ -651,6 +703,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the reference CPU baseline leg")
     ap.add_argument("--no-fp32", action="store_true", help="skip the fp32 sub-records (N=1)")
     ap.add_argument("--no-image", action="store_true", help="skip the window-sharded sub-record (N>1)")
+    ap.add_argument("--no-fp16", action="store_true", help="skip the fp16-operand sub-record (N=1)")
     args = ap.parse_args()
     args.warmup_ref = 0
     global GRID

@@ -47,8 +47,8 @@ int DitB200::sync_check(cudaStream_t s, const char* what) {
 }
 
 int DitB200::create(int device, int precision) {
-    if (precision == PREC_FP16) return fail(ERR_UNSUPPORTED, "fp16 operands are not offered on B200; use fp32 (0) or bf16 (2)");
-    if (precision != PREC_FP32 && precision != PREC_BF16) return fail(ERR_ARG, "precision must be 0 (fp32) or 2 (bf16)");
+    if (precision != PREC_FP32 && precision != PREC_FP16 && precision != PREC_BF16)
+        return fail(ERR_ARG, "precision must be 0 (fp32), 1 (fp16) or 2 (bf16)");
     int n = 0;
     if (int rc = cuda_check(cudaGetDeviceCount(&n), "cudaGetDeviceCount")) return rc;
     if (device < 0 || device >= n) return fail(ERR_ARG, "device index out of range");
@@ -58,7 +58,7 @@ int DitB200::create(int device, int precision) {
     if (int rc = cuda_check(cudaGetDeviceProperties(&prop, dev_), "cudaGetDeviceProperties")) return rc;
     if (prop.major != 10) return fail(ERR_UNSUPPORTED, std::string("sm_100a kernels need a B200-class GPU, found ") + prop.name);
     prec_ = precision;
-    act_ = (precision == PREC_BF16) ? ACT_BF16 : ACT_F32;
+    act_ = precision == PREC_BF16 ? ACT_BF16 : precision == PREC_FP16 ? ACT_F16 : ACT_F32;
     // fp32 attention on the tensor cores (split3 operands) unless S2B_FP32_ATTN=simt
     const char* aenv = std::getenv("S2B_FP32_ATTN");
     attn_split3_ = act_ == ACT_F32 && !(aenv && aenv[0] == 's');
@@ -545,9 +545,12 @@ void DitB200::gemm(const void* A, int lda, const Linear& L, int M, const GemmEpi
     const double flops = 2.0 * M * L.out * L.in;
     const double bytes = (double)M * L.in * act_bytes(act_) + (double)L.out * L.in * act_bytes(L.t) +
                          (double)M * L.out * (e.mode == EPI_GATE_RESID ? 8 : e.mode == EPI_SWIGLU ? act_bytes(e.out_t) / 2.0 : act_bytes(e.out_t));
-    if (act_ == ACT_BF16 && L.t == ACT_BF16 && gemm_tc_supported(M, L.out, L.in, lda, L.ld)) {
+    if (act_half(act_) && L.t == act_ && gemm_tc_supported(M, L.out, L.in, lda, L.ld)) {
+        // 16-bit operands on tcgen05: A and W are both of the context's type
         pbeg(KK_GEMM_TC, flops, bytes, s);
-        gemm_tc(A, lda, L.w.p, L.ld, M, L.out, L.in, e, s, &launches_);
+        GemmEpi et = e;
+        et.op_t = act_;
+        gemm_tc(A, lda, L.w.p, L.ld, M, L.out, L.in, et, s, &launches_);
         pend(s);
         return;
     }
@@ -570,14 +573,16 @@ void DitB200::gemm(const void* A, int lda, const Linear& L, int M, const GemmEpi
 // two launches.
 void DitB200::gemm2(const void* A0, int lda0, const Linear& L0, int M0, const GemmEpi& e0, const void* A1, int lda1,
                     const Linear& L1, int M1, const GemmEpi& e1, cudaStream_t s) {
-    if (act_ == ACT_BF16 && L0.t == ACT_BF16 && L1.t == ACT_BF16 && M0 > 128 && M1 > 0 && L0.out == L1.out &&
+    if (act_half(act_) && L0.t == act_ && L1.t == act_ && M0 > 128 && M1 > 0 && L0.out == L1.out &&
         L0.in == L1.in && gemm_tc_supported(M0, L0.out, L0.in, lda0, L0.ld) &&
         gemm_tc_supported(M1, L1.out, L1.in, lda1, L1.ld)) {
         const double flops = 2.0 * (M0 + M1) * L0.out * L0.in;
         const double bytes = (double)(M0 + M1) * L0.in * act_bytes(act_) + 2.0 * L0.out * L0.in * act_bytes(L0.t) +
                              (double)(M0 + M1) * L0.out * (e0.mode == EPI_GATE_RESID ? 8 : e0.mode == EPI_SWIGLU ? act_bytes(e0.out_t) / 2.0 : act_bytes(e0.out_t));
         pbeg(KK_GEMM_TC, flops, bytes, s);
-        const int rc = gemm_tc_grouped(A0, lda0, L0.w.p, L0.ld, M0, e0, A1, lda1, L1.w.p, L1.ld, M1, e1, L0.out,
+        GemmEpi f0 = e0, f1 = e1;
+        f0.op_t = f1.op_t = act_;
+        const int rc = gemm_tc_grouped(A0, lda0, L0.w.p, L0.ld, M0, f0, A1, lda1, L1.w.p, L1.ld, M1, f1, L0.out,
                                        L0.in, s, &launches_);
         pend(s);
         if (rc == 0) return;
@@ -726,7 +731,7 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
         e.sq_out = B.SQ + (size_t)row0 * SQ_SLOTS;
     };
     // 2. qkv projection (no bias), then qk-norm + RoPE + window packing
-    const bool fused_pack = act_ == ACT_BF16 && BV.qkv.t == ACT_BF16 && G.structured &&
+    const bool fused_pack = act_half(act_) && BV.qkv.t == act_ && G.structured &&
                             G.cs.bytes >= (size_t)G.npos * 21 * sizeof(float2) &&
                             gemm_tc_supported(M, QKV, DIM, DIM, DIM);
     if (fused_pack) {
@@ -736,7 +741,7 @@ int DitB200::enqueue_layer_on(int i, int Lv, int TXT, cudaStream_t s, const Laye
         k.tokpos = G.tokpos.as<const int4>(); k.cums = G.view.cums; k.cs = G.cs.as<const float2>(); k.npos = G.npos;
         k.nq0 = normw(i, 0, 0); k.nk0 = normw(i, 0, 1); k.nq1 = normw(i, 1, 0); k.nk1 = normw(i, 1, 1);
         k.eps = NORM_EPS; k.Lv = Lv; k.TXT = TXT; k.nwin = G.view.nwin; k.sumS = G.view.sumS;
-        k.Qp = B.Qp; k.Kp = B.Kp; k.Vp = B.Vp;
+        k.Qp = B.Qp; k.Kp = B.Kp; k.Vp = B.Vp; k.qkv_t = act_;
         if (dual) {
             GemmEpi et = e;
             k.row_base = 0; et.pk.row_base = Lv;

@@ -259,6 +259,12 @@ void awa_pack(const void* vqkv, const void* tqkv, ActT in_t, int ldq, const AwaD
     else if (in_t == ACT_F32 && pt == ACT_BF16)
         k_awa_pack<float, bf16><<<g.sumS, 640, 0, s>>>((const float*)vqkv, (const float*)tqkv, ldq, g, nqv, nkv,
                                                        nqt, nkt, eps, (bf16*)Qp, (bf16*)Kp, (bf16*)Vp);
+    else if (in_t == ACT_F16 && pt == ACT_F16)
+        k_awa_pack<f16, f16><<<g.sumS, 640, 0, s>>>((const f16*)vqkv, (const f16*)tqkv, ldq, g, nqv, nkv,
+                                                    nqt, nkt, eps, (f16*)Qp, (f16*)Kp, (f16*)Vp);
+    else if (in_t == ACT_F32 && pt == ACT_F16)
+        k_awa_pack<float, f16><<<g.sumS, 640, 0, s>>>((const float*)vqkv, (const float*)tqkv, ldq, g, nqv, nkv,
+                                                      nqt, nkt, eps, (f16*)Qp, (f16*)Kp, (f16*)Vp);
     else
         k_awa_pack<bf16, float><<<g.sumS, 640, 0, s>>>((const bf16*)vqkv, (const bf16*)tqkv, ldq, g, nqv, nkv,
                                                        nqt, nkt, eps, (float*)Qp, (float*)Kp, (float*)Vp);
@@ -276,16 +282,16 @@ void awa_pack_split3(const void* vqkv, const void* tqkv, ActT in_t, int ldq, con
                                                             nqt, nkt, eps, (bf16*)Q3, (bf16*)K3, (bf16*)V3);
 }
 
-int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, const AwaDev& g, float scale, void* att, int ld_att,
-                  ActT at, float* toutw, cudaStream_t s);
+int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, ActT qkv_t, const AwaDev& g, float scale, void* att,
+                  int ld_att, ActT at, float* toutw, cudaStream_t s);
 
 int awa_attend(const void* Qp, const void* Kp, const void* Vp, ActT pt, const AwaDev& g, float scale,
                void* att, int ld_att, ActT at, float* toutw, cudaStream_t s, int* launches) {
     if (g.nwin <= 0) return 0;
-    // bf16 operands: the tensor-core kernel (k_awa_tc.cu), and nothing else;
-    // fp32 operands: the SIMT kernel below
-    if (pt == ACT_BF16) {
-        if (awa_attend_tc(Qp, Kp, Vp, g, scale, att, ld_att, at, toutw, s) != 0) return -1;
+    // 16-bit operands (bf16 or f16): the tensor-core kernel (k_awa_tc.cu),
+    // and nothing else; fp32 operands: the SIMT kernel below
+    if (act_half(pt)) {
+        if (awa_attend_tc(Qp, Kp, Vp, pt, g, scale, att, ld_att, at, toutw, s) != 0) return -1;
         if (launches) (*launches)++;
         return 0;
     }
@@ -323,6 +329,7 @@ void awa_coalesce_div(const float* toutw, int nwin, int TXT, void* att_txt, int 
     if (n <= 0 || nwin <= 0) return;
     const int n4 = n / 4;
     if (at == ACT_F32) k_coalesce<float><<<(n4 + 127) / 128, 128, 0, s>>>(toutw, nwin, TXT, (float*)att_txt, ld_att, divisor);
+    else if (at == ACT_F16) k_coalesce<f16><<<(n4 + 127) / 128, 128, 0, s>>>(toutw, nwin, TXT, (f16*)att_txt, ld_att, divisor);
     else k_coalesce<bf16><<<(n4 + 127) / 128, 128, 0, s>>>(toutw, nwin, TXT, (bf16*)att_txt, ld_att, divisor);
 }
 

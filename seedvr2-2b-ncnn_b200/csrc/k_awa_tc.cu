@@ -43,7 +43,7 @@ struct AttnParams {
     float scale_log2;     // softmax scale * log2(e)
     void* att;            // vid rows: [Lv][ld_att] in att_t
     int ld_att;
-    int att_bf16;
+    ActT att_t;           // ACT_F32, ACT_BF16 or ACT_F16
     float* toutw;         // txt rows: [nwin][TXT][2560] fp32
 };
 
@@ -84,6 +84,13 @@ __device__ __forceinline__ uint32_t pack_bf16x2_rn(float a, float b) {
     __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&v);
 }
+// The same in IEEE binary16 (the fp16 operand mode's P).
+__device__ __forceinline__ uint32_t pack_f16x2_rn(float a, float b) {
+    __half2 v = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+// kind::f16 A / B format fields (bits 7-9, 10-12): 1 = bf16, 0 = f16
+constexpr uint32_t idesc_f16(uint32_t idesc_bf16) { return idesc_bf16 & ~((7u << 7) | (7u << 10)); }
 
 // Max of n (<= 64) leading values of v, -inf for the rest, through 8
 // independent accumulators (a chain of 8 instead of 64 dependent fmaxf).
@@ -228,7 +235,7 @@ __device__ __forceinline__ float max64_full(const float* v) {
 }
 
 // NP of every 4 exponential pairs on the FMA pipe (ex2_poly2), the rest on MUFU.
-template <int NP>
+template <int NP, bool F16>
 __global__ void __launch_bounds__(T4_THREADS, 2)
 k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CUtensorMap tK,
                const __grid_constant__ CUtensorMap tV, const AttnParams p) {
@@ -348,7 +355,8 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
                     const uint32_t aoff = (kk >> 2) * HALF_BYTES + (kk & 3) * 32;
                     const uint32_t boff = (kk >> 2) * KV4_HALF + (kk & 3) * 32;
                     sm100::mma_bf16(tmem + (j & 1) * 64, sm100::desc_kmajor_sw128(sQ, aoff),
-                                    sm100::desc_kmajor_sw128(k, boff), IDESC_QK4, kk != 0);
+                                    sm100::desc_kmajor_sw128(k, boff), F16 ? idesc_f16(IDESC_QK4) : IDESC_QK4,
+                                    kk != 0);
                 }
                 sm100::mma_commit(&ctl->s_full[j & 1]);
                 sm100::mma_commit(&ctl->k_empty[j & 1]);
@@ -373,8 +381,8 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
                 const uint8_t* v = sV + st * KV4_BYTES;
                 #pragma unroll
                 for (int kk = 0; kk < KT4 / 16; kk++)
-                    sm100::mma_bf16_tmem_a(tO, tmem + st * 64 + kk * 8, desc_v64(v, kk * 2048), IDESC_PV,
-                                           (j | kk) != 0);
+                    sm100::mma_bf16_tmem_a(tO, tmem + st * 64 + kk * 8, desc_v64(v, kk * 2048),
+                                           F16 ? idesc_f16(IDESC_PV) : IDESC_PV, (j | kk) != 0);
                 sm100::mma_commit(&ctl->pv_done);
                 sm100::mma_commit(&ctl->v_empty[st]);
                 if (j + 1 == nkt) sm100::mma_commit(&ctl->o_full);
@@ -425,7 +433,7 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
                         m = mn;
                     }
                 }
-                // P_j as packed bf16 pairs over the slot's columns [0, 32)
+                // P_j as packed 16-bit pairs (the operand type) over the slot's columns [0, 32)
                 const uint64_t sl2 = f2pack(sl, sl), nm2 = f2pack(-m, -m);
                 uint32_t pk[32];
                 uint64_t ls[4];
@@ -445,7 +453,7 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
                     }
                     if (!full) { a = (2 * u < kvalid) ? a : 0.f; b = (2 * u + 1 < kvalid) ? b : 0.f; }
                     ls[u & 3] = fadd2(ls[u & 3], f2pack(a, b));
-                    pk[u] = pack_bf16x2_rn(a, b);
+                    pk[u] = F16 ? pack_f16x2_rn(a, b) : pack_bf16x2_rn(a, b);
                 }
                 float s8[8];
                 #pragma unroll
@@ -487,8 +495,10 @@ k_awa_attn_tc4(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ C
                 const float4 x = *reinterpret_cast<const float4*>(stage + rr * STG_LD + lane * 4);
                 const float xv[4] = {x.x, x.y, x.z, x.w};
                 if (q < f) {
-                    if (p.att_bf16)
+                    if (p.att_t == ACT_BF16)
                         store4((bf16*)p.att + (size_t)tok * p.ld_att + h * D + lane * 4, xv);
+                    else if (p.att_t == ACT_F16)
+                        store4((f16*)p.att + (size_t)tok * p.ld_att + h * D + lane * 4, xv);
                     else
                         store4((float*)p.att + (size_t)tok * p.ld_att + h * D + lane * 4, xv);
                 } else {
@@ -784,8 +794,10 @@ k_awa_attn_x3(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CU
                 const float4 x = *reinterpret_cast<const float4*>(stage + rr * STG_LD + lane * 4);
                 const float xv[4] = {x.x, x.y, x.z, x.w};
                 if (q < f) {
-                    if (p.att_bf16)
+                    if (p.att_t == ACT_BF16)
                         store4((bf16*)p.att + (size_t)tok * p.ld_att + h * D + lane * 4, xv);
+                    else if (p.att_t == ACT_F16)
+                        store4((f16*)p.att + (size_t)tok * p.ld_att + h * D + lane * 4, xv);
                     else
                         store4((float*)p.att + (size_t)tok * p.ld_att + h * D + lane * 4, xv);
                 } else {
@@ -806,8 +818,9 @@ k_awa_attn_x3(const __grid_constant__ CUtensorMap tQ, const __grid_constant__ CU
 
 bool awa_tc_available() { return true; }
 
-int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, const AwaDev& g, float scale, void* att, int ld_att,
-                  ActT at, float* toutw, cudaStream_t s) {
+int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, ActT qkv_t, const AwaDev& g, float scale, void* att,
+                  int ld_att, ActT at, float* toutw, cudaStream_t s) {
+    if (qkv_t != ACT_BF16 && qkv_t != ACT_F16) return -1;
     const int rows = 20 * g.sumS;
     CUtensorMap tq, tk, tv;
     if (!make_tmap_bf16(&tq, Qp, rows, D, D, QT, 64) || !make_tmap_bf16(&tk, Kp, rows, D, D, KT4, 64) ||
@@ -818,14 +831,20 @@ int awa_attend_tc(const void* Qp, const void* Kp, const void* Vp, const AwaDev& 
     p.scale_log2 = scale * 1.4426950408889634f;
     p.att = att;
     p.ld_att = ld_att;
-    p.att_bf16 = (at == ACT_BF16);
+    p.att_t = at;
     p.toutw = toutw;
     {
         dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
         const int np = awa_tc_poly_exp();
-        if (np == 2) k_awa_attn_tc4<2><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk, tv, p);
-        else if (np == 1) k_awa_attn_tc4<1><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk, tv, p);
-        else k_awa_attn_tc4<0><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk, tv, p);
+        if (qkv_t == ACT_F16) {
+            if (np == 2) k_awa_attn_tc4<2, true><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk, tv, p);
+            else if (np == 1) k_awa_attn_tc4<1, true><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk, tv, p);
+            else k_awa_attn_tc4<0, true><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk, tv, p);
+        } else {
+            if (np == 2) k_awa_attn_tc4<2, false><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk, tv, p);
+            else if (np == 1) k_awa_attn_tc4<1, false><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk, tv, p);
+            else k_awa_attn_tc4<0, false><<<grid, T4_THREADS, T4_SMEM, s>>>(tq, tk, tv, p);
+        }
     }
     return 0;
 }
@@ -842,7 +861,7 @@ int awa_attend_split3(const void* Q3, const void* K3, const void* V3, const AwaD
     p.scale_log2 = scale * 1.4426950408889634f;
     p.att = att;
     p.ld_att = ld_att;
-    p.att_bf16 = (at == ACT_BF16);
+    p.att_t = at;
     p.toutw = toutw;
     dim3 grid((g.maxS + QT - 1) / QT, 20, g.nwin);
     k_awa_attn_x3<<<grid, T4_THREADS, X3_SMEM, s>>>(tq, tk, tv, p);
@@ -852,8 +871,9 @@ int awa_attend_split3(const void* Q3, const void* K3, const void* V3, const AwaD
 int awa_tc_init_device() {
     if (cudaError_t e = cudaFuncSetAttribute(k_awa_attn_x3, cudaFuncAttributeMaxDynamicSharedMemorySize, X3_SMEM))
         return (int)e;
-    const void* v4[3] = {(const void*)k_awa_attn_tc4<0>, (const void*)k_awa_attn_tc4<1>,
-                         (const void*)k_awa_attn_tc4<2>};
+    const void* v4[6] = {(const void*)k_awa_attn_tc4<0, false>, (const void*)k_awa_attn_tc4<1, false>,
+                         (const void*)k_awa_attn_tc4<2, false>, (const void*)k_awa_attn_tc4<0, true>,
+                         (const void*)k_awa_attn_tc4<1, true>, (const void*)k_awa_attn_tc4<2, true>};
     for (const void* k : v4)
         if (cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, T4_SMEM)) return (int)e;
     return 0;

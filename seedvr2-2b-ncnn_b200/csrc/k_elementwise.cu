@@ -220,12 +220,16 @@ void rmsnorm_mod(const float* X, int ldx, int rows, int split, const float* sc0,
         const int blocks = (rows + NORM_ROWS - 1) / NORM_ROWS;
         if (yt == ACT_F32)
             k_rmsnorm_mod_w<float><<<blocks, NORM_ROWS * 32, 0, s>>>(X, ldx, rows, split, sc0, sh0, sc1, sh1, affine, eps, (float*)Y, ldy);
+        else if (yt == ACT_F16)
+            k_rmsnorm_mod_w<f16><<<blocks, NORM_ROWS * 32, 0, s>>>(X, ldx, rows, split, sc0, sh0, sc1, sh1, affine, eps, (f16*)Y, ldy);
         else
             k_rmsnorm_mod_w<bf16><<<blocks, NORM_ROWS * 32, 0, s>>>(X, ldx, rows, split, sc0, sh0, sc1, sh1, affine, eps, (bf16*)Y, ldy);
         return;
     }
     if (yt == ACT_F32)
         k_rmsnorm_mod<float><<<rows, NORM_THREADS, 0, s>>>(X, ldx, split, sc0, sh0, sc1, sh1, affine, eps, (float*)Y, ldy);
+    else if (yt == ACT_F16)
+        k_rmsnorm_mod<f16><<<rows, NORM_THREADS, 0, s>>>(X, ldx, split, sc0, sh0, sc1, sh1, affine, eps, (f16*)Y, ldy);
     else
         k_rmsnorm_mod<bf16><<<rows, NORM_THREADS, 0, s>>>(X, ldx, split, sc0, sh0, sc1, sh1, affine, eps, (bf16*)Y, ldy);
 }
@@ -235,6 +239,7 @@ void swiglu_rows(const float* HG, int M, int ldhg, void* Hs, int ldh, ActT ht, c
     const size_t n = (size_t)M * (6912 / 4);
     const int blocks = (int)((n + 255) / 256);
     if (ht == ACT_F32) k_swiglu<float><<<blocks, 256, 0, s>>>(HG, M, ldhg, (float*)Hs, ldh);
+    else if (ht == ACT_F16) k_swiglu<f16><<<blocks, 256, 0, s>>>(HG, M, ldhg, (f16*)Hs, ldh);
     else k_swiglu<bf16><<<blocks, 256, 0, s>>>(HG, M, ldhg, (bf16*)Hs, ldh);
 }
 
@@ -249,6 +254,7 @@ void pad_convert_rows(const float* src, int rows, int cols, void* dst, int ld_ds
     if (!n) return;
     const int blocks = (int)((n + 255) / 256);
     if (t == ACT_F32) k_pad_convert<float><<<blocks, 256, 0, s>>>(src, rows, cols, (float*)dst, ld_dst);
+    else if (t == ACT_F16) k_pad_convert<f16><<<blocks, 256, 0, s>>>(src, rows, cols, (f16*)dst, ld_dst);
     else k_pad_convert<bf16><<<blocks, 256, 0, s>>>(src, rows, cols, (bf16*)dst, ld_dst);
 }
 
@@ -260,6 +266,7 @@ void convert_to_f32(const void* src, ActT t, size_t n, float* dst, cudaStream_t 
     if (!n) return;
     const int blocks = (int)((n + 255) / 256);
     if (t == ACT_F32) cudaMemcpyAsync(dst, src, n * 4, cudaMemcpyDeviceToDevice, s);
+    else if (t == ACT_F16) k_to_f32<f16><<<blocks, 256, 0, s>>>((const f16*)src, n, dst);
     else k_to_f32<bf16><<<blocks, 256, 0, s>>>((const bf16*)src, n, dst);
 }
 
@@ -274,6 +281,7 @@ void ingest_weight(const void* src, bool src_f16, int out, int in, void* dst, Ac
     const size_t n = (size_t)out * ld;
     const int blocks = (int)((n + 255) / 256);
     if (t == ACT_F32) k_ingest<float><<<blocks, 256, 0, s>>>(src, src_f16, out, in, (float*)dst, ld, blk_rows, blk_stride, row_off);
+    else if (t == ACT_F16) k_ingest<f16><<<blocks, 256, 0, s>>>(src, src_f16, out, in, (f16*)dst, ld, blk_rows, blk_stride, row_off);
     else k_ingest<bf16><<<blocks, 256, 0, s>>>(src, src_f16, out, in, (bf16*)dst, ld, blk_rows, blk_stride, row_off);
 }
 

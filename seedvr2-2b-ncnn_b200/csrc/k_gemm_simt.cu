@@ -90,6 +90,8 @@ k_gemm(const TA* __restrict__ A, int lda, const TW* __restrict__ W, int ldw, int
                 *dst = __fadd_rn(v, *dst);
             } else if (e.out_t == ACT_F32) {
                 ((float*)e.out)[(size_t)r * e.ldo + c] = v;
+            } else if (e.out_t == ACT_F16) {
+                ((f16*)e.out)[(size_t)r * e.ldo + c] = __float2half_rn(v);
             } else {
                 ((bf16*)e.out)[(size_t)r * e.ldo + c] = __float2bfloat16_rn(v);
             }
@@ -143,6 +145,8 @@ void gemm_simt(const void* A, ActT at, int lda, const void* W, ActT wt, int ldw,
         k_gemm<float, float><<<grid, 256, 0, s>>>((const float*)A, lda, (const float*)W, ldw, M, N, K, e);
     else if (at == ACT_BF16 && wt == ACT_BF16)
         k_gemm<bf16, bf16><<<grid, 256, 0, s>>>((const bf16*)A, lda, (const bf16*)W, ldw, M, N, K, e);
+    else if (at == ACT_F16 && wt == ACT_F16)
+        k_gemm<f16, f16><<<grid, 256, 0, s>>>((const f16*)A, lda, (const f16*)W, ldw, M, N, K, e);
     else if (at == ACT_F32 && wt == ACT_BF16)
         k_gemm<float, bf16><<<grid, 256, 0, s>>>((const float*)A, lda, (const bf16*)W, ldw, M, N, K, e);
     else

@@ -49,6 +49,11 @@ constexpr int A1_BYTES = BM1 * BK * 2, B1_BYTES = BN1 * BK * 2, STAGE1_BYTES = A
 constexpr int RBOX_BYTES = 32 * 32 * 4, RES_BYTES = 4 * 2 * RBOX_BYTES;
 constexpr int SMEM1_BYTES = STAGES1 * STAGE1_BYTES + RES_BYTES + 1024 + 512;
 constexpr uint32_t IDESC1 = sm100::idesc_bf16_f32(BM1, BN1);
+// kind::f16 A / B format fields (bits 7-9, 10-12): 1 = bf16, 0 = f16
+constexpr uint32_t IDESC_AB_FMT = (7u << 7) | (7u << 10);
+__host__ __device__ constexpr uint32_t idesc_for(uint32_t idesc_bf16, int op_f16) {
+    return op_f16 ? (idesc_bf16 & ~IDESC_AB_FMT) : idesc_bf16;
+}
 
 // CTA-pair kernel: per CTA 128 rows of A and 128 rows of B per stage
 // Tiles of BM2 x BN rows per pair (BN = 256, or 128 where 256-wide tiles
@@ -110,6 +115,17 @@ __device__ __forceinline__ void store32(float* dst, const float v[32]) {
     #pragma unroll
     for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
 }
+__device__ __forceinline__ void store32(f16* dst, const float v[32]) {
+    #pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+        uint4 u;
+        __half2 a = __floats2half2_rn(v[j], v[j + 1]), b = __floats2half2_rn(v[j + 2], v[j + 3]);
+        __half2 c = __floats2half2_rn(v[j + 4], v[j + 5]), d = __floats2half2_rn(v[j + 6], v[j + 7]);
+        u.x = *reinterpret_cast<uint32_t*>(&a); u.y = *reinterpret_cast<uint32_t*>(&b);
+        u.z = *reinterpret_cast<uint32_t*>(&c); u.w = *reinterpret_cast<uint32_t*>(&d);
+        *reinterpret_cast<uint4*>(dst + j) = u;
+    }
+}
 __device__ __forceinline__ void store32(bf16* dst, const float v[32]) {
     #pragma unroll
     for (int j = 0; j < 32; j += 8) {
@@ -120,6 +136,11 @@ __device__ __forceinline__ void store32(bf16* dst, const float v[32]) {
         u.z = *reinterpret_cast<uint32_t*>(&c); u.w = *reinterpret_cast<uint32_t*>(&d);
         *reinterpret_cast<uint4*>(dst + j) = u;
     }
+}
+// 32 values to a row of the 16-bit operand type t (bf16 or f16)
+__device__ __forceinline__ void store32h(void* dst, ActT t, const float v[32]) {
+    if (t == ACT_F16) store32((f16*)dst, v);
+    else store32((bf16*)dst, v);
 }
 
 // Pull this thread's residual row segment of a tile into L2 ahead of its
@@ -195,7 +216,7 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
     const bool vid = gr < k.Lv;
     const int sec = n0 / 2560;                     // 0 q, 1 k, 2 v
     const int h0 = (n0 % 2560) / 128;
-    bf16* base = (bf16*)(sec == 0 ? k.Qp : sec == 1 ? k.Kp : k.Vp);
+    uint16_t* base = (uint16_t*)(sec == 0 ? k.Qp : sec == 1 ? k.Kp : k.Vp);   // 16-bit elements of k.qkv_t
     int gi = 0, wi = 0, ti = 0, p0 = 0, p1 = 0, p2 = 0;
     if (row_ok && vid) {
         const int4 tp = k.tokpos[gr];
@@ -247,7 +268,7 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
         }
         const int h = h0 + hh;
         // destination of this row: one packed slot (vid) or the first window's (txt)
-        bf16* dst0 = nullptr;
+        uint16_t* dst0 = nullptr;
         if (vid) dst0 = base + ((size_t)h * k.sumS + gi + (size_t)wi * k.TXT) * 128;
         else dst0 = base + ((size_t)h * k.sumS + k.cums[1] - k.TXT + ti) * 128;
         #pragma unroll 1
@@ -264,14 +285,14 @@ __device__ __forceinline__ void epilogue_qkv_pack(const TcParams& p, uint32_t ta
                 }
                 rope64(x, c * 64, cs, p0, p1, p2);
             }
-            store32(dst0 + c * 64, x);
-            store32(dst0 + c * 64 + 32, x + 32);
+            store32h(dst0 + c * 64, k.qkv_t, x);
+            store32h(dst0 + c * 64 + 32, k.qkv_t, x + 32);
         }
         if (!row_ok || vid) continue;
         // txt row: the same rotated head in every window's slot
         #pragma unroll 1
         for (int wj = 1; wj < k.nwin; wj++) {
-            bf16* dst = base + ((size_t)h * k.sumS + k.cums[wj + 1] - k.TXT + ti) * 128;
+            uint16_t* dst = base + ((size_t)h * k.sumS + k.cums[wj + 1] - k.TXT + ti) * 128;
             #pragma unroll
             for (int c = 0; c < 16; c++)
                 reinterpret_cast<uint4*>(dst)[c] = reinterpret_cast<const uint4*>(dst0)[c];
@@ -320,7 +341,7 @@ __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, 
             #pragma unroll
             for (int j = 0; j < 32; j++) h[j] = __fmul_rn(silu_f(g[j]), h[j]);
             const size_t off = (size_t)row * e.ldo + n0 / 2 + jc * 32;
-            if (e.out_t == ACT_BF16) store32((bf16*)e.out + off, h);
+            if (act_half(e.out_t)) store32h((uint16_t*)e.out + off, e.out_t, h);
             else store32((float*)e.out + off, h);
         }
         return;
@@ -400,11 +421,12 @@ __device__ __forceinline__ void epilogue_row(const TcParams& p, uint32_t taddr, 
             {
                 const size_t off = (size_t)row * e.ldo + col;
                 if (full) {
-                    if (e.out_t == ACT_BF16) store32((bf16*)e.out + off, v);
+                    if (act_half(e.out_t)) store32h((uint16_t*)e.out + off, e.out_t, v);
                     else store32((float*)e.out + off, v);
                 } else {
                     for (int j = 0; j < 32 && col + j < p.N; j++) {
                         if (e.out_t == ACT_BF16) ((bf16*)e.out)[off + j] = __float2bfloat16_rn(v[j]);
+                        else if (e.out_t == ACT_F16) ((f16*)e.out)[off + j] = __float2half_rn(v[j]);
                         else ((float*)e.out)[off + j] = v[j];
                     }
                 }
@@ -591,6 +613,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
         }
     } else if (warp == 1) {
         if (lane == 0) {
+            const uint32_t idesc1 = idesc_for(IDESC1, p.e.op_t == ACT_F16);
             uint32_t stage = 0, phase = 0;
             int it = 0;
             bool ok = true;
@@ -608,7 +631,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtens
                     #pragma unroll
                     for (int kk = 0; kk < BK / 16; kk++)
                         sm100::mma_bf16(d, sm100::desc_kmajor_sw128(a, kk * 32), sm100::desc_kmajor_sw128(b, kk * 32),
-                                        IDESC1, (kb | kk) != 0);
+                                        idesc1, (kb | kk) != 0);
                     sm100::mma_commit(&ctl->empty[stage]);
                     if (++stage == STAGES1) { stage = 0; phase ^= 1; }
                 }
@@ -768,6 +791,7 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
         }
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
+            const uint32_t idesc16 = idesc_for(C::IDESC, p0.e.op_t == ACT_F16);   // groups share the operand type
             uint32_t bs = 0, phase = 0;
             int it = 0;
             bool ok = true;
@@ -791,7 +815,7 @@ k_gemm_tc_pair(const __grid_constant__ PairMaps maps, const __grid_constant__ Tc
                             #pragma unroll
                             for (int kk = 0; kk < BK / 16; kk++)
                                 sm100::mma_bf16_pair(d, sm100::desc_kmajor_sw128(a, kk * 32),
-                                                     sm100::desc_kmajor_sw128(b, kk * 32), C::IDESC, (kb | kk) != 0);
+                                                     sm100::desc_kmajor_sw128(b, kk * 32), idesc16, (kb | kk) != 0);
                         } else {
                             const uint8_t* al = a + C::A_TILE;
                             const uint8_t* bl = b + C::B_TILE;
@@ -928,6 +952,8 @@ static bool gemm_args_ok(const void* A, int lda, const void* W, int ldw, int M, 
     if (((uintptr_t)A & 15) || ((uintptr_t)W & 15)) return false;
     if (e.mode == EPI_SWIGLU && N % 256) return false;
     if (e.mode == EPI_QKV_PACK && N != 3 * 2560) return false;
+    if (e.op_t != ACT_BF16 && e.op_t != ACT_F16) return false;
+    if (e.mode == EPI_QKV_PACK && e.pk.qkv_t != ACT_BF16 && e.pk.qkv_t != ACT_F16) return false;
     return true;
 }
 
@@ -1075,7 +1101,7 @@ int gemm_tf32x3(const void* A2, int lda2, const void* W2, int ldw2, int M, int N
 int gemm_tc_grouped(const void* A0, int lda0, const void* W0, int ldw0, int M0, const GemmEpi& e0, const void* A1,
                     int lda1, const void* W1, int ldw1, int M1, const GemmEpi& e1, int N, int K, cudaStream_t s,
                     int* launches) {
-    if (e0.mode != e1.mode || M0 <= 0 || M1 <= 0) return -1;
+    if (e0.mode != e1.mode || e0.op_t != e1.op_t || M0 <= 0 || M1 <= 0) return -1;
     if (!gemm_args_ok(A0, lda0, W0, ldw0, M0, N, K, e0) || !gemm_args_ok(A1, lda1, W1, ldw1, M1, N, K, e1)) return -1;
     PairMaps maps;
     TcParams p0, p1;

@@ -144,6 +144,7 @@ void shard_txt_reduce(const ShardPeers& P, const uint32_t* epoch, int layer, int
     const int n = TXT * 2560;
     const int blocks = 64;
     if (t == ACT_F32) k_txt_reduce<float><<<blocks, 256, 0, s>>>(P, epoch, layer, n, divisor, (float*)out, ld);
+    else if (t == ACT_F16) k_txt_reduce<f16><<<blocks, 256, 0, s>>>(P, epoch, layer, n, divisor, (f16*)out, ld);
     else k_txt_reduce<bf16><<<blocks, 256, 0, s>>>(P, epoch, layer, n, divisor, (bf16*)out, ld);
 }
 

@@ -6,8 +6,11 @@
 
 namespace s2b {
 
-enum ActT { ACT_F32 = 0, ACT_BF16 = 1 };
-inline size_t act_bytes(ActT t) { return t == ACT_F32 ? 4 : 2; }
+// Operand types: fp32, and the two 16-bit types of the tensor cores' kind::f16
+// (bf16 for the bf16 precision, IEEE binary16 for the fp16 precision).
+enum ActT { ACT_F32 = 0, ACT_BF16 = 1, ACT_F16 = 2 };
+__host__ __device__ inline size_t act_bytes(ActT t) { return t == ACT_F32 ? 4 : 2; }
+__host__ __device__ inline bool act_half(ActT t) { return t != ACT_F32; }
 
 // ---------------------------------------------------------------- GEMM
 enum EpiMode {
@@ -34,12 +37,14 @@ struct PackEpi {
     const float *nq1 = nullptr, *nk1 = nullptr;     // txt flow
     float eps = 1e-5f;
     int Lv = 0, TXT = 0, nwin = 0, sumS = 0, row_base = 0;
-    void *Qp = nullptr, *Kp = nullptr, *Vp = nullptr;   // bf16 [20][sumS][128]
+    void *Qp = nullptr, *Kp = nullptr, *Vp = nullptr;   // [20][sumS][128] in qkv_t
+    ActT qkv_t = ACT_BF16;                              // ACT_BF16 or ACT_F16
 };
 
 struct GemmEpi {
     PackEpi pk;
     EpiMode mode = EPI_STORE;
+    ActT op_t = ACT_BF16;            // tcgen05 kernels: the 16-bit type of A and W (both the same)
     const float* bias = nullptr;     // [N] or null
     void* out = nullptr;             // STORE / SWIGLU output
     int ldo = 0;

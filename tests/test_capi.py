@@ -36,10 +36,11 @@ def test_ctx_create_without_gpu_fails_loudly():
         s2b.DitB200(0, s2b.PREC_FP32)
 
 
-def test_fp16_precision_is_rejected_before_device_work():
-    ctx = ctypes.c_void_p()
-    rc = s2b.lib().s2b_ctx_create(0, s2b.PREC_FP16, ctypes.byref(ctx))
-    assert rc != 0 and not ctx
+def test_unknown_precision_is_rejected_before_device_work():
+    for prec in (-1, 3, 7):
+        ctx = ctypes.c_void_p()
+        rc = s2b.lib().s2b_ctx_create(0, prec, ctypes.byref(ctx))
+        assert rc == 1 and not ctx          # S2B_ERR_ARG, whether or not a GPU is present
 
 
 def test_make_win_argument_validation():

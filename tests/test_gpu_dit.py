@@ -86,14 +86,52 @@ def test_fp32_last_layers_vs_port(port, m5_small, inputs):
     c.close()
 
 
-def test_bf16_vs_fp32_reference(m5_small, inputs):
+@pytest.mark.parametrize("prec", [s2b.PREC_BF16, s2b.PREC_FP16], ids=["bf16", "fp16"])
+def test_half_vs_fp32_reference(m5_small, inputs, prec):
     vp, txt = inputs[:2]
     g = np.load(os.path.join(GOLD, "dit_small.npz"))
-    c = make_ctx(s2b.PREC_BF16, m5_small, 0, 2, inputs)
+    c = make_ctx(prec, m5_small, 0, 2, inputs)
     _, _, sr = c.forward_latent(vp, Lv, txt, TXT, TS, 0, 2, True, True)
     cos, rel = cases.compare(sr, g["sr01"])
     assert cos >= 0.9999, (cos, rel)
     c.close()
+
+
+# GPU 16-bit path against the port with the same operand rounding emulated
+# (GEMM operands, Q/K/V and P rounded to the type, fp32 arithmetic): per
+# layer, each fed the port's input.  What is left is fp32 summation order and
+# the point where P is rounded (before normalisation here, after it in the
+# port).
+# Measured worst (720p-like 24x28 grid, layers 0-1): bf16 cos 0.9999927 /
+# rel 4.1e-3, fp16 cos 0.99999989 / rel 5.1e-4; bars at about 3x those.
+HALF_BARS = {s2b.PREC_BF16: (1, 0.99998, 1.2e-2), s2b.PREC_FP16: (2, 0.9999996, 1.5e-3)}
+
+
+@pytest.mark.parametrize("prec", [s2b.PREC_BF16, s2b.PREC_FP16], ids=["bf16", "fp16"])
+def test_half_layers_vs_port_same_operand_rounding(port, m5_small, inputs, prec):
+    vp, txt, gns, gsh = inputs[:4]
+    mode, cbar, rbar = HALF_BARS[prec]
+    port.load(m5_small, 0, 2)
+    c = make_ctx(prec, m5_small, 0, 2, inputs)
+    port.set_operand_rounding(mode)
+    try:
+        v0, t0, _ = port.forward_latent(gns, gsh, vp, txt, TS, 0, 0, True, False)
+        rows = []
+        for layer in (0, 1):
+            v1, t1, _ = port.forward_latent(gns, gsh, v0, t0, TS, layer, layer + 1, False, False)
+            gv, gt, _ = c.forward_latent(v0, Lv, t0, TXT, TS, layer, layer + 1, False, False)
+            rows += [(f"layer {layer} vid",) + cases.compare(gv, v1), (f"layer {layer} txt",) + cases.compare(gt, t1)]
+            v0, t0 = v1, t1
+        _, _, sr_r = port.forward_latent(gns, gsh, v0, t0, TS, 2, 2, False, True)
+        _, _, sr = c.forward_latent(v0, Lv, t0, TXT, TS, 2, 2, False, True)
+        rows.append(("final",) + cases.compare(sr, sr_r))
+    finally:
+        port.set_operand_rounding(0)
+        c.close()
+    for r in rows:
+        print("%-14s cos %.9f rel %.2e" % r)
+    for what, cos, rel in rows:
+        assert cos >= cbar and rel <= rbar, (what, cos, rel)
 
 
 def test_time_embedding_and_ada_compose(port, m5_small, inputs):
@@ -123,7 +161,7 @@ def test_forward_latent_argument_errors(m5_small, inputs):
     c.close()
 
 
-@pytest.mark.parametrize("prec", [s2b.PREC_FP32, s2b.PREC_BF16], ids=["fp32", "bf16"])
+@pytest.mark.parametrize("prec", [s2b.PREC_FP32, s2b.PREC_BF16, s2b.PREC_FP16], ids=["fp32", "bf16", "fp16"])
 def test_full_graph_forward_equals_forward_latent(prec):
     # all 32 layers (synthetic weights in memory) on a 8x10 grid: the
     # captured CUDA graph replays exactly the kernels forward_latent runs
@@ -221,7 +259,7 @@ def test_cpp_dropin_engine_matches_python(m5_small, inputs, tmp_path):
     np.testing.assert_array_equal(got, np.concatenate([vl.ravel(), tl.ravel()]))
 
 
-@pytest.mark.parametrize("prec", [s2b.PREC_FP32, s2b.PREC_BF16], ids=["fp32", "bf16"])
+@pytest.mark.parametrize("prec", [s2b.PREC_FP32, s2b.PREC_BF16, s2b.PREC_FP16], ids=["fp32", "bf16", "fp16"])
 def test_temporal_windows_vs_port(port, m5_small, prec):
     """T > 1 (temporal windows and RoPE time offsets, src/awa_window.cpp:26-27,
     103-105): a 3 x 12 x 14 token grid through layers [0, 2) against the port."""
