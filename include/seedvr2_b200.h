@@ -187,7 +187,9 @@ int s2b_awa_forward(s2b_ctx* ctx, const float* vqkv, const float* tqkv, const s2
 /* Replaces AwaLayer::forward (src/awa_layer.cpp:284-453): same op on device
  * buffers, enqueued on `stream`; the geometry is the one last passed to
  * s2b_awa_set_geometry for `win_type` (0 non-shifted, 1 shifted), like
- * AwaLayer::set_window_geometry (src/awa_layer.cpp:73-91). */
+ * AwaLayer::set_window_geometry (src/awa_layer.cpp:73-91).  Every device
+ * buffer must be 16-byte aligned (S2B_ERR_ARG otherwise; cudaMalloc'ed
+ * buffers are). */
 int s2b_awa_set_geometry(s2b_ctx* ctx, int win_type, const s2b_win* win);
 int s2b_awa_forward_dev(s2b_ctx* ctx, int win_type, const float* d_vqkv, const float* d_tqkv,
                         const float* d_nq_v, const float* d_nk_v, const float* d_nq_t, const float* d_nk_t,
@@ -205,8 +207,9 @@ int s2b_awa_forward_dev(s2b_ctx* ctx, int win_type, const float* d_vqkv, const f
  * geometry comes from s2b_awa_set_geometry, which does allocate: call it at
  * set-up time.  The first call on a device also resolves the array's device
  * address: make it before any stream capture.  Calls share the array, so
- * calls whose GPU work overlaps race; serialise them.  Enqueues on `stream`
- * and returns without waiting. */
+ * calls whose GPU work overlaps race; serialise them.  Device buffers
+ * 16-byte aligned, as for s2b_awa_forward_dev.  Enqueues on `stream` and
+ * returns without waiting. */
 int s2b_awa_forward_dev_static(s2b_ctx* ctx, int win_type, const float* d_vqkv, const float* d_tqkv,
                                const float* d_nq_v, const float* d_nk_v, const float* d_nq_t, const float* d_nk_t,
                                int Lv, int TXT, float eps, float* d_vid_out, float* d_txt_out, void* stream);

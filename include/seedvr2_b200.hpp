@@ -11,8 +11,9 @@
 // behaviour.  The Vulkan-only housekeeping (reclaim_vram, reset_vulkan_device,
 // release_graph, load_graph) has nothing to do here: weights stay resident in
 // HBM and the 32-layer forward is one captured CUDA graph.  The reference's
-// CPU mode (use_cpu) and fp16 storage (precision 1) are not offered: init
-// then fails with a message, as the reference does for a missing model.
+// CPU mode (use_cpu) is not offered: init then fails with a message, as the
+// reference does for a missing model.  Its fp16 arithmetic switch maps to
+// fp16 operands (precision 1) when no storage precision is given.
 #ifndef SEEDVR2_B200_HPP
 #define SEEDVR2_B200_HPP
 
@@ -65,7 +66,7 @@ public:
     // DitVk::init(model_dir, fp16_arith, precision{0 fp32, 1 fp16, 2 bf16}, use_cpu)
     bool init(const std::string& model_dir, bool fp16_arith = false, int precision = 0, bool use_cpu = false) {
         if (use_cpu) return fail("DitB200: CPU mode is not offered (B200 only)");
-        if (fp16_arith && precision == 0) precision = S2B_PREC_BF16;   // low-precision arithmetic asked for
+        if (fp16_arith && precision == 0) precision = S2B_PREC_FP16;   // fp16 arithmetic asked for
         if (ctx_) { s2b_ctx_destroy(ctx_); ctx_ = nullptr; }
         if (s2b_ctx_create(device_, precision, &ctx_) != S2B_OK) {
             ctx_ = nullptr;

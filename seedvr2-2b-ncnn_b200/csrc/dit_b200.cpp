@@ -17,6 +17,8 @@
 #include "dit_shard.h"
 #include "synth.h"
 #include <cmath>
+#include <cstdint>
+#include <initializer_list>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
@@ -1185,6 +1187,9 @@ int DitB200::awa_forward_dev(int win_type, const float* vqkv, const float* tqkv,
                              float* txt_out, cudaStream_t user) {
     if (win_type != 0 && win_type != 1) return fail(ERR_ARG, "win_type must be 0 or 1");
     if (!vqkv || !tqkv || !nqv || !nkv || !nqt || !nkt || !vid_out || !txt_out) return fail(ERR_ARG, "null buffer");
+    for (const void* b : {(const void*)vqkv, (const void*)tqkv, (const void*)nqv, (const void*)nkv, (const void*)nqt,
+                          (const void*)nkt, (const void*)vid_out, (const void*)txt_out})
+        if ((uintptr_t)b & 15) return fail(ERR_ARG, "device buffers must be 16-byte aligned");
     cudaSetDevice(dev_);
     return awa_run(awa_geom_[win_type], vqkv, tqkv, nqv, nkv, nqt, nkt, Lv, TXT, eps, vid_out, txt_out, user);
 }
@@ -1201,6 +1206,9 @@ int DitB200::awa_forward_dev_static(int win_type, const float* vqkv, const float
     if (dev_ < 0) return fail(ERR_STATE, "context not created");
     if (win_type != 0 && win_type != 1) return fail(ERR_ARG, "win_type must be 0 or 1");
     if (!vqkv || !tqkv || !nqv || !nkv || !nqt || !nkt || !vid_out || !txt_out) return fail(ERR_ARG, "null buffer");
+    for (const void* b : {(const void*)vqkv, (const void*)tqkv, (const void*)nqv, (const void*)nkv, (const void*)nqt,
+                          (const void*)nkt, (const void*)vid_out, (const void*)txt_out})
+        if ((uintptr_t)b & 15) return fail(ERR_ARG, "device buffers must be 16-byte aligned");
     const GeomDev& G = awa_geom_[win_type];
     if (!G.ready) return fail(ERR_STATE, "AWA geometry not set (s2b_awa_set_geometry)");
     if (Lv != G.view.Lv || TXT != G.view.TXT || TXT <= 0) return fail(ERR_ARG, "Lv/TXT do not match the geometry");
