@@ -149,6 +149,33 @@ def test_awa_1080p_half_vs_fp32(shifted, half):
         assert cos >= cbar and rel <= rbar, (cos, rel)
 
 
+@pytest.mark.parametrize("poly", ["1", "2"])
+def test_awa_1080p_poly_exp_variant(poly):
+    """S2B_ATTN_POLY=n (read at each launch): n of every 4 exponential pairs
+    of the bf16 softmax on the FMA pipe; same bar as the MUFU default."""
+    T, H, W, TXT = 1, 68, 80, 58
+    Lv = T * H * W
+    win = s2b.make_win(T, H, W, (4, 3, 3), TXT, False)
+    vqkv = s2b.synth_normal((Lv, 7680), 11, "vqkv")
+    tqkv = s2b.synth_normal((TXT, 7680), 11, "tqkv")
+    nq = [s2b.synth_normal((128,), 11, n, 1.0, 0.02) for n in ("a", "b", "c", "d")]
+    c = s2b.DitB200(0, s2b.PREC_FP32)
+    try:
+        ref = c.awa_forward(vqkv, tqkv, win, *nq, Lv, TXT, 1e-5)
+    finally:
+        c.close()
+    c = s2b.DitB200(0, s2b.PREC_BF16)
+    os.environ["S2B_ATTN_POLY"] = poly
+    try:
+        out = c.awa_forward(vqkv, tqkv, win, *nq, Lv, TXT, 1e-5)
+    finally:
+        del os.environ["S2B_ATTN_POLY"]
+        c.close()
+    for a, b in zip(out, ref):
+        cos, rel = cases.compare(a, b)
+        assert cos >= 0.9995 and rel <= 2e-2, (cos, rel)
+
+
 def test_awa_fp32_simt_fallback_vs_port(port):
     """fp32 contexts run the attention on the tensor cores from split3
     operands; S2B_FP32_ATTN=simt (read at context creation) keeps the SIMT

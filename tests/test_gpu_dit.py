@@ -134,6 +134,23 @@ def test_half_layers_vs_port_same_operand_rounding(port, m5_small, inputs, prec)
         assert cos >= cbar and rel <= rbar, (what, cos, rel)
 
 
+def test_fp32_ffma_gemms_vs_reference_golden(m5_small, inputs):
+    """S2B_FP32_TC=0 (read when the weights load): the fp32 path's Linears on
+    the FFMA kernel instead of 3xTF32, held to the same fp32 bar."""
+    vp, txt = inputs[:2]
+    g = np.load(os.path.join(GOLD, "dit_small.npz"))
+    os.environ["S2B_FP32_TC"] = "0"
+    try:
+        c = make_ctx(s2b.PREC_FP32, m5_small, 0, 2, inputs)
+    finally:
+        del os.environ["S2B_FP32_TC"]
+    try:
+        _, _, sr = c.forward_latent(vp, Lv, txt, TXT, TS, 0, 2, True, True)
+    finally:
+        c.close()
+    assert_fp32(sr, g["sr01"], "sr [0,2) FFMA GEMMs")
+
+
 def test_time_embedding_and_ada_compose(port, m5_small, inputs):
     c = make_ctx(s2b.PREC_FP32, m5_small, 0, 2, inputs)
     port.load(m5_small, 0, 2)
