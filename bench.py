@@ -269,10 +269,11 @@ def fp32_records(steps: int):
             ms = e0.elapsed_time(e1) / steps
             ctx.check_errors()
             h_vid, h_txt = torch.from_numpy(vid).pin_memory(), torch.from_numpy(txt).pin_memory()
-            ctx.forward(h_vid.numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
+            h_sr = torch.empty((Lv, 64), dtype=torch.float32).pin_memory().numpy()
+            ctx.forward(h_vid.numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP, out=h_sr)
             w0 = time.perf_counter()
             for _ in range(steps):
-                ctx.forward(h_vid.numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
+                ctx.forward(h_vid.numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP, out=h_sr)
             e2e = (time.perf_counter() - w0) * 1e3 / steps
             prof = best_profile(ctx, vid, Lv, txt, TXT, TIMESTEP)
             g, a = prof["gemm_tcgen05"] if prof["gemm_tcgen05"]["launches"] else prof["gemm_fp32"], prof["attention"]
@@ -388,10 +389,11 @@ def image_record(ctx, args, world, rank, local, frames, txt):
     # e2e through the host-buffer call (the whole frame in, the whole sr out on every rank)
     h_vid, h_txt = torch.from_numpy(frames[0]).pin_memory(), torch.from_numpy(txt).pin_memory()
     sr_shard = ctx.shard_forward(h_vid.numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
+    h_sr = torch.empty((Lv, 64), dtype=torch.float32).pin_memory().numpy()
     torch.distributed.barrier()
     w0 = time.perf_counter()
     for i in range(args.steps):
-        ctx.shard_forward(h_vid.numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
+        ctx.shard_forward(h_vid.numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP, out=h_sr)
     te = torch.tensor([(time.perf_counter() - w0) * 1e3 / args.steps], device=dev, dtype=torch.float64)
     torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
     prof = best_profile(ctx, frames[0], Lv, txt, TXT, TIMESTEP, sharded=True)
@@ -497,13 +499,14 @@ def run_ours(args):
     # e2e through the host-buffer public API: pinned input -> forward -> host result
     h_vid = [torch.from_numpy(f).pin_memory() for f in frames]
     h_txt = torch.from_numpy(txt).pin_memory()
+    h_sr = torch.empty((Lv, 64), dtype=torch.float32).pin_memory().numpy()   # the result lands in page-locked memory
     host_fwd = ctx.shard_forward if image else ctx.forward
     for i in range(2):
-        host_fwd(h_vid[i % len(frames)].numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
+        host_fwd(h_vid[i % len(frames)].numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP, out=h_sr)
     barrier()
     w0 = time.perf_counter()
     for i in range(args.steps):
-        host_fwd(h_vid[i % len(frames)].numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP)
+        host_fwd(h_vid[i % len(frames)].numpy(), Lv, h_txt.numpy(), TXT, TIMESTEP, out=h_sr)
     w1 = time.perf_counter()
     barrier()
     te = torch.tensor([(w1 - w0) * 1e3], device=dev, dtype=torch.float64)

@@ -139,6 +139,14 @@ def _f32(a) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.float32)
 
 
+def _out(out, Lv: int) -> np.ndarray:
+    if out is None:
+        return np.zeros((Lv, OUT_CH), np.float32)
+    if out.dtype != np.float32 or out.shape != (Lv, OUT_CH) or not out.flags["C_CONTIGUOUS"]:
+        raise ValueError(f"out must be a C-contiguous float32 array of shape ({Lv}, {OUT_CH})")
+    return out
+
+
 def _p(a: np.ndarray):
     return a.ctypes.data_as(_F32P) if a is not None else None
 
@@ -384,9 +392,11 @@ class DitB200:
                                          _p(vl), _p(tl), None))
         return vl, tl, None
 
-    def forward(self, vid_patch, Lv, txt, TXT, timestep=1000.0):
+    def forward(self, vid_patch, Lv, txt, TXT, timestep=1000.0, out=None):
+        """sr (Lv, 64); `out`, when given, is the float32 C-contiguous array written
+        (a page-locked one makes the device-to-host copy direct)."""
         v, t = _f32(vid_patch), _f32(txt)
-        sr = np.zeros((Lv, OUT_CH), np.float32)
+        sr = _out(out, Lv)
         self._c(lib().s2b_forward(self._ctx, _p(v), Lv, _p(t), TXT, timestep, _p(sr)))
         return sr
 
@@ -458,9 +468,9 @@ class DitB200:
         buf = (ctypes.c_uint8 * 128).from_buffer_copy(nccl_id)
         self._c(lib().s2b_shard_init(self._ctx, buf, world, rank))
 
-    def shard_forward(self, vid_patch, Lv, txt, TXT, timestep=1000.0):
+    def shard_forward(self, vid_patch, Lv, txt, TXT, timestep=1000.0, out=None):
         v, t = _f32(vid_patch), _f32(txt)
-        sr = np.zeros((Lv, OUT_CH), np.float32)
+        sr = _out(out, Lv)
         self._c(lib().s2b_shard_forward(self._ctx, _p(v), Lv, _p(t), TXT, timestep, _p(sr)))
         return sr
 

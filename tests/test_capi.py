@@ -123,3 +123,12 @@ def test_nccl_watchdog_host_logic():
     assert L.s2b_debug_watchdog_selftest(3, 10000, ctypes.byref(polls), ctypes.byref(aborted)) == 3
     assert aborted.value == 0
     assert L.s2b_debug_watchdog_selftest(7, 10, None, None) == -1
+
+
+def test_forward_output_buffer_validation():
+    ok = np.zeros((3, 64), np.float32)
+    assert s2b._out(ok, 3) is ok
+    assert s2b._out(None, 3).shape == (3, 64)
+    for bad in (np.zeros((3, 64), np.float64), np.zeros((4, 64), np.float32), np.zeros((64, 3), np.float32).T):
+        with pytest.raises(ValueError):
+            s2b._out(bad, 3)
