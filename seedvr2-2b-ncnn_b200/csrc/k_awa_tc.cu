@@ -6,7 +6,8 @@
 // the per-window partials averaged later.  Keys past the window's end are
 // masked (their shared-memory rows hold the neighbouring window's finite data
 // or TMA zero fill).  Two kernels:
-//   k_awa_attn_tc4   bf16 operands: one CTA per (window, head, 128-query
+//   k_awa_attn_tc4   16-bit operands (bf16, or f16 for the fp16 precision; P
+//                    in the same type): one CTA per (window, head, 128-query
 //                    tile), two CTAs per SM, 64-key K/V tiles double-
 //                    buffered; S in two TMEM slots, P written back into TMEM
 //                    and used as the A operand of O += P V.

@@ -1,6 +1,8 @@
-// k_gemm_tc.cu -- persistent tcgen05 BF16 GEMMs with the DiT's fused epilogues.
+// k_gemm_tc.cu -- persistent tcgen05 16-bit GEMMs with the DiT's fused epilogues.
 //
-// C[M,N] = A[M,K] B[N,K]^T, A/B bf16 K-major, fp32 accumulation in TMEM.
+// C[M,N] = A[M,K] B[N,K]^T, A/B K-major and of one 16-bit type (bf16, or IEEE
+// binary16 for the fp16 precision: the kind::f16 instruction descriptor's A/B
+// format fields come from GemmEpi::op_t at run time), fp32 accumulation in TMEM.
 //
 // Pair kernel (M > 128, every vid Linear): clusters of two CTAs on two SMs
 // share one 256x256 output tile per step through tcgen05 cta_group::2.  Each
@@ -60,7 +62,7 @@ __host__ __device__ constexpr uint32_t idesc_for(uint32_t idesc_bf16, int op_f16
 // would leave much of the last wave idle); each CTA stages 128 A rows and
 // BN / 2 B rows per k-block.
 constexpr int BM2 = 256;
-// KIND_BF16: bf16 operands, 64-element k-blocks.  KIND_TF32X3: the fp32
+// KIND_BF16: 16-bit operands (bf16 or f16, see op_t), 64-element k-blocks.  KIND_TF32X3: the fp32
 // path's "3xTF32" split product -- A and B arrive as [hi | lo] halves of fp32
 // (hi = x rounded to tf32, lo = x - hi), and every k-step issues
 // hi*hi + hi*lo + lo*hi as tcgen05.mma kind::tf32 (fp32 accumulate), which
@@ -204,7 +206,7 @@ __device__ __forceinline__ float row_rs(const GemmEpi& e, int row, bool row_ok) 
 
 // EPI_QKV_PACK: the tile's 256 columns are two heads of one of q / k / v.
 // q and k heads get RMSNorm over their 128 dims (x / sqrt(mean(x^2)+eps) * w,
-// the division as a reciprocal multiply: this epilogue serves the bf16 path)
+// the division as a reciprocal multiply: this epilogue serves the 16-bit paths)
 // and RoPE, v heads pass through; each row lands in its window-packed slot(s)
 // (a txt row in every window, with the same angles in each).
 template <int BN>
@@ -1070,7 +1072,7 @@ int gemm_tf32x3(const void* A2, int lda2, const void* W2, int ldw2, int M, int N
     if (!gemm_tf32x3_supported(M, N, K, lda2, ldw2)) return -1;
     if (((uintptr_t)A2 & 15) || ((uintptr_t)W2 & 15)) return -1;
     if (e.mode == EPI_SWIGLU && N % 256) return -1;
-    if (e.mode == EPI_QKV_PACK) return -1;            // the fused pack writes bf16 operands
+    if (e.mode == EPI_QKV_PACK) return -1;            // the fused pack writes 16-bit operands
     using C = PairCfg<256, KIND_TF32X3>;
     PairMaps maps;
     TcParams p;

@@ -181,7 +181,7 @@ void awa_pack_split3(const void* vqkv, const void* tqkv, ActT in_t, int ldq, con
 int awa_attend_split3(const void* Q3, const void* K3, const void* V3, const AwaDev& g, float scale, void* att,
                       int ld_att, ActT at, float* toutw, cudaStream_t s);
 // Per-window SDPA.  vid rows scattered to att[vidx]; txt rows to toutw[wi][i].
-// bf16 operands run the tcgen05 kernel only: -1 (nothing launched) when its
+// 16-bit operands (bf16 / f16) run the tcgen05 kernel only: -1 (nothing launched) when its
 // tensor maps cannot be encoded.  fp32 operands run the SIMT kernel.
 int awa_attend(const void* Qp, const void* Kp, const void* Vp, ActT pt, const AwaDev& g, float scale,
                 void* att, int ld_att, ActT at, float* toutw, cudaStream_t s, int* launches);
